@@ -1,0 +1,417 @@
+#!/usr/bin/env python
+"""Benchmark of the chunked BASED hot path, one JSON line.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--mode heads|sp] [--workload c4|c2|c3|c5]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+Default workload: chunked BASED, B=8, H=16, N=32768,
+d_qk=16, d_v=64, bf16 inputs iid N(0,1)*0.5 (seeded per head), sharded by
+batch x head over the ranks (no collective on the data path).  A step is one
+pass of the chunked kernel over the rank's heads.  ``--mode sp`` runs the
+sequence-parallel variant (B=1, H=16, N=262144 split over the ranks, one
+NCCL all-gather of per-rank states per step).
+
+Timing: W untimed warm-up steps, then exactly K steps, each bracketed by CUDA
+events on the launching stream; L2 is flushed (256 MB write) before every
+timed step, outside the events; the per-rank sum is max-reduced over ranks
+after a barrier.  ``value`` = B*N tokens (heads not counted, the reference's
+convention) / that time.  ``e2e`` repeats the measurement through the public
+API with pinned host inputs copied in and the output copied back every step.
+``--impl reference`` times the CPU port of the reference's chunked algorithm
+(oracle/, numpy, all host threads) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOADS = {
+    # name: (batch, heads, seq_len, d_qk, d_v, kind)
+    "c4": (8, 16, 32768, 16, 64, "chunked"),
+    "c2": (4, 16, 2048, 16, 64, "chunked"),
+    "c3": (4, 16, 4096, 64, 64, "sliding"),
+    "c5": (None, 16, None, 16, 64, "crossover"),
+}
+METRIC = "BASED chunked attn tokens/s @N=32K,H=16 on 1/2/4/8 B200; % of roofline"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--mode", choices=["heads", "sp"], default="heads")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c4")
+    ap.add_argument("--seq-len", type=int, default=None, help="override N (c5 sweep point)")
+    ap.add_argument("--segments", type=int, default=0, help="0 = library's choice")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    return args
+
+
+# --------------------------------------------------------------------------- peaks
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def profile_traffic_per_token(kernel: str):
+    """DRAM bytes per token from the committed ncu summary, if present.
+
+    The summary line reads ``traffic_bytes_per_token: <float>`` and comes from
+    one ``ncu`` capture of the named kernel (see the summary's own header)."""
+    p = ROOT / "profiles" / f"{kernel}.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_token:"):
+            try:
+                return float(line.split(":", 1)[1])
+            except ValueError:
+                return None
+    return None
+
+
+# --------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000080: "hw_power_brake_slowdown",
+        0x0000000000000002: "applications_clocks_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.period = period_s
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------------------- inputs
+
+def make_head_inputs(heads_range, seq_len, d_qk, d_v, scale, seed=1234):
+    """Per-head seeded N(0,1)*scale inputs, generated on the host in fp32.
+
+    Head ``i`` (flattened b*H + h) always gets generator seed ``seed + i``, so
+    any rank's shard is reproducible on its own."""
+    import torch
+    qs, ks, vs = [], [], []
+    for i in range(*heads_range):
+        g = torch.Generator().manual_seed(seed + i)
+        qs.append(torch.randn(seq_len, d_qk, generator=g) * scale)
+        ks.append(torch.randn(seq_len, d_qk, generator=g) * scale)
+        vs.append(torch.randn(seq_len, d_v, generator=g) * scale)
+    return torch.stack(qs), torch.stack(ks), torch.stack(vs)
+
+
+# --------------------------------------------------------------------------- reference arm
+
+def cpu_port_sample(seq_len, d_qk, d_v, heads_in_metric, sample_heads, sample_tokens):
+    """Time the oracle's numpy port of the reference chunked algorithm once.
+
+    Returns (metric tokens/s, seconds).  The metric counts B*N tokens for all
+    ``heads_in_metric`` heads, so ``sample_heads`` heads of ``sample_tokens``
+    tokens stand for sample_tokens * sample_heads / heads_in_metric tokens."""
+    import numpy as np
+    import oracle as O
+    rng = np.random.default_rng(7)
+    q = (rng.standard_normal((1, sample_heads, sample_tokens, d_qk)) * 0.5).astype(np.float32)
+    k = (rng.standard_normal((1, sample_heads, sample_tokens, d_qk)) * 0.5).astype(np.float32)
+    v = (rng.standard_normal((1, sample_heads, sample_tokens, d_v)) * 0.5).astype(np.float32)
+    t0 = time.perf_counter()
+    O.based_chunked(q, k, v, chunk=64, dtype=np.float32)
+    dt = time.perf_counter() - t0
+    return sample_tokens * sample_heads / heads_in_metric / dt, dt
+
+
+def host_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return int(max(n))
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # rank 0 alone runs the CPU arm
+    b, h, n, dqk, dv, kind = WORKLOADS["c4"]
+    n = args.seq_len or n
+    sample_heads = 16 if args.mode == "heads" else 4
+    sample_tokens = min(n, 32768)
+    for _ in range(args.warmup):
+        cpu_port_sample(n, dqk, dv, h, sample_heads, sample_tokens)
+    rates, secs = [], 0.0
+    for _ in range(args.steps):
+        r, dt = cpu_port_sample(n, dqk, dv, h, sample_heads, sample_tokens)
+        rates.append(r)
+        secs += dt
+    value = args.steps * sample_tokens * sample_heads / h / secs
+    sample = (f"{sample_heads} heads x {sample_tokens} tokens per step, fp32 numpy port of the "
+              "reference chunked recurrence (oracle/based_oracle.py based_chunked)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args, b, h, n, dqk, dv),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": host_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(args, b, h, n, dqk, dv):
+    return {"workload": ("C4 chunked BASED, batch x head sharded" if args.mode == "heads"
+                         else "C4-SP chunked BASED, sequence parallel"),
+            "batch": b, "heads": h, "seq_len": n, "d_qk": dqk, "d_v": dv, "chunk_size": 64,
+            "global_batch": b, "parallelism": (f"heads{args.gpus}" if args.mode == "heads"
+                                               else f"sp{args.gpus}"),
+            "inputs": "iid N(0,1)*0.5, seeded per head, bf16",
+            "l2": "flushed (256 MB write) before every timed step"}
+
+
+# --------------------------------------------------------------------------- our arm
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from trainium_linear_attention_b200 import distributed as D
+    from trainium_linear_attention_b200 import ops
+
+    rank, world, local = D.init_process_group_from_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    if args.mode == "heads":
+        b, h, n, dqk, dv, _ = WORKLOADS["c4"]
+        n = args.seq_len or n
+        lo, hi = D.head_range(b * h, rank, world)
+        tok_lo, tok_hi = 0, n
+    else:
+        b, h, n, dqk, dv = 1, 16, args.seq_len or 262144, 16, 64
+        lo, hi = 0, b * h
+        tok_lo, tok_hi = D.token_range(n, rank, world)
+    local_heads = hi - lo
+    t_local = tok_hi - tok_lo
+
+    # inputs: host fp32 -> bf16 (pinned for the end-to-end leg) -> device
+    if args.mode == "heads":
+        qh, kh, vh = make_head_inputs((lo, hi), n, dqk, dv, 0.5)
+    else:
+        qf, kf, vf = make_head_inputs((0, h), n, dqk, dv, 0.5)
+        qh, kh, vh = (x[:, tok_lo:tok_hi] for x in (qf, kf, vf))
+    qh, kh, vh = (x.to(torch.bfloat16).reshape(1, local_heads, t_local, -1).contiguous().pin_memory()
+                  for x in (qh, kh, vh))
+    q, k, v = (x.to(dev) for x in (qh, kh, vh))
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    seg = args.segments
+    g, ws_bytes = ops.chunked_plan(local_heads, t_local, dqk, dv, torch.bfloat16, seg)
+    workspace = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    if args.mode == "heads":
+        def step():
+            return ops.based_chunked(q, k, v, chunk_size=64, segments=g, workspace=workspace)
+        launches_per_step = 2 if g > 1 else 1
+    else:
+        def step():
+            return D.sequence_parallel_forward(q, k, v, chunk_size=64)
+        launches_per_step = (3 if g > 1 else 1) + 1  # state (+sum) pass, forward
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident value
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = max_over_ranks(sum(step_ms))
+    tokens = b * n  # B*N, the reference's tokens convention (heads not counted)
+    value = tokens * args.steps / (total_ms / 1e3)
+    ms_per_step = total_ms / args.steps
+
+    # ---- end to end through the public API (pinned host in, host out)
+    e2e = None
+    if not args.no_e2e:
+        out_host = torch.empty((1, local_heads, t_local, dv), dtype=torch.bfloat16).pin_memory()
+        from trainium_linear_attention_b200 import based_chunked as api_based_chunked
+
+        def e2e_step():
+            qd = qh.to(dev, non_blocking=True)
+            kd = kh.to(dev, non_blocking=True)
+            vd = vh.to(dev, non_blocking=True)
+            if args.mode == "heads":
+                y = api_based_chunked(qd, kd, vd, chunk_size=64)
+            else:
+                y = D.sequence_parallel_forward(qd, kd, vd, chunk_size=64)
+            out_host.copy_(y, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        es = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        es[0].record(stream)
+        for i in range(args.steps):
+            e2e_step()
+            es[i + 1].record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(es[0].elapsed_time(es[-1]))
+        h2d = sum(x.numel() * x.element_size() for x in (qh, kh, vh))
+        d2h = out_host.numel() * out_host.element_size()
+        e2e = {"value": tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "ms_per_step": e2e_ms / args.steps}
+
+    # ---- roofline of the step on this rank (the chunked kernel dominates it)
+    hbm_gbs, tflops, peak_kind = measured_peaks()
+    local_tokens = local_heads * t_local  # token-heads this rank processes
+    alg_bytes = local_tokens * (2 * dqk * 2 + dv * 2 + dv * 2)  # q,k,v read + out write, bf16
+    rank_ms = sum(step_ms) / args.steps
+    achieved = alg_bytes / (rank_ms / 1e3) / 1e9
+    traffic_tok = profile_traffic_per_token("chunked_output_c4")
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s",
+                "frac": achieved / hbm_gbs, "peak_source": peak_kind,
+                "traffic": (traffic_tok * local_tokens / 16 if traffic_tok else None),
+                "alg_bytes_per_launch": alg_bytes,
+                "flop_frac": (local_tokens / 16 * 1216592) / (rank_ms / 1e3) / (tflops * 1e12)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rates, secs = [], 0.0
+        while secs < 12.0 and len(rates) < 12:
+            r, dt = cpu_port_sample(n, dqk, dv, h, 16, min(n, 32768))
+            rates.append(r)
+            secs += dt
+        cpu = {"value": statistics.median(rates), "unit": "tokens/s", "cores": host_threads(),
+               "kind": "port",
+               "sample": f"16 heads x {min(n, 32768)} tokens, fp32 numpy port of the reference "
+                         f"chunked recurrence, {len(rates)} runs (median)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": dict(config_dict(args, b, h, n, dqk, dv), segments=g),
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "clocks": clk.summary(), "gpu_launches": launches_per_step * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

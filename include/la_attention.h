@@ -1,0 +1,149 @@
+/*
+ * la_attention.h -- C ABI of the B200 (sm_100a) BASED / sliding-window
+ * attention library (libla_attention.so).
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * passed as void*, enqueues its kernels on that stream and returns an int
+ * status (LA_OK == 0).  No entry point synchronises the stream, allocates
+ * device memory or keeps state between calls; all are safe to call from
+ * several host threads at once.
+ *
+ * Tensor layout: every q/k/v/out is a contiguous (batch, heads, seq_len, d)
+ * row-major array in the element type given by `dtype`.  q and k have width
+ * d_qk, v and out have width d_v (d_v may differ from d_qk).  Inputs are never
+ * written.
+ *
+ * Semantics (identical to the reference's PyTorch functions):
+ *   s = (q . k) / sqrt(d_qk), causal mask includes the diagonal,
+ *   BASED:   out_i = sum_{j<=i} (1 + s_ij + s_ij^2/2) v_j
+ *                    / (sum_{j<=i} (1 + s_ij + s_ij^2/2) + eps)
+ *   sliding: out_i = softmax_{i-W+1 <= j <= i}(s_ij) . v_j
+ */
+#ifndef LA_ATTENTION_H
+#define LA_ATTENTION_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------------
+ * The reference's dispatcher swallows every failure and silently falls back
+ * to PyTorch (kernels/pytorch_attention.py:87-92).  This library never falls
+ * back: every failure is reported to the caller.                            */
+#define LA_OK                    0
+#define LA_ERR_INVALID_ARGUMENT  1  /* null pointer, negative size, bad dtype ... */
+#define LA_ERR_UNSUPPORTED       2  /* valid request this build has no kernel for  */
+#define LA_ERR_CUDA              3  /* a CUDA runtime / launch error               */
+#define LA_ERR_WORKSPACE         4  /* workspace missing, too small or misaligned  */
+#define LA_ERR_NO_DEVICE         5  /* no sm_100 device is current                 */
+
+/* ---- element types --------------------------------------------------------*/
+#define LA_DTYPE_FLOAT32   0
+#define LA_DTYPE_BFLOAT16  1
+
+/* ---- flags for the chunked entry points ------------------------------------*/
+#define LA_CHUNKED_NORMALIZE        1u  /* divide by the normaliser (+eps)        */
+#define LA_CHUNKED_REUSE_SEGMENTS   2u  /* workspace already holds the segment
+                                           states written by la_based_chunked_state */
+
+/* Human-readable name of a status code (static storage, never NULL). */
+const char *la_status_string(int status);
+
+/* ABI version of this header (bumped on any incompatible change). */
+int la_abi_version(void);
+
+/* Width F of the Taylor feature basis for key width d_qk: 1 + d + d(d+1)/2
+ * (153 at d_qk = 16).  Replaces the width computed by the reference's
+ * taylor_feature_map (benchmarks/chunked_attention_benchmark.py:34-53). */
+int64_t la_based_feature_dim(int64_t d_qk);
+
+/* ---------------------------------------------------------------------------
+ * Parallel (quadratic) fused BASED attention.
+ *
+ * Replaces solution_nki (kernels/pytorch_attention.py:44-78) together with the
+ * kernel it builds, get_based_attn_kernel / _kernel (kernels/nki_attention.py:
+ * 25-115): one call computes the normalised output; no padding copies and no
+ * host-side num/den division.  fp32 inputs compute in fp32 (CUDA cores);
+ * bf16 inputs at d_qk = 16, d_v = 64 use the tcgen05 tensor-core kernel.
+ * ------------------------------------------------------------------------- */
+int la_based_parallel_fwd(const void *q, const void *k, const void *v, void *out,
+                          int64_t batch, int64_t heads, int64_t seq_len,
+                          int64_t d_qk, int64_t d_v, int dtype, float eps,
+                          void *stream);
+
+/* ---------------------------------------------------------------------------
+ * Chunked recurrent BASED attention.
+ *
+ * Replaces chunked_nki_numerator (benchmarks/chunked_attention_benchmark.py:
+ * 96-126) and the kernel of get_chunked_attn_kernel (kernels/
+ * nki_attention_chunked.py:20-113).  Unlike the reference, the Taylor features
+ * are never materialised in HBM, the recurrent state lives on chip, and with
+ * LA_CHUNKED_NORMALIZE the normaliser is carried too (the reference returns
+ * the numerator only).
+ *
+ * State layout (init_state / final_state / la_based_chunked_state): fp32
+ * (batch*heads, F, d_v + 1) in the key-side feature basis
+ *     phi_k(k) = [1, k_0 .. k_{d-1}, k_i * k_j for i <= j in row-major order]
+ * i.e. state[f][e] = sum_j phi_k(k_j)[f] * v_j[e] and state[f][d_v] =
+ * sum_j phi_k(k_j)[f].  The query side carries the scale factors
+ * (phi_q(q) = [1, q_i/sqrt(d), q_i q_j w_ij], w_ii = 1/(2d), w_ij = 1/d), so
+ * phi_q(q) . phi_k(k) = 1 + s + s^2/2 exactly as the reference's feature map.
+ *
+ * segments: the sequence of each head is split into this many contiguous
+ * segments processed by different CTAs (0 = let the library choose).  A
+ * segmented run needs a workspace of la_based_chunked_workspace_size() bytes
+ * (256-byte aligned); an unsegmented run needs none (workspace may be NULL).
+ * chunk_size: the reference's chunk length.  The result does not depend on it
+ * beyond floating-point rounding (any positive value is accepted); the
+ * kernels tile the sequence at their own fixed length.
+ * ------------------------------------------------------------------------- */
+int la_based_chunked_plan(int64_t batch_heads, int64_t seq_len, int64_t d_qk,
+                          int64_t d_v, int dtype, int segments_requested,
+                          int *segments_out, size_t *workspace_bytes_out);
+
+size_t la_based_chunked_workspace_size(int64_t batch_heads, int64_t seq_len,
+                                       int64_t d_qk, int64_t d_v, int segments);
+
+int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
+                         int64_t batch, int64_t heads, int64_t seq_len,
+                         int64_t d_qk, int64_t d_v, int dtype,
+                         int64_t chunk_size, float eps, unsigned flags,
+                         const float *init_state, float *final_state,
+                         void *workspace, size_t workspace_bytes, int segments,
+                         void *stream);
+
+/* Total state sum_j phi_k(k_j) [v_j, 1]^T of every head over all seq_len
+ * tokens, written to state_out (fp32, (batch*heads, F, d_v + 1)).  This is the
+ * per-rank contribution exchanged by the sequence-parallel mode.  With a
+ * workspace and segments > 1 the per-segment states are left in the workspace
+ * so that a following la_based_chunked_fwd with LA_CHUNKED_REUSE_SEGMENTS
+ * (same shapes and segments) skips its own state pass.  The reference has no
+ * counterpart (it has no multi-device mode). */
+int la_based_chunked_state(const void *k, const void *v, float *state_out,
+                           int64_t batch, int64_t heads, int64_t seq_len,
+                           int64_t d_qk, int64_t d_v, int dtype,
+                           void *workspace, size_t workspace_bytes, int segments,
+                           void *stream);
+
+/* ---------------------------------------------------------------------------
+ * Sliding-window causal softmax attention, window [i-W+1, i].
+ *
+ * Replaces nki_sliding_window_attn (benchmarks/sliding_attention_benchmark.py:
+ * 59-99) and get_sliding_window_kernel / _kernel (kernels/
+ * nki_attention_sliding.py:30-132).  The mask is computed from indices (never
+ * loaded), no padding copies are made, and any window >= 1 is accepted (the
+ * reference asserts W <= 66 at block 64).  fp32 softmax accumulation.
+ * ------------------------------------------------------------------------- */
+int la_sliding_window_fwd(const void *q, const void *k, const void *v, void *out,
+                          int64_t batch, int64_t heads, int64_t seq_len,
+                          int64_t head_dim, int dtype, int64_t window,
+                          void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LA_ATTENTION_H */

@@ -1,0 +1,221 @@
+"""GPU parity: the CUDA kernels (through the C ABI) against the CPU oracle and
+the reference's golden vectors.
+
+Tolerances (rel-L2 over the whole output, the north-star's metric):
+  * fp32 inputs:  <= 1e-4 against the fp32 reference;
+  * bf16 inputs:  <= 2e-2 against the fp32/fp64 reference evaluated on the
+    same bf16-rounded inputs.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+import trainium_linear_attention_b200 as T
+from trainium_linear_attention_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+TOL_FP32 = 1e-4
+TOL_BF16 = 2e-2
+DEV = "cuda"
+
+
+def inputs(shape_qk, dv, seed, scale=0.5, dtype=torch.bfloat16):
+    """Seeded N(0,1)*scale inputs generated on the host in fp32, cast to dtype."""
+    g = torch.Generator().manual_seed(seed)
+    b, h, t, d = shape_qk
+    q = (torch.randn(b, h, t, d, generator=g) * scale).to(dtype)
+    k = (torch.randn(b, h, t, d, generator=g) * scale).to(dtype)
+    v = (torch.randn(b, h, t, dv, generator=g) * scale).to(dtype)
+    return q, k, v
+
+
+def np64(x):
+    return x.float().cpu().numpy().astype(np.float64)
+
+
+def cuda(*xs):
+    return [x.to(DEV) for x in xs]
+
+
+# ---------------------------------------------------------------- parallel ---
+
+@pytest.mark.parametrize("case", ["c1", "par_odd", "par_n1", "par_d8"])
+def test_parallel_fp32_golden(golden, case):
+    q, k, v = (torch.from_numpy(golden[f"{case}.{n}"]).to(DEV) for n in "qkv")
+    y = T.solution_nki(q, k, v)
+    assert y.dtype == torch.float32 and y.shape == v.shape
+    assert O.rel_l2(y.cpu().numpy(), golden[f"{case}.out"]) <= TOL_FP32
+
+
+@pytest.mark.parametrize("shape,dv", [((2, 3, 1000, 16), 64), ((1, 2, 1, 16), 64),
+                                      ((1, 2, 127, 16), 64), ((1, 1, 513, 16), 64),
+                                      ((2, 2, 300, 32), 48)])
+def test_parallel_bf16(shape, dv):
+    q, k, v = inputs(shape, dv, seed=shape[2])
+    y = T.solution_nki(*cuda(q, k, v))
+    assert y.dtype == torch.bfloat16
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+
+
+# ----------------------------------------------------------------- chunked ---
+
+def test_chunked_fp32_golden(golden):
+    q, k, v = (torch.from_numpy(golden[f"dense.{n}"]).to(DEV) for n in "qkv")
+    num = T.chunked_nki_numerator(q, k, v)
+    assert O.rel_l2(num.cpu().numpy(), golden["dense.num"]) <= TOL_FP32
+    y = T.based_chunked(q, k, v)
+    assert O.rel_l2(y.cpu().numpy(), golden["dense.out"]) <= TOL_FP32
+
+
+def test_chunked_config2():
+    """B=4, H=16, N=2048, d_qk=16, d_v=64, bf16, chunk 64."""
+    q, k, v = inputs((4, 16, 2048, 16), 64, seed=2)
+    y = T.based_chunked(*cuda(q, k, v), chunk_size=64)
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+    num = T.chunked_nki_numerator(*cuda(q, k, v), chunk_size=64)
+    want_num = O.based_chunked(np64(q), np64(k), np64(v), normalize=False)
+    assert O.rel_l2(np64(num), want_num) <= TOL_BF16
+
+
+@pytest.mark.parametrize("t", [1, 63, 64, 65, 127, 128, 129, 1000])
+def test_chunked_ragged_lengths(t):
+    q, k, v = inputs((1, 3, t, 16), 64, seed=t)
+    y = T.based_chunked(*cuda(q, k, v))
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+
+
+@pytest.mark.parametrize("dqk,dv,dtype", [(16, 32, torch.float32), (8, 24, torch.float32),
+                                          (16, 64, torch.float32), (32, 64, torch.bfloat16)])
+def test_chunked_other_widths(dqk, dv, dtype):
+    q, k, v = inputs((1, 2, 300, dqk), dv, seed=dqk + dv, dtype=dtype)
+    y = T.based_chunked(*cuda(q, k, v))
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    tol = TOL_FP32 if dtype == torch.float32 else TOL_BF16
+    assert O.rel_l2(np64(y), want) <= tol
+
+
+@pytest.mark.parametrize("segments", [2, 3, 8])
+def test_chunked_segments_agree(segments):
+    q, k, v = cuda(*inputs((1, 4, 3000, 16), 64, seed=7))
+    y1 = ops.based_chunked(q, k, v, segments=1)
+    yg = ops.based_chunked(q, k, v, segments=segments)
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(yg), want) <= TOL_BF16
+    assert O.rel_l2(np64(yg), np64(y1)) <= 1e-2
+
+
+def test_chunked_state_roundtrip():
+    """Seeding the second half with the first half's final state reproduces
+    the whole sequence; the states match the oracle's."""
+    q, k, v = cuda(*inputs((2, 2, 1500, 16), 64, seed=11))
+    whole, s_whole = ops.based_chunked(q, k, v, return_state=True)
+    cut = 700
+    a, s_a = ops.based_chunked(q[:, :, :cut], k[:, :, :cut], v[:, :, :cut], return_state=True)
+    b = ops.based_chunked(q[:, :, cut:], k[:, :, cut:], v[:, :, cut:], init_state=s_a)
+    assert O.rel_l2(np64(torch.cat([a, b], 2)), np64(whole)) <= 1e-2
+    want = O.chunked_state(np64(k), np64(v)).reshape(4, 153, 65)
+    assert O.rel_l2(s_whole.cpu().numpy(), want) <= 1e-3
+    st = ops.based_chunked_state(k, v)
+    assert O.rel_l2(st.cpu().numpy(), want) <= 1e-3
+    st3 = ops.based_chunked_state(k, v, segments=3)
+    assert O.rel_l2(st3.cpu().numpy(), want) <= 1e-3
+
+
+def test_chunked_reuse_segments():
+    q, k, v = cuda(*inputs((1, 2, 2500, 16), 64, seed=12))
+    g, ws_bytes = ops.chunked_plan(2, 2500, 16, 64, torch.bfloat16, segments=4)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=DEV)
+    ops.based_chunked_state(k, v, segments=g, workspace=ws)
+    y = ops.based_chunked(q, k, v, segments=g, workspace=ws, reuse_segments=True)
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+
+
+def test_chunked_sequence_parallel_emulated():
+    """The sequence-parallel recipe (per-rank states, exclusive prefix, seeded
+    forward) run for 4 emulated ranks on one GPU."""
+    q, k, v = cuda(*inputs((1, 4, 4096, 16), 64, seed=13))
+    world = 4
+    parts = [(q[:, :, r * 1024:(r + 1) * 1024], k[:, :, r * 1024:(r + 1) * 1024],
+              v[:, :, r * 1024:(r + 1) * 1024]) for r in range(world)]
+    states = torch.stack([ops.based_chunked_state(pk, pv) for _, pk, pv in parts])
+    outs = []
+    for r, (pq, pk, pv) in enumerate(parts):
+        prefix = states[:r].sum(0) if r else torch.zeros_like(states[0])
+        outs.append(ops.based_chunked(pq, pk, pv, init_state=prefix))
+    y = torch.cat(outs, 2)
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+
+
+def test_chunked_full_size_properties():
+    """BASELINE config 4 sizes (B=8, H=16, N=32768): two heads against the
+    oracle, every head through size-independent properties -- the output is a
+    convex combination of the values (weights 1+s+s^2/2 > 0), and the
+    segmented and unsegmented runs agree."""
+    q, k, v = inputs((8, 16, 32768, 16), 64, seed=4)
+    qd, kd, vd = cuda(q, k, v)
+    y = T.based_chunked(qd, kd, vd)
+    for bh in (0, 127):
+        b, h = divmod(bh, 16)
+        want = O.based_chunked(np64(q[b, h]), np64(k[b, h]), np64(v[b, h]))
+        assert O.rel_l2(np64(y[b, h]), want) <= TOL_BF16
+    vmax = vd.float().abs().amax(dim=2, keepdim=True)
+    assert bool((y.float().abs() <= vmax * 1.01 + 1e-3).all())
+    assert bool(torch.isfinite(y.float()).all())
+    yg = ops.based_chunked(qd, kd, vd, segments=4)
+    assert O.rel_l2(np64(yg), np64(y)) <= 1e-2
+
+
+def test_deterministic():
+    q, k, v = cuda(*inputs((2, 4, 2048, 16), 64, seed=5))
+    a = ops.based_chunked(q, k, v, segments=3)
+    b = ops.based_chunked(q, k, v, segments=3)
+    assert torch.equal(a, b)
+    assert torch.equal(T.solution_nki(q, k, v), T.solution_nki(q, k, v))
+
+
+# ----------------------------------------------------------------- sliding ---
+
+@pytest.mark.parametrize("case", ["slide_w64", "slide_w16_odd", "slide_w1", "slide_wbig",
+                                  "slide_w100"])
+def test_sliding_fp32_golden(golden, case):
+    q, k, v = (torch.from_numpy(golden[f"{case}.{n}"]).to(DEV) for n in "qkv")
+    y = T.nki_sliding_window_attn(q, k, v, window_size=int(golden[f"{case}.window"]))
+    assert O.rel_l2(y.cpu().numpy(), golden[f"{case}.out"]) <= TOL_FP32
+
+
+def test_sliding_config3():
+    """W=64, B=4, H=16, N=4096, d=64, bf16, N(0,1) inputs."""
+    q, k, v = inputs((4, 16, 4096, 64), 64, seed=3, scale=1.0)
+    y = T.nki_sliding_window_attn(*cuda(q, k, v), window_size=64)
+    want = O.sliding_window_attn(np64(q), np64(k), np64(v), 64)
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+
+
+@pytest.mark.parametrize("t,w", [(1, 64), (65, 64), (200, 1), (300, 128), (129, 500), (1000, 65)])
+def test_sliding_edges_bf16(t, w):
+    q, k, v = inputs((1, 2, t, 64), 64, seed=t + w, scale=1.0)
+    y = T.nki_sliding_window_attn(*cuda(q, k, v), window_size=w)
+    want = O.sliding_window_attn(np64(q), np64(k), np64(v), w)
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+
+
+# -------------------------------------------------------------- dispatch ---
+
+def test_solution_dispatch_and_errors():
+    q, k, v = cuda(*inputs((1, 2, 3000, 16), 64, seed=9))
+    y = T.solution(q, k, v)
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+    with pytest.raises(TypeError):
+        T.solution(q.half(), k.half(), v.half())
+    with pytest.raises(RuntimeError):  # d_qk beyond the kernels: raises, no fallback
+        qq = torch.zeros(1, 1, 8, 256, device=DEV, dtype=torch.bfloat16)
+        T.solution_nki(qq, qq, qq)

@@ -1,0 +1,264 @@
+// C ABI entry points (include/la_attention.h): argument validation, planning
+// and dispatch between the tcgen05 tensor-core kernels (bf16, d_qk = 16,
+// d_v = 64 on sm_100) and the SIMT kernels (fp32 and every other shape).
+#include <math.h>
+#include <mutex>
+
+#include "common.cuh"
+#include "tc_kernels.cuh"
+
+namespace la {
+
+int current_device_info(DeviceInfo *info) {
+  static std::mutex mu;
+  static DeviceInfo cache[64];
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return LA_ERR_NO_DEVICE;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev].device != dev) {
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, dev) != cudaSuccess) {
+      cudaGetLastError();
+      return LA_ERR_NO_DEVICE;
+    }
+    cache[dev].sm_count = p.multiProcessorCount;
+    cache[dev].cc_major = p.major;
+    cache[dev].cc_minor = p.minor;
+    cache[dev].smem_optin = p.sharedMemPerBlockOptin;
+    cache[dev].device = dev;
+  }
+  *info = cache[dev];
+  return LA_OK;
+}
+
+namespace {
+
+constexpr int64_t kSegmentTile = 128;     // segment boundaries are multiples of this
+constexpr int64_t kMinSegmentTokens = 1024;
+
+// The library is built for sm_100a only.
+int require_sm100(DeviceInfo *info) {
+  int st = current_device_info(info);
+  if (st != LA_OK) return st;
+  if (info->cc_major != 10) return LA_ERR_NO_DEVICE;
+  return LA_OK;
+}
+
+bool valid_dtype(int dtype) { return dtype == LA_DTYPE_FLOAT32 || dtype == LA_DTYPE_BFLOAT16; }
+
+int check_common(const void *q, const void *k, const void *v, const void *out, int64_t batch,
+                 int64_t heads, int64_t n, int64_t dqk, int64_t dv, int dtype) {
+  if (batch < 0 || heads < 0 || n < 0 || dqk < 1 || dv < 1) return LA_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(dtype)) return LA_ERR_INVALID_ARGUMENT;
+  if (batch * heads * n == 0) return LA_OK;
+  if (!q || !k || !v || !out) return LA_ERR_INVALID_ARGUMENT;
+  if (batch * heads > 65535) return LA_ERR_UNSUPPORTED;
+  return LA_OK;
+}
+
+int64_t segment_len(int64_t n, int segments) {
+  int64_t len = (n + segments - 1) / segments;
+  len = (len + kSegmentTile - 1) / kSegmentTile * kSegmentTile;
+  return len < kSegmentTile ? kSegmentTile : len;
+}
+
+// Number of segments actually used (the last one may not be empty).
+int effective_segments(int64_t n, int segments) {
+  if (segments <= 1 || n <= 0) return 1;
+  const int64_t len = segment_len(n, segments);
+  return (int)((n + len - 1) / len);
+}
+
+int auto_segments(int64_t bh, int64_t n, int sm_count) {
+  if (bh <= 0 || n <= 0) return 1;
+  if (bh * 4 >= (int64_t)sm_count * 3) return 1;  // >= 75% of the SMs busy already
+  int64_t g = (sm_count + bh - 1) / bh;
+  const int64_t max_g = (n + kMinSegmentTokens - 1) / kMinSegmentTokens;
+  if (g > max_g) g = max_g;
+  if (g < 1) g = 1;
+  return effective_segments(n, (int)g);
+}
+
+bool use_tensor_cores(int dtype, int64_t dqk, int64_t dv) {
+  return dtype == LA_DTYPE_BFLOAT16 && dqk == 16 && dv == 64 && tc_kernels_enabled();
+}
+
+size_t state_floats(int64_t bh, int64_t dqk, int64_t dv) {
+  return (size_t)bh * (size_t)feature_dim(dqk) * (size_t)(dv + 1);
+}
+
+}  // namespace
+}  // namespace la
+
+using namespace la;
+
+extern "C" {
+
+const char *la_status_string(int status) {
+  switch (status) {
+    case LA_OK: return "ok";
+    case LA_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case LA_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+    case LA_ERR_CUDA: return "CUDA error";
+    case LA_ERR_WORKSPACE: return "workspace missing, too small or misaligned";
+    case LA_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
+    default: return "unknown status";
+  }
+}
+
+int la_abi_version(void) { return 1; }
+
+int64_t la_based_feature_dim(int64_t d_qk) { return d_qk < 1 ? 0 : feature_dim(d_qk); }
+
+int la_based_parallel_fwd(const void *q, const void *k, const void *v, void *out, int64_t batch,
+                          int64_t heads, int64_t seq_len, int64_t d_qk, int64_t d_v, int dtype,
+                          float eps, void *stream) {
+  int st = check_common(q, k, v, out, batch, heads, seq_len, d_qk, d_v, dtype);
+  if (st != LA_OK || batch * heads * seq_len == 0) return st;
+  DeviceInfo info;
+  if ((st = require_sm100(&info)) != LA_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (use_tensor_cores(dtype, d_qk, d_v))
+    return launch_parallel_tc(q, k, v, out, batch * heads, seq_len, eps, info, s);
+  return launch_parallel_simt(q, k, v, out, batch * heads, seq_len, (int)d_qk, (int)d_v, dtype,
+                              eps, s);
+}
+
+int la_based_chunked_plan(int64_t batch_heads, int64_t seq_len, int64_t d_qk, int64_t d_v,
+                          int dtype, int segments_requested, int *segments_out,
+                          size_t *workspace_bytes_out) {
+  if (batch_heads < 0 || seq_len < 0 || d_qk < 1 || d_v < 1 || segments_requested < 0 ||
+      !valid_dtype(dtype))
+    return LA_ERR_INVALID_ARGUMENT;
+  int g = segments_requested;
+  if (g == 0) {
+    DeviceInfo info;
+    int st = require_sm100(&info);
+    if (st != LA_OK) return st;
+    g = auto_segments(batch_heads, seq_len, info.sm_count);
+  }
+  g = effective_segments(seq_len, g);
+  if (segments_out) *segments_out = g;
+  if (workspace_bytes_out)
+    *workspace_bytes_out = la_based_chunked_workspace_size(batch_heads, seq_len, d_qk, d_v, g);
+  return LA_OK;
+}
+
+size_t la_based_chunked_workspace_size(int64_t batch_heads, int64_t seq_len, int64_t d_qk,
+                                       int64_t d_v, int segments) {
+  if (batch_heads <= 0 || d_qk < 1 || d_v < 1) return 0;
+  const int g = effective_segments(seq_len, segments);
+  if (g <= 1) return 0;
+  size_t bytes = state_floats(batch_heads, d_qk, d_v) * (size_t)g * sizeof(float);
+  return (bytes + 255) / 256 * 256;
+}
+
+int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out, int64_t batch,
+                         int64_t heads, int64_t seq_len, int64_t d_qk, int64_t d_v, int dtype,
+                         int64_t chunk_size, float eps, unsigned flags, const float *init_state,
+                         float *final_state, void *workspace, size_t workspace_bytes,
+                         int segments, void *stream) {
+  int st = check_common(q, k, v, out, batch, heads, seq_len, d_qk, d_v, dtype);
+  if (st != LA_OK) return st;
+  if (chunk_size < 1 || segments < 0) return LA_ERR_INVALID_ARGUMENT;
+  if (flags & ~(LA_CHUNKED_NORMALIZE | LA_CHUNKED_REUSE_SEGMENTS)) return LA_ERR_INVALID_ARGUMENT;
+  const int64_t bh = batch * heads;
+  if (bh == 0) return LA_OK;
+  DeviceInfo info;
+  if ((st = require_sm100(&info)) != LA_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool tc = use_tensor_cores(dtype, d_qk, d_v);
+  if (!tc && !chunked_simt_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
+  if (seq_len == 0) {
+    // no tokens: the final state is the initial state (or zero)
+    if (final_state) {
+      const size_t bytes = state_floats(bh, d_qk, d_v) * sizeof(float);
+      cudaError_t e = init_state ? cudaMemcpyAsync(final_state, init_state, bytes,
+                                                   cudaMemcpyDeviceToDevice, s)
+                                 : cudaMemsetAsync(final_state, 0, bytes, s);
+      return cuda_status(e);
+    }
+    return LA_OK;
+  }
+  const int g = segments == 0 ? auto_segments(bh, seq_len, info.sm_count)
+                              : effective_segments(seq_len, segments);
+  const int64_t seg_len = g > 1 ? segment_len(seq_len, g) : seq_len;
+  float *seg_states = nullptr;
+  if (g > 1) {
+    const size_t need = la_based_chunked_workspace_size(bh, seq_len, d_qk, d_v, g);
+    if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u))
+      return LA_ERR_WORKSPACE;
+    seg_states = (float *)workspace;
+  } else if (flags & LA_CHUNKED_REUSE_SEGMENTS) {
+    return LA_ERR_INVALID_ARGUMENT;  // nothing to reuse without segments
+  }
+  const bool normalize = (flags & LA_CHUNKED_NORMALIZE) != 0;
+  if (g > 1 && !(flags & LA_CHUNKED_REUSE_SEGMENTS)) {
+    // states of segments 0 .. g-2 seed the later segments
+    st = tc ? launch_chunked_state_tc(k, v, seg_states, bh, seq_len, g, g - 1, seg_len, info, s)
+            : launch_chunked_state_simt(k, v, seg_states, bh, seq_len, (int)d_qk, (int)d_v,
+                                        dtype, g, seg_len, s);
+    if (st != LA_OK) return st;
+  }
+  if (tc)
+    return launch_chunked_output_tc(q, k, v, out, init_state, final_state, seg_states, bh,
+                                    seq_len, eps, normalize, g, seg_len, info, s);
+  return launch_chunked_output_simt(q, k, v, out, init_state, final_state, seg_states, bh,
+                                    seq_len, (int)d_qk, (int)d_v, dtype, eps, normalize, g,
+                                    seg_len, s);
+}
+
+int la_based_chunked_state(const void *k, const void *v, float *state_out, int64_t batch,
+                           int64_t heads, int64_t seq_len, int64_t d_qk, int64_t d_v, int dtype,
+                           void *workspace, size_t workspace_bytes, int segments, void *stream) {
+  if (batch < 0 || heads < 0 || seq_len < 0 || d_qk < 1 || d_v < 1 || segments < 0 ||
+      !valid_dtype(dtype))
+    return LA_ERR_INVALID_ARGUMENT;
+  const int64_t bh = batch * heads;
+  if (bh == 0) return LA_OK;
+  if (!state_out || (seq_len > 0 && (!k || !v))) return LA_ERR_INVALID_ARGUMENT;
+  if (bh > 65535) return LA_ERR_UNSUPPORTED;
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != LA_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t state_bytes = state_floats(bh, d_qk, d_v) * sizeof(float);
+  if (seq_len == 0) return cuda_status(cudaMemsetAsync(state_out, 0, state_bytes, s));
+  const bool tc = use_tensor_cores(dtype, d_qk, d_v);
+  if (!tc && !chunked_simt_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
+  int g = segments == 0 ? auto_segments(bh, seq_len, info.sm_count)
+                        : effective_segments(seq_len, segments);
+  if (g > 1) {
+    const size_t need = la_based_chunked_workspace_size(bh, seq_len, d_qk, d_v, g);
+    if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u))
+      return LA_ERR_WORKSPACE;
+  }
+  const int64_t seg_len = g > 1 ? segment_len(seq_len, g) : seq_len;
+  float *dst = g > 1 ? (float *)workspace : state_out;
+  st = tc ? launch_chunked_state_tc(k, v, dst, bh, seq_len, g, g, seg_len, info, s)
+          : launch_chunked_state_simt(k, v, dst, bh, seq_len, (int)d_qk, (int)d_v, dtype, g,
+                                      seg_len, s);
+  if (st != LA_OK || g == 1) return st;
+  return launch_sum_segments(dst, state_out, bh, g, (int64_t)feature_dim(d_qk) * (d_v + 1), s);
+}
+
+int la_sliding_window_fwd(const void *q, const void *k, const void *v, void *out, int64_t batch,
+                          int64_t heads, int64_t seq_len, int64_t head_dim, int dtype,
+                          int64_t window, void *stream) {
+  int st = check_common(q, k, v, out, batch, heads, seq_len, head_dim, head_dim, dtype);
+  if (st != LA_OK) return st;
+  if (window < 1) return LA_ERR_INVALID_ARGUMENT;
+  if (batch * heads * seq_len == 0) return LA_OK;
+  DeviceInfo info;
+  if ((st = require_sm100(&info)) != LA_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == LA_DTYPE_BFLOAT16 && head_dim == 64 && tc_kernels_enabled())
+    return launch_sliding_tc(q, k, v, out, batch * heads, seq_len, window, info, s);
+  return launch_sliding_simt(q, k, v, out, batch * heads, seq_len, (int)head_dim, dtype, window,
+                             s);
+}
+
+}  // extern "C"

@@ -1,0 +1,520 @@
+// CUDA-core (SIMT) kernels: the fp32 path and the generic-shape path.
+//
+// These compute in fp32 on CUDA cores for any head widths up to 128 and any
+// sequence length.  They are the permanent fp32 implementation (BASED config
+// 1 asks for rel-L2 <= 1e-4 against the fp32 reference, beyond what bf16 /
+// tf32 tensor-core operands give) and cover shapes the tensor-core kernels do
+// not specialise.  Layout of every tensor: (batch*heads, seq_len, d) row-major.
+#include "common.cuh"
+
+#include <math.h>
+
+namespace la {
+namespace {
+
+constexpr int kRows = 64;          // query rows per CTA
+constexpr int kLanesPerRow = 4;    // threads cooperating on one query row
+constexpr int kThreads = kRows * kLanesPerRow;
+constexpr int kKeyTile = 64;       // keys staged in shared memory per step
+constexpr int kMaxD = 128;
+constexpr int kMaxCols = (kMaxD + 1 + kLanesPerRow - 1) / kLanesPerRow;  // 33
+
+template <typename T>
+__device__ __forceinline__ void load_tile(float *dst, int ld_dst, const T *src, int64_t row0,
+                                          int64_t nrows_total, int rows, int cols, float mul) {
+  for (int idx = threadIdx.x; idx < rows * cols; idx += blockDim.x) {
+    int r = idx / cols, c = idx - r * cols;
+    int64_t gr = row0 + r;
+    float x = 0.f;
+    if (gr >= 0 && gr < nrows_total) x = to_f32(src[gr * cols + c]) * mul;
+    dst[r * ld_dst + c] = x;
+  }
+}
+
+// Sum over the kLanesPerRow threads of one row (they are adjacent lanes).
+__device__ __forceinline__ float row_allreduce(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  x += __shfl_xor_sync(0xffffffffu, x, 2);
+  return x;
+}
+
+// ---------------------------------------------------------------------------
+// Parallel BASED (kernels/pytorch_attention.py:27-42 semantics).
+// grid (ceil(n/64), bh); 256 threads = 64 query rows x 4 lanes.  Each lane
+// owns output columns lane, lane+4, ...; the q.k dot product is split over the
+// 4 lanes and all-reduced, so every lane sees the same poly weight.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+based_parallel_simt_kernel(const T *__restrict__ q, const T *__restrict__ k,
+                           const T *__restrict__ v, T *__restrict__ out, int64_t n, int dqk,
+                           int dv, float scale, float eps) {
+  extern __shared__ float smem[];
+  const int ldq = dqk + 1;
+  float *qs = smem;                       // [64][dqk+1]
+  float *ks = qs + kRows * ldq;           // [64][dqk+1]
+  float *vs = ks + kKeyTile * ldq;        // [64][dv]
+
+  const int64_t bh = blockIdx.y;
+  const int64_t q0 = (int64_t)blockIdx.x * kRows;
+  const int row = threadIdx.x / kLanesPerRow;
+  const int lane = threadIdx.x % kLanesPerRow;
+  const int64_t qi = q0 + row;
+  const T *qh = q + bh * n * dqk;
+  const T *kh = k + bh * n * dqk;
+  const T *vh = v + bh * n * dv;
+
+  load_tile(qs, ldq, qh, q0, n, kRows, dqk, scale);
+
+  float acc[kMaxCols];
+#pragma unroll
+  for (int i = 0; i < kMaxCols; ++i) acc[i] = 0.f;
+  float den = 0.f;
+
+  const int64_t last_key = min64(n, q0 + kRows) - 1;
+  for (int64_t k0 = 0; k0 <= last_key; k0 += kKeyTile) {
+    __syncthreads();
+    load_tile(ks, ldq, kh, k0, n, kKeyTile, dqk, 1.f);
+    load_tile(vs, dv, vh, k0, n, kKeyTile, dv, 1.f);
+    __syncthreads();
+    const int jmax = (int)min64(kKeyTile, last_key - k0 + 1);
+    for (int j = 0; j < jmax; ++j) {
+      float s = 0.f;
+      for (int a = lane; a < dqk; a += kLanesPerRow) s = fmaf(qs[row * ldq + a], ks[j * ldq + a], s);
+      s = row_allreduce(s);
+      float p = fmaf(s, fmaf(0.5f, s, 1.f), 1.f);  // 1 + s + s^2/2
+      p = (k0 + j <= qi) ? p : 0.f;
+      den += p;
+#pragma unroll
+      for (int i = 0; i < kMaxCols; ++i) {
+        int c = lane + i * kLanesPerRow;
+        if (c < dv) acc[i] = fmaf(p, vs[j * dv + c], acc[i]);
+      }
+    }
+  }
+  if (qi < n) {
+    const float inv = 1.f / (den + eps);
+    T *oh = out + (bh * n + qi) * dv;
+#pragma unroll
+    for (int i = 0; i < kMaxCols; ++i) {
+      int c = lane + i * kLanesPerRow;
+      if (c < dv) oh[c] = from_f32<T>(acc[i] * inv);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Sliding-window softmax (benchmarks/sliding_attention_benchmark.py:32-56
+// semantics), online softmax over the band [i-W+1, i] only.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+sliding_simt_kernel(const T *__restrict__ q, const T *__restrict__ k, const T *__restrict__ v,
+                    T *__restrict__ out, int64_t n, int d, int64_t window, float scale) {
+  extern __shared__ float smem[];
+  const int ldq = d + 1;
+  float *qs = smem;
+  float *ks = qs + kRows * ldq;
+  float *vs = ks + kKeyTile * ldq;
+
+  const int64_t bh = blockIdx.y;
+  const int64_t q0 = (int64_t)blockIdx.x * kRows;
+  const int row = threadIdx.x / kLanesPerRow;
+  const int lane = threadIdx.x % kLanesPerRow;
+  const int64_t qi = q0 + row;
+  const T *qh = q + bh * n * d;
+  const T *kh = k + bh * n * d;
+  const T *vh = v + bh * n * d;
+
+  load_tile(qs, ldq, qh, q0, n, kRows, d, scale);
+
+  float acc[kMaxCols];
+#pragma unroll
+  for (int i = 0; i < kMaxCols; ++i) acc[i] = 0.f;
+  float m = -INFINITY, l = 0.f;
+
+  const int64_t first_key = max64(0, q0 - window + 1);
+  const int64_t last_key = min64(n, q0 + kRows) - 1;
+  for (int64_t k0 = first_key; k0 <= last_key; k0 += kKeyTile) {
+    __syncthreads();
+    load_tile(ks, ldq, kh, k0, n, kKeyTile, d, 1.f);
+    load_tile(vs, d, vh, k0, n, kKeyTile, d, 1.f);
+    __syncthreads();
+    const int jmax = (int)min64(kKeyTile, last_key - k0 + 1);
+    for (int j = 0; j < jmax; ++j) {
+      const int64_t key = k0 + j;
+      float s = 0.f;
+      for (int a = lane; a < d; a += kLanesPerRow) s = fmaf(qs[row * ldq + a], ks[j * ldq + a], s);
+      s = row_allreduce(s);
+      const bool valid = key <= qi && key >= qi - window + 1;
+      if (!valid) continue;  // uniform across the 4 lanes of the row
+      if (s > m) {
+        const float corr = expf(m - s);  // exp(-inf) = 0 on the first valid key
+        l *= corr;
+#pragma unroll
+        for (int i = 0; i < kMaxCols; ++i) acc[i] *= corr;
+        m = s;
+      }
+      const float p = expf(s - m);
+      l += p;
+#pragma unroll
+      for (int i = 0; i < kMaxCols; ++i) {
+        int c = lane + i * kLanesPerRow;
+        if (c < d) acc[i] = fmaf(p, vs[j * d + c], acc[i]);
+      }
+    }
+  }
+  if (qi < n) {
+    const float inv = 1.f / l;
+    T *oh = out + (bh * n + qi) * d;
+#pragma unroll
+    for (int i = 0; i < kMaxCols; ++i) {
+      int c = lane + i * kLanesPerRow;
+      if (c < d) oh[c] = from_f32<T>(acc[i] * inv);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Chunked recurrent BASED (kernels/nki_attention_chunked.py:71-109 recurrence,
+// plus the normaliser as state column d_v).  The state S[F][dv+1] (fp32) lives
+// in shared memory for the whole segment.  Key-side basis phi_k = [1, k_a,
+// k_a k_b (a<=b)], query side phi_q = [1, q_a/sqrt(d), q_a q_b w_ab].
+// ---------------------------------------------------------------------------
+constexpr int kChunk = 64;
+
+struct ChunkSmem {
+  float *S;   // [F][dv+1]
+  float *qs;  // [64][dqk+1]   raw q
+  float *ks;  // [64][dqk+1]   raw k
+  float *vs;  // [64][dv+1]    v with a trailing 1 (normaliser column)
+};
+
+__device__ __forceinline__ ChunkSmem carve(float *smem, int F, int dqk, int dv) {
+  ChunkSmem c;
+  c.S = smem;
+  c.qs = c.S + F * (dv + 1);
+  c.ks = c.qs + kChunk * (dqk + 1);
+  c.vs = c.ks + kChunk * (dqk + 1);
+  return c;
+}
+
+template <typename T>
+__device__ __forceinline__ void load_chunk_kv(const ChunkSmem &c, const T *kh, const T *vh,
+                                              int64_t t0, int64_t t_end, int dqk, int dv) {
+  const int ldk = dqk + 1, ldv = dv + 1;
+  for (int idx = threadIdx.x; idx < kChunk * dqk; idx += blockDim.x) {
+    int r = idx / dqk, a = idx - r * dqk;
+    int64_t t = t0 + r;
+    c.ks[r * ldk + a] = t < t_end ? to_f32(kh[t * dqk + a]) : 0.f;
+  }
+  for (int idx = threadIdx.x; idx < kChunk * ldv; idx += blockDim.x) {
+    int r = idx / ldv, e = idx - r * ldv;
+    int64_t t = t0 + r;
+    float x = 0.f;
+    if (t < t_end) x = (e < dv) ? to_f32(vh[t * dv + e]) : 1.f;
+    c.vs[r * ldv + e] = x;
+  }
+}
+
+// S[f][e] += sum_{t in chunk} phi_k(k_t)[f] * vaug_t[e]; thread per feature row
+// (rows strided by blockDim), columns in register blocks of 32.
+__device__ void chunk_state_update(const ChunkSmem &c, int F, int dqk, int dv, int rows) {
+  const int ldk = dqk + 1, ldv = dv + 1;
+  for (int f = threadIdx.x; f < F; f += blockDim.x) {
+    // decode feature f -> (a, b) ; kind 0 const, 1 linear, 2 quadratic
+    int kind, a = 0, b = 0;
+    if (f == 0) {
+      kind = 0;
+    } else if (f <= dqk) {
+      kind = 1;
+      a = f - 1;
+    } else {
+      kind = 2;
+      int r = f - 1 - dqk;
+      a = 0;
+      while (r >= dqk - a) {
+        r -= dqk - a;
+        ++a;
+      }
+      b = a + r;
+    }
+    for (int e0 = 0; e0 < ldv; e0 += 32) {
+      float acc[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+      for (int t = 0; t < rows; ++t) {
+        float phi = 1.f;
+        if (kind == 1) phi = c.ks[t * ldk + a];
+        if (kind == 2) phi = c.ks[t * ldk + a] * c.ks[t * ldk + b];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (e0 + i < ldv) acc[i] = fmaf(phi, c.vs[t * ldv + e0 + i], acc[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (e0 + i < ldv) c.S[f * ldv + e0 + i] += acc[i];
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+chunked_state_simt_kernel(const T *__restrict__ k, const T *__restrict__ v,
+                          float *__restrict__ seg_states, int64_t n, int dqk, int dv,
+                          int segments, int64_t seg_len) {
+  extern __shared__ float smem[];
+  const int F = (int)feature_dim(dqk);
+  const int ldv = dv + 1;
+  ChunkSmem c = carve(smem, F, dqk, dv);
+  const int64_t bh = blockIdx.y;
+  const int g = blockIdx.x;
+  const int64_t t_begin = (int64_t)g * seg_len;
+  const int64_t t_end = min64(n, t_begin + seg_len);
+  const T *kh = k + bh * n * dqk;
+  const T *vh = v + bh * n * dv;
+  for (int i = threadIdx.x; i < F * ldv; i += blockDim.x) c.S[i] = 0.f;
+  for (int64_t t0 = t_begin; t0 < t_end; t0 += kChunk) {
+    __syncthreads();
+    load_chunk_kv(c, kh, vh, t0, t_end, dqk, dv);
+    __syncthreads();
+    chunk_state_update(c, F, dqk, dv, (int)min64(kChunk, t_end - t0));
+  }
+  __syncthreads();
+  float *dst = seg_states + (bh * segments + g) * (int64_t)F * ldv;
+  for (int i = threadIdx.x; i < F * ldv; i += blockDim.x) dst[i] = c.S[i];
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+chunked_output_simt_kernel(const T *__restrict__ q, const T *__restrict__ k,
+                           const T *__restrict__ v, T *__restrict__ out,
+                           const float *__restrict__ init_state, float *__restrict__ final_state,
+                           const float *__restrict__ seg_states, int64_t n, int dqk, int dv,
+                           float eps, int normalize, int segments, int64_t seg_len) {
+  extern __shared__ float smem[];
+  const int F = (int)feature_dim(dqk);
+  const int ldv = dv + 1, ldq = dqk + 1;
+  ChunkSmem c = carve(smem, F, dqk, dv);
+  const int64_t bh = blockIdx.y;
+  const int g = blockIdx.x;
+  const int64_t t_begin = (int64_t)g * seg_len;
+  const int64_t t_end = min64(n, t_begin + seg_len);
+  const T *qh = q + bh * n * dqk;
+  const T *kh = k + bh * n * dqk;
+  const T *vh = v + bh * n * dv;
+
+  // prefix state: init + sum of earlier segments, summed in segment order
+  for (int i = threadIdx.x; i < F * ldv; i += blockDim.x) {
+    float s = init_state ? init_state[bh * (int64_t)F * ldv + i] : 0.f;
+    for (int gg = 0; gg < g; ++gg) s += seg_states[(bh * segments + gg) * (int64_t)F * ldv + i];
+    c.S[i] = s;
+  }
+
+  const int row = threadIdx.x / kLanesPerRow;
+  const int lane = threadIdx.x % kLanesPerRow;
+  const float rsd = 1.f / sqrtf((float)dqk);
+  const float w_diag = 1.f / (2.f * dqk), w_off = 1.f / (float)dqk;
+
+  for (int64_t t0 = t_begin; t0 < t_end; t0 += kChunk) {
+    __syncthreads();
+    load_chunk_kv(c, kh, vh, t0, t_end, dqk, dv);
+    for (int idx = threadIdx.x; idx < kChunk * dqk; idx += blockDim.x) {
+      int r = idx / dqk, a = idx - r * dqk;
+      int64_t t = t0 + r;
+      c.qs[r * ldq + a] = t < t_end ? to_f32(qh[t * dqk + a]) : 0.f;
+    }
+    __syncthreads();
+    const int rows = (int)min64(kChunk, t_end - t0);
+
+    float acc[kMaxCols];
+#pragma unroll
+    for (int i = 0; i < kMaxCols; ++i) acc[i] = 0.f;
+    const float *qr = c.qs + row * ldq;
+    // inter-chunk: phi_q(q_t) . S (state before this chunk's update)
+    {
+      int f = 0;
+#pragma unroll
+      for (int i = 0; i < kMaxCols; ++i) {
+        int e = lane + i * kLanesPerRow;
+        if (e < ldv) acc[i] = c.S[e];
+      }
+      f = 1;
+      for (int a = 0; a < dqk; ++a, ++f) {
+        const float phi = qr[a] * rsd;
+#pragma unroll
+        for (int i = 0; i < kMaxCols; ++i) {
+          int e = lane + i * kLanesPerRow;
+          if (e < ldv) acc[i] = fmaf(phi, c.S[f * ldv + e], acc[i]);
+        }
+      }
+      for (int a = 0; a < dqk; ++a) {
+        for (int b = a; b < dqk; ++b, ++f) {
+          const float phi = qr[a] * qr[b] * (a == b ? w_diag : w_off);
+#pragma unroll
+          for (int i = 0; i < kMaxCols; ++i) {
+            int e = lane + i * kLanesPerRow;
+            if (e < ldv) acc[i] = fmaf(phi, c.S[f * ldv + e], acc[i]);
+          }
+        }
+      }
+    }
+    // intra-chunk: causal 1 + s + s^2/2 against this chunk's keys.  The loop
+    // bound is uniform over the CTA (the all-reduce is a full-warp shuffle);
+    // keys after the row are masked to weight 0.
+    for (int j = 0; j < rows; ++j) {
+      float s = 0.f;
+      for (int a = lane; a < dqk; a += kLanesPerRow) s = fmaf(qr[a], c.ks[j * ldq + a], s);
+      s = row_allreduce(s) * rsd;
+      float p = fmaf(s, fmaf(0.5f, s, 1.f), 1.f);
+      p = (j <= row) ? p : 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxCols; ++i) {
+        int e = lane + i * kLanesPerRow;
+        if (e < ldv) acc[i] = fmaf(p, c.vs[j * ldv + e], acc[i]);
+      }
+    }
+    // the lane holding column dv broadcasts the denominator to its row
+    float den_part = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxCols; ++i)
+      if (lane + i * kLanesPerRow == dv) den_part = acc[i];
+    const float den = row_allreduce(den_part);
+    if (row < rows) {
+      const float inv = normalize ? 1.f / (den + eps) : 1.f;
+      T *oh = out + (bh * n + t0 + row) * dv;
+#pragma unroll
+      for (int i = 0; i < kMaxCols; ++i) {
+        int e = lane + i * kLanesPerRow;
+        if (e < dv) oh[e] = from_f32<T>(acc[i] * inv);
+      }
+    }
+    __syncthreads();  // every row read S before the update
+    chunk_state_update(c, F, dqk, dv, rows);
+  }
+  if (final_state && g == segments - 1) {
+    __syncthreads();
+    float *dst = final_state + bh * (int64_t)F * ldv;
+    for (int i = threadIdx.x; i < F * ldv; i += blockDim.x) dst[i] = c.S[i];
+  }
+}
+
+size_t chunked_simt_smem(int dqk, int dv) {
+  const int64_t F = feature_dim(dqk);
+  return sizeof(float) * (size_t)(F * (dv + 1) + 2 * kChunk * (dqk + 1) + kChunk * (dv + 1));
+}
+
+}  // namespace
+
+bool chunked_simt_supported(int64_t dqk, int64_t dv) {
+  if (dqk < 1 || dqk > kMaxD || dv < 1 || dv > kMaxD) return false;
+  return chunked_simt_smem((int)dqk, (int)dv) <= 200 * 1024;
+}
+
+#define LA_DISPATCH_DTYPE(dtype, T, ...)                    \
+  do {                                                      \
+    if ((dtype) == LA_DTYPE_FLOAT32) {                      \
+      using T = float;                                      \
+      __VA_ARGS__;                                          \
+    } else if ((dtype) == LA_DTYPE_BFLOAT16) {              \
+      using T = __nv_bfloat16;                              \
+      __VA_ARGS__;                                          \
+    } else {                                                \
+      return LA_ERR_INVALID_ARGUMENT;                       \
+    }                                                       \
+  } while (0)
+
+int launch_parallel_simt(const void *q, const void *k, const void *v, void *out, int64_t bh,
+                         int64_t n, int dqk, int dv, int dtype, float eps, cudaStream_t s) {
+  if (dqk > kMaxD || dv > kMaxD) return LA_ERR_UNSUPPORTED;
+  const size_t smem = sizeof(float) * (size_t)((kRows + kKeyTile) * (dqk + 1) + kKeyTile * dv);
+  dim3 grid((unsigned)((n + kRows - 1) / kRows), (unsigned)bh);
+  const float scale = 1.f / sqrtf((float)dqk);
+  LA_DISPATCH_DTYPE(dtype, T, {
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(based_parallel_simt_kernel<T>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return LA_ERR_CUDA;
+    }
+    based_parallel_simt_kernel<T><<<grid, kThreads, smem, s>>>(
+        (const T *)q, (const T *)k, (const T *)v, (T *)out, n, dqk, dv, scale, eps);
+  });
+  return check_launch();
+}
+
+int launch_sliding_simt(const void *q, const void *k, const void *v, void *out, int64_t bh,
+                        int64_t n, int d, int dtype, int64_t window, cudaStream_t s) {
+  if (d > kMaxD) return LA_ERR_UNSUPPORTED;
+  const size_t smem = sizeof(float) * (size_t)((kRows + kKeyTile) * (d + 1) + kKeyTile * d);
+  dim3 grid((unsigned)((n + kRows - 1) / kRows), (unsigned)bh);
+  const float scale = 1.f / sqrtf((float)d);
+  LA_DISPATCH_DTYPE(dtype, T, {
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(sliding_simt_kernel<T>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return LA_ERR_CUDA;
+    }
+    sliding_simt_kernel<T><<<grid, kThreads, smem, s>>>((const T *)q, (const T *)k, (const T *)v,
+                                                        (T *)out, n, d, window, scale);
+  });
+  return check_launch();
+}
+
+int launch_chunked_state_simt(const void *k, const void *v, float *seg_states, int64_t bh,
+                              int64_t n, int dqk, int dv, int dtype, int segments,
+                              int64_t seg_len, cudaStream_t s) {
+  if (!chunked_simt_supported(dqk, dv)) return LA_ERR_UNSUPPORTED;
+  const size_t smem = chunked_simt_smem(dqk, dv);
+  dim3 grid((unsigned)segments, (unsigned)bh);
+  LA_DISPATCH_DTYPE(dtype, T, {
+    cudaError_t e = cudaFuncSetAttribute(chunked_state_simt_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return LA_ERR_CUDA;
+    chunked_state_simt_kernel<T><<<grid, kThreads, smem, s>>>(
+        (const T *)k, (const T *)v, seg_states, n, dqk, dv, segments, seg_len);
+  });
+  return check_launch();
+}
+
+int launch_chunked_output_simt(const void *q, const void *k, const void *v, void *out,
+                               const float *init_state, float *final_state,
+                               const float *seg_states, int64_t bh, int64_t n, int dqk, int dv,
+                               int dtype, float eps, bool normalize, int segments,
+                               int64_t seg_len, cudaStream_t s) {
+  if (!chunked_simt_supported(dqk, dv)) return LA_ERR_UNSUPPORTED;
+  const size_t smem = chunked_simt_smem(dqk, dv);
+  dim3 grid((unsigned)segments, (unsigned)bh);
+  LA_DISPATCH_DTYPE(dtype, T, {
+    cudaError_t e = cudaFuncSetAttribute(chunked_output_simt_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return LA_ERR_CUDA;
+    chunked_output_simt_kernel<T><<<grid, kThreads, smem, s>>>(
+        (const T *)q, (const T *)k, (const T *)v, (T *)out, init_state, final_state, seg_states,
+        n, dqk, dv, eps, normalize ? 1 : 0, segments, seg_len);
+  });
+  return check_launch();
+}
+
+}  // namespace la
+
+namespace la {
+namespace {
+__global__ void sum_segments_kernel(const float *__restrict__ seg, float *__restrict__ out,
+                                    int segments, int64_t per_head) {
+  const int64_t bh = blockIdx.y;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per_head;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int g = 0; g < segments; ++g) acc += seg[(bh * segments + g) * per_head + i];
+    out[bh * per_head + i] = acc;
+  }
+}
+}  // namespace
+
+int launch_sum_segments(const float *seg, float *out, int64_t bh, int segments, int64_t per_head,
+                        cudaStream_t s) {
+  dim3 grid((unsigned)((per_head + 255) / 256), (unsigned)bh);
+  sum_segments_kernel<<<grid, 256, 0, s>>>(seg, out, segments, per_head);
+  return check_launch();
+}
+}  // namespace la

@@ -1,0 +1,35 @@
+// Launchers of the tcgen05 / TMEM / TMA tensor-core kernels (sm_100a).
+//
+// Fast-path shapes: bf16 inputs, d_qk = 16 and d_v = 64 for BASED, head_dim =
+// 64 for the sliding window.  Every other request goes to the SIMT kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace la {
+
+// True when this build contains the tensor-core kernels.
+bool tc_kernels_enabled();
+
+int launch_parallel_tc(const void *q, const void *k, const void *v, void *out, int64_t bh,
+                       int64_t n, float eps, const DeviceInfo &info, cudaStream_t s);
+
+// State pass over segments [0, n_launch) of every head (n_launch <= segments).
+int launch_chunked_state_tc(const void *k, const void *v, float *seg_states, int64_t bh,
+                            int64_t n, int segments, int n_launch, int64_t seg_len,
+                            const DeviceInfo &info, cudaStream_t s);
+
+int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *out,
+                             const float *init_state, float *final_state,
+                             const float *seg_states, int64_t bh, int64_t n, float eps,
+                             bool normalize, int segments, int64_t seg_len,
+                             const DeviceInfo &info, cudaStream_t s);
+
+int launch_sliding_tc(const void *q, const void *k, const void *v, void *out, int64_t bh,
+                      int64_t n, int64_t window, const DeviceInfo &info, cudaStream_t s);
+
+// out[bh][i] = sum_g seg[bh][g][i]  (fixed order, deterministic)
+int launch_sum_segments(const float *seg, float *out, int64_t bh, int segments, int64_t per_head,
+                        cudaStream_t s);
+
+}  // namespace la

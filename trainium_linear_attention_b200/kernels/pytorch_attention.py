@@ -1,0 +1,82 @@
+"""BASED causal attention: the reference's public API on B200 kernels.
+
+Same names, signatures and defaults as kernels/pytorch_attention.py of the
+reference:
+
+* ``ref_based_attn(q, k, v, eps=1e-6)`` -- the reference formula in plain
+  PyTorch (kernels/pytorch_attention.py:27-42), for comparisons only; no
+  CUDA path calls it.
+* ``solution_nki(q, k, v, eps=1e-6)`` -- the name of the reference's device
+  path (kernels/pytorch_attention.py:44-78); here the sm_100a parallel fused
+  kernel.  d_v may differ from d_qk (the reference assumes they are equal).
+* ``solution(q, k, v, eps=1e-6)`` -- dispatch (kernels/pytorch_attention.py:
+  81-92).  It picks the parallel or the chunked kernel by sequence length and
+  RAISES on failure; unlike the reference it never falls back to PyTorch.
+* ``_check_nki()`` -- whether the native kernels can run here
+  (kernels/pytorch_attention.py:16-24).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import ops
+
+_native_available = None
+
+#: sequence length up to which ``solution`` uses the parallel kernel (bf16
+#: tensor-core path); longer sequences use the chunked kernel.
+CROSSOVER_SEQ_LEN_BF16 = 1024
+#: the same for fp32 inputs (both SIMT kernels)
+CROSSOVER_SEQ_LEN_FP32 = 2048
+
+
+def _check_nki() -> bool:
+    """True when the native library loads and a CUDA device is visible."""
+    global _native_available
+    if _native_available is None:
+        try:
+            from .. import _native
+            _native.lib()
+            _native_available = torch.cuda.is_available()
+        except Exception:
+            _native_available = False
+    return _native_available
+
+
+def ref_based_attn(q, k, v, eps=1e-6):
+    """Reference BASED causal attention in plain PyTorch (any device).
+
+    q, k: (b, h, t, d_qk); v: (b, h, t, d_v).  Returns (b, h, t, d_v).
+    Computed in the input dtype, as the reference does.
+    """
+    d = q.shape[-1]
+    scale = 1.0 / math.sqrt(d)
+    scores = torch.matmul(q * scale, k.transpose(-2, -1))
+    poly = 1.0 + scores + 0.5 * scores * scores
+    t = q.shape[-2]
+    mask = torch.tril(torch.ones(t, t, device=q.device, dtype=q.dtype))
+    masked = poly * mask
+    den = masked.sum(dim=-1, keepdim=True) + eps
+    return torch.matmul(masked, v) / den
+
+
+def solution_nki(q, k, v, eps=1e-6):
+    """BASED causal attention via the sm_100a parallel fused kernel.
+
+    q, k: (b, h, t, d_qk); v: (b, h, t, d_v), CUDA, float32 or bfloat16.
+    Returns (b, h, t, d_v) in q.dtype.
+    """
+    return ops.based_parallel(q, k, v, eps=eps)
+
+
+def solution(q, k, v, eps=1e-6):
+    """BASED causal attention on B200: parallel kernel for short sequences,
+    chunked recurrent kernel for long ones.  Raises on any failure."""
+    t = q.shape[-2]
+    limit = CROSSOVER_SEQ_LEN_FP32 if q.dtype == torch.float32 else CROSSOVER_SEQ_LEN_BF16
+    if t <= limit:
+        return ops.based_parallel(q, k, v, eps=eps)
+    return ops.based_chunked(q, k, v, eps=eps)

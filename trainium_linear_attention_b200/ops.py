@@ -1,0 +1,165 @@
+"""Torch-facing calls into the native library (device memory + streams only).
+
+Every function takes ``(b, h, t, d)`` CUDA tensors, enqueues the kernel on
+``torch.cuda.current_stream()`` and returns a freshly allocated output in
+``q.dtype``.  Inputs are never modified.  Failures raise; nothing falls back
+to another implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native as N
+
+_DTYPES = {torch.float32: N.LA_DTYPE_FLOAT32, torch.bfloat16: N.LA_DTYPE_BFLOAT16}
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}; expected float32 or bfloat16") from None
+
+
+def _check_qkv(q, k, v, same_dv: bool = False):
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if t.device.type != "cuda":
+            raise ValueError(f"{name} must be a CUDA tensor (got {t.device}); "
+                             "this library has no CPU implementation")
+        if t.dim() != 4:
+            raise ValueError(f"{name} must be (batch, heads, seq_len, dim), got shape {tuple(t.shape)}")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError(f"q, k, v dtypes differ: {q.dtype}, {k.dtype}, {v.dtype}")
+    if not (q.device == k.device == v.device):
+        raise ValueError("q, k, v are on different devices")
+    if q.shape != k.shape:
+        raise ValueError(f"q and k shapes differ: {tuple(q.shape)} vs {tuple(k.shape)}")
+    if v.shape[:3] != q.shape[:3]:
+        raise ValueError(f"v shape {tuple(v.shape)} does not match q {tuple(q.shape)}")
+    if same_dv and v.shape[-1] != q.shape[-1]:
+        raise ValueError("v must have the same head dim as q for this op")
+    return _dtype_code(q)
+
+
+def _stream_ptr(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def based_parallel(q, k, v, eps: float = 1e-6) -> torch.Tensor:
+    """Parallel (quadratic) BASED attention, normalised, causal."""
+    code = _check_qkv(q, k, v)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    b, h, t, d = q.shape
+    dv = v.shape[-1]
+    out = torch.empty((b, h, t, dv), dtype=q.dtype, device=q.device)
+    with torch.cuda.device(q.device):
+        st = N.lib().la_based_parallel_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(out), b, h, t, d, dv,
+                                           code, float(eps), _stream_ptr(q.device))
+    N.check(st, "la_based_parallel_fwd")
+    return out
+
+
+def feature_dim(d_qk: int) -> int:
+    return 1 + d_qk + d_qk * (d_qk + 1) // 2
+
+
+def chunked_plan(batch_heads: int, seq_len: int, d_qk: int, d_v: int, dtype: torch.dtype,
+                 segments: int = 0):
+    """(segments, workspace_bytes) the library will use for this shape."""
+    g = ctypes.c_int(0)
+    ws = ctypes.c_size_t(0)
+    st = N.lib().la_based_chunked_plan(batch_heads, seq_len, d_qk, d_v, _DTYPES[dtype],
+                                       int(segments), ctypes.byref(g), ctypes.byref(ws))
+    N.check(st, "la_based_chunked_plan")
+    return g.value, ws.value
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor | None:
+    if nbytes == 0:
+        return None
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+def based_chunked(q, k, v, chunk_size: int = 64, eps: float = 1e-6, normalize: bool = True,
+                  init_state: torch.Tensor | None = None, return_state: bool = False,
+                  segments: int = 0, workspace: torch.Tensor | None = None,
+                  reuse_segments: bool = False):
+    """Chunked recurrent BASED attention.
+
+    ``init_state`` / the returned final state are fp32 ``(b*h, F, d_v + 1)``
+    in the key-side feature basis documented in ``include/la_attention.h``.
+    """
+    code = _check_qkv(q, k, v)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    b, h, t, d = q.shape
+    dv = v.shape[-1]
+    if chunk_size < 1:
+        raise ValueError("chunk_size must be >= 1")
+    F = feature_dim(d)
+    if init_state is not None:
+        if (init_state.dtype != torch.float32 or init_state.device != q.device
+                or tuple(init_state.shape) != (b * h, F, dv + 1)):
+            raise ValueError(f"init_state must be float32 {(b * h, F, dv + 1)} on {q.device}")
+        init_state = init_state.contiguous()
+    out = torch.empty((b, h, t, dv), dtype=q.dtype, device=q.device)
+    final = torch.empty((b * h, F, dv + 1), dtype=torch.float32, device=q.device) if return_state else None
+    with torch.cuda.device(q.device):
+        g, ws_bytes = chunked_plan(b * h, t, d, dv, q.dtype, segments)
+        if workspace is None:
+            workspace = _workspace(ws_bytes, q.device)
+        elif workspace.numel() * workspace.element_size() < ws_bytes:
+            raise ValueError(f"workspace too small: need {ws_bytes} bytes")
+        flags = (N.LA_CHUNKED_NORMALIZE if normalize else 0) | (
+            N.LA_CHUNKED_REUSE_SEGMENTS if reuse_segments else 0)
+        st = N.lib().la_based_chunked_fwd(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(out), b, h, t, d, dv, code, int(chunk_size),
+            float(eps), flags, _ptr(init_state), _ptr(final), _ptr(workspace),
+            0 if workspace is None else workspace.numel() * workspace.element_size(), g,
+            _stream_ptr(q.device))
+    N.check(st, "la_based_chunked_fwd")
+    if return_state:
+        return out, final
+    return out
+
+
+def based_chunked_state(k, v, segments: int = 0, workspace: torch.Tensor | None = None):
+    """Total state sum_j phi_k(k_j) [v_j, 1]^T per head, fp32 ``(b*h, F, d_v+1)``."""
+    code = _check_qkv(k, k, v)
+    k, v = k.contiguous(), v.contiguous()
+    b, h, t, d = k.shape
+    dv = v.shape[-1]
+    state = torch.empty((b * h, feature_dim(d), dv + 1), dtype=torch.float32, device=k.device)
+    with torch.cuda.device(k.device):
+        g, ws_bytes = chunked_plan(b * h, t, d, dv, k.dtype, segments)
+        if workspace is None:
+            workspace = _workspace(ws_bytes, k.device)
+        st = N.lib().la_based_chunked_state(
+            _ptr(k), _ptr(v), _ptr(state), b, h, t, d, dv, code, _ptr(workspace),
+            0 if workspace is None else workspace.numel() * workspace.element_size(), g,
+            _stream_ptr(k.device))
+    N.check(st, "la_based_chunked_state")
+    return state
+
+
+def sliding_window(q, k, v, window_size: int = 64) -> torch.Tensor:
+    """Causal sliding-window softmax attention over [i - W + 1, i]."""
+    code = _check_qkv(q, k, v, same_dv=True)
+    if int(window_size) < 1:
+        raise ValueError("window_size must be >= 1")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    b, h, t, d = q.shape
+    out = torch.empty_like(q)
+    with torch.cuda.device(q.device):
+        st = N.lib().la_sliding_window_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(out), b, h, t, d, code,
+                                           int(window_size), _stream_ptr(q.device))
+    N.check(st, "la_sliding_window_fwd")
+    return out
