@@ -39,6 +39,7 @@ extern "C" {
 #define LA_ERR_CUDA              3  /* a CUDA runtime / launch error               */
 #define LA_ERR_WORKSPACE         4  /* workspace missing, too small or misaligned  */
 #define LA_ERR_NO_DEVICE         5  /* no sm_100 device is current                 */
+#define LA_ERR_DEVICE_TIMEOUT    6  /* a kernel abandoned a wait that never ended  */
 
 /* ---- element types --------------------------------------------------------*/
 #define LA_DTYPE_FLOAT32   0
@@ -54,6 +55,14 @@ const char *la_status_string(int status);
 
 /* ABI version of this header (bumped on any incompatible change). */
 int la_abi_version(void);
+
+/* Every wait inside the tensor-core kernels is bounded (2 s); a kernel that
+ * gives up records it in a per-device error word and exits cleanly, leaving
+ * the CUDA context usable.  This call synchronises `stream`, then returns
+ * LA_ERR_DEVICE_TIMEOUT (and clears the word) if any kernel of this library
+ * on the current device has given up since the last call, else LA_OK.
+ * The reference has no counterpart (its dispatcher hides all failures). */
+int la_take_device_error(void *stream);
 
 /* Width F of the Taylor feature basis for key width d_qk: 1 + d + d(d+1)/2
  * (153 at d_qk = 16).  Replaces the width computed by the reference's

@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_status_strings():
     assert N.status_string(N.LA_OK) == "ok"
-    for code in range(1, 6):
+    for code in range(1, 7):
         assert N.status_string(code) not in ("ok", "unknown status")
     assert N.status_string(99) == "unknown status"
 

@@ -20,6 +20,7 @@ LA_ERR_UNSUPPORTED = 2
 LA_ERR_CUDA = 3
 LA_ERR_WORKSPACE = 4
 LA_ERR_NO_DEVICE = 5
+LA_ERR_DEVICE_TIMEOUT = 6
 
 LA_DTYPE_FLOAT32 = 0
 LA_DTYPE_BFLOAT16 = 1
@@ -31,6 +32,7 @@ LA_CHUNKED_REUSE_SEGMENTS = 2
 EXPORTED_SYMBOLS = (
     "la_status_string",
     "la_abi_version",
+    "la_take_device_error",
     "la_based_feature_dim",
     "la_based_parallel_fwd",
     "la_based_chunked_plan",
@@ -63,6 +65,8 @@ def _declare(lib) -> None:
     lib.la_status_string.restype = ctypes.c_char_p
     lib.la_abi_version.argtypes = []
     lib.la_abi_version.restype = _int
+    lib.la_take_device_error.argtypes = [_p]
+    lib.la_take_device_error.restype = _int
     lib.la_based_feature_dim.argtypes = [_i64]
     lib.la_based_feature_dim.restype = _i64
     lib.la_based_parallel_fwd.argtypes = [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _f, _p]

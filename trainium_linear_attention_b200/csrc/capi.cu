@@ -9,6 +9,29 @@
 
 namespace la {
 
+// The library's device error word (one per device that loads the library).
+__device__ int la_device_error_word;
+
+int *device_error_word() {
+  static std::mutex mu;
+  static int *cache[64] = {};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    int *ptr = nullptr;
+    if (cudaGetSymbolAddress((void **)&ptr, la_device_error_word) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    cache[dev] = ptr;
+  }
+  return cache[dev];
+}
+
 int current_device_info(DeviceInfo *info) {
   static std::mutex mu;
   static DeviceInfo cache[64];
@@ -83,7 +106,7 @@ int auto_segments(int64_t bh, int64_t n, int sm_count) {
 }
 
 bool use_tensor_cores(int dtype, int64_t dqk, int64_t dv) {
-  return dtype == LA_DTYPE_BFLOAT16 && dqk == 16 && dv == 64 && tc_kernels_enabled();
+  return dtype == LA_DTYPE_BFLOAT16 && dqk == 16 && dv == 64;
 }
 
 size_t state_floats(int64_t bh, int64_t dqk, int64_t dv) {
@@ -105,11 +128,31 @@ const char *la_status_string(int status) {
     case LA_ERR_CUDA: return "CUDA error";
     case LA_ERR_WORKSPACE: return "workspace missing, too small or misaligned";
     case LA_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
+    case LA_ERR_DEVICE_TIMEOUT: return "a kernel gave up on a wait that never completed";
     default: return "unknown status";
   }
 }
 
 int la_abi_version(void) { return 1; }
+
+int la_take_device_error(void *stream) {
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != LA_OK) return st;
+  if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return LA_ERR_CUDA;
+  int *word = device_error_word();
+  if (!word) return LA_ERR_CUDA;
+  int value = 0;
+  if (cudaMemcpy(&value, word, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return LA_ERR_CUDA;
+  if (value != 0) {
+    const int zero = 0;
+    if (cudaMemcpy(word, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+      return LA_ERR_CUDA;
+    return LA_ERR_DEVICE_TIMEOUT;
+  }
+  return LA_OK;
+}
 
 int64_t la_based_feature_dim(int64_t d_qk) { return d_qk < 1 ? 0 : feature_dim(d_qk); }
 
@@ -121,7 +164,7 @@ int la_based_parallel_fwd(const void *q, const void *k, const void *v, void *out
   DeviceInfo info;
   if ((st = require_sm100(&info)) != LA_OK) return st;
   cudaStream_t s = (cudaStream_t)stream;
-  if (use_tensor_cores(dtype, d_qk, d_v))
+  if (use_tensor_cores(dtype, d_qk, d_v) && tc_parallel_enabled())
     return launch_parallel_tc(q, k, v, out, batch * heads, seq_len, eps, info, s);
   return launch_parallel_simt(q, k, v, out, batch * heads, seq_len, (int)d_qk, (int)d_v, dtype,
                               eps, s);
@@ -170,7 +213,7 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
   DeviceInfo info;
   if ((st = require_sm100(&info)) != LA_OK) return st;
   cudaStream_t s = (cudaStream_t)stream;
-  const bool tc = use_tensor_cores(dtype, d_qk, d_v);
+  const bool tc = use_tensor_cores(dtype, d_qk, d_v) && tc_chunked_enabled();
   if (!tc && !chunked_simt_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
   if (seq_len == 0) {
     // no tokens: the final state is the initial state (or zero)
@@ -227,7 +270,7 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
   cudaStream_t s = (cudaStream_t)stream;
   const size_t state_bytes = state_floats(bh, d_qk, d_v) * sizeof(float);
   if (seq_len == 0) return cuda_status(cudaMemsetAsync(state_out, 0, state_bytes, s));
-  const bool tc = use_tensor_cores(dtype, d_qk, d_v);
+  const bool tc = use_tensor_cores(dtype, d_qk, d_v) && tc_chunked_enabled();
   if (!tc && !chunked_simt_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
   int g = segments == 0 ? auto_segments(bh, seq_len, info.sm_count)
                         : effective_segments(seq_len, segments);
@@ -255,7 +298,7 @@ int la_sliding_window_fwd(const void *q, const void *k, const void *v, void *out
   DeviceInfo info;
   if ((st = require_sm100(&info)) != LA_OK) return st;
   cudaStream_t s = (cudaStream_t)stream;
-  if (dtype == LA_DTYPE_BFLOAT16 && head_dim == 64 && tc_kernels_enabled())
+  if (dtype == LA_DTYPE_BFLOAT16 && head_dim == 64 && tc_sliding_enabled())
     return launch_sliding_tc(q, k, v, out, batch * heads, seq_len, window, info, s);
   return launch_sliding_simt(q, k, v, out, batch * heads, seq_len, (int)head_dim, dtype, window,
                              s);

@@ -1,0 +1,651 @@
+// Chunked recurrent BASED attention on tcgen05 tensor cores (sm_100a).
+//
+// Fast path: bf16 q/k/v, d_qk = 16, d_v = 64.  One CTA owns one (head,
+// segment) and walks its tokens in 128-token tiles.  Per tile c (Q, K, V are
+// the tile's rows, S_c the fp32 state of all earlier tokens, phi the Taylor
+// feature map in the query/key-split basis of include/la_attention.h):
+//
+//   scores = Q K^T                      tcgen05 M=128 N=128 K=16 -> TMEM
+//   P      = tril(1 + s + s^2/2)        s = scores/4, CUDA cores, P -> TMEM (bf16)
+//   O      = phi(Q) S_c                 tcgen05 M=128 N=80  K=160, A = phi(Q) in TMEM
+//   O     += P V                        tcgen05 M=128 N=64  K=128, A = P in TMEM
+//   S^T   += [V 1 0]^T phi(K)           tcgen05 M=128 N=160 K=128 (state in TMEM)
+//   out    = O[:, :64] / (O[:, 64] + rowsum(P) + eps)
+//
+// which is the reference recurrence of kernels/nki_attention_chunked.py:71-109
+// (acc_o = Q_phi S; scores = Q_phi K_phi^T; S += K_phi^T V; acc_o +=
+// tril(scores) V) with the intra-tile term evaluated in the equivalent
+// polynomial form 1 + s + s^2/2 and the normaliser carried as state row 64.
+// The 153 features never touch HBM: phi(Q) is written straight to TMEM and
+// phi(K) to shared memory by the thread that owns the token.
+//
+// Warp roles (448 threads):
+//   warp 0      TMA producer (Q, K, V tiles; 2-stage ring)
+//   warp 1      TMEM allocator + single-thread MMA issuer
+//   warps 2-5   feature warpgroup: phi(Q) -> TMEM, phi(K) -> smem
+//   warps 6-9   polynomial + epilogue warpgroup
+//   warps 10-13 state warpgroup: S^T (TMEM, fp32) -> bf16 snapshot in smem
+//
+// The state-only variant (kStateOnly) runs just the phi(K) / update path and
+// writes the segment's state; it seeds the later segments of a head.
+#include <mutex>
+#include <utility>
+
+#include "tc_common.cuh"
+#include "tc_kernels.cuh"
+
+namespace la {
+namespace {
+using namespace tc;
+
+constexpr int kT = 128;       // tokens per tile
+constexpr int kDqk = 16;
+constexpr int kDv = 64;
+constexpr int kF = 153;       // 1 + 16 + 136 features
+constexpr int kFPad = 160;    // padded feature count (K of phi(Q) S, N of the update)
+constexpr int kSV = kDv + 1;  // state columns in global memory: values + normaliser
+constexpr int kNO = 80;       // N of phi(Q) S: 64 values, normaliser, 15 zero rows
+
+constexpr int kWarpTma = 0, kWarpMma = 1, kWarpFeat = 2, kWarpPoly = 6, kWarpState = 10;
+constexpr int kThreads = 14 * 32;
+
+// TMEM columns (one CTA per SM owns all 512)
+constexpr uint32_t kColS = 0;       // S^T  128 lanes x 160 fp32
+constexpr uint32_t kColO = 160;     // O    128 lanes x 80 fp32
+constexpr uint32_t kColPhiQ = 256;  // phi(Q) bf16 pairs, 80 columns
+constexpr uint32_t kColSc = 384;    // scores fp32 (128) / P bf16 pairs (64)
+constexpr uint32_t kTmemCols = 512;
+
+// Shared memory (offsets from a 1024-byte aligned base)
+constexpr uint32_t kQBytes = kT * kDqk * 2;     // 4 KB, 32B-swizzled rows
+constexpr uint32_t kVBytes = kT * kDv * 2;      // 16 KB, 128B-swizzled rows
+constexpr uint32_t kOffQ = 0;                   // 2 stages
+constexpr uint32_t kOffK = kOffQ + 2 * kQBytes;
+constexpr uint32_t kOffV = kOffK + 2 * kQBytes;  // 16384
+constexpr uint32_t kOffOnes = kOffV + 2 * kVBytes;  // 49152: 16 rows x 128 B
+constexpr uint32_t kOffPhiK = kOffOnes + 2048;      // 51200: 3 feature blocks x 16 KB
+constexpr uint32_t kPhiKBlock = kT * 128;
+constexpr uint32_t kOffSnap = kOffPhiK + 3 * kPhiKBlock;  // 100352: 2 x 30 KB
+constexpr uint32_t kSnapKBlock = kNO * 128;               // 10 KB per 64-feature block
+constexpr uint32_t kSnapBytes = 3 * kSnapKBlock;
+constexpr uint32_t kOffBar = kOffSnap + 2 * kSnapBytes;   // 161792
+constexpr uint32_t kSmemBytes = kOffBar + 256;
+constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;        // alignment slack
+
+static_assert(kOffV % 1024 == 0 && kOffOnes % 1024 == 0 && kOffPhiK % 1024 == 0 &&
+                  kOffSnap % 1024 == 0 && kSnapKBlock % 1024 == 0,
+              "128B-swizzled regions need 1024-byte alignment");
+
+enum Bar { kFull0, kFull1, kEmpty0, kEmpty1, kPhiReady, kPhiFree, kScReady, kPReady, kOReady,
+           kOFree, kSReady, kSnapReady, kDone, kNumBars };
+
+// Feature f of the query/key-split basis ->
+//   kind 0: 1;  kind 1: x_a;  kind 2: x_a x_b (a < b);  kind 3: x_a^2;  kind 4: padding 0.
+// Evaluated at compile time: every caller indexes with an unrolled constant.
+__host__ __device__ constexpr int feat_quad_row(int r) {  // row a of quadratic index r
+  int a = 0;
+  while (a < kDqk - 1 && r >= kDqk - a) {
+    r -= kDqk - a;
+    ++a;
+  }
+  return a;
+}
+__host__ __device__ constexpr int feat_quad_col(int r) {
+  int a = 0;
+  while (a < kDqk - 1 && r >= kDqk - a) {
+    r -= kDqk - a;
+    ++a;
+  }
+  return a + r;
+}
+__host__ __device__ constexpr int feat_kind(int f) {
+  return f == 0 ? 0 : f <= kDqk ? 1 : f >= kF ? 4
+                : (feat_quad_row(f - 1 - kDqk) == feat_quad_col(f - 1 - kDqk) ? 3 : 2);
+}
+__host__ __device__ constexpr int feat_a(int f) {
+  return f == 0 || f >= kF ? 0 : f <= kDqk ? f - 1 : feat_quad_row(f - 1 - kDqk);
+}
+__host__ __device__ constexpr int feat_b(int f) {
+  return f == 0 || f >= kF ? 0 : f <= kDqk ? f - 1 : feat_quad_col(f - 1 - kDqk);
+}
+static_assert(feat_kind(17) == 3 && feat_a(18) == 0 && feat_b(18) == 1 && feat_kind(152) == 3 &&
+                  feat_a(152) == 15 && feat_b(151) == 15 && feat_a(151) == 14 && feat_kind(153) == 4,
+              "feature order: const, 16 linear, (a, b) a <= b row-major");
+
+// Key side: [1, k_a, k_a k_b]; the scale factors all live on the query side.
+template <int F>
+__device__ __forceinline__ float phi_k(const float (&x)[kDqk], bool valid) {
+  constexpr int kind = feat_kind(F), a = feat_a(F), b = feat_b(F);
+  if constexpr (kind == 0) return valid ? 1.f : 0.f;
+  else if constexpr (kind == 1) return x[a];
+  else if constexpr (kind == 4) return 0.f;
+  else return x[a] * x[b];
+}
+// Query side: [1, q_a / 4, q_a q_b / 16 (a < b), q_a^2 / 32]  (d = 16)
+template <int F>
+__device__ __forceinline__ float phi_q(const float (&x)[kDqk]) {
+  constexpr int kind = feat_kind(F), a = feat_a(F), b = feat_b(F);
+  if constexpr (kind == 0) return 1.f;
+  else if constexpr (kind == 1) return x[a] * 0.25f;
+  else if constexpr (kind == 2) return x[a] * x[b] * 0.0625f;
+  else if constexpr (kind == 3) return x[a] * x[a] * 0.03125f;
+  else return 0.f;
+}
+
+// phi(K) chunk J (features 8J .. 8J+7) of token `row` -> 128B-swizzled smem
+template <int J>
+__device__ __forceinline__ void store_phik_chunk(const float (&x)[kDqk], bool valid, uint32_t base,
+                                                 int row) {
+  st_shared_v4(base + (J >> 3) * (kT * 128) + sw128_offset(row, J & 7),
+               pack_bf16(phi_k<8 * J + 0>(x, valid), phi_k<8 * J + 1>(x, valid)),
+               pack_bf16(phi_k<8 * J + 2>(x, valid), phi_k<8 * J + 3>(x, valid)),
+               pack_bf16(phi_k<8 * J + 4>(x, valid), phi_k<8 * J + 5>(x, valid)),
+               pack_bf16(phi_k<8 * J + 6>(x, valid), phi_k<8 * J + 7>(x, valid)));
+}
+template <int... J>
+__device__ __forceinline__ void store_phik(const float (&x)[kDqk], bool valid, uint32_t base,
+                                           int row, std::integer_sequence<int, J...>) {
+  (store_phik_chunk<J>(x, valid, base, row), ...);
+}
+
+// phi(Q) columns [16G, 16G+16) (features 32G .. 32G+31) of TMEM lane `row`
+template <int G, int... I>
+__device__ __forceinline__ void store_phiq_group(const float (&x)[kDqk], uint32_t addr,
+                                                 std::integer_sequence<int, I...>) {
+  const uint32_t w[16] = {pack_bf16(phi_q<32 * G + 2 * I>(x), phi_q<32 * G + 2 * I + 1>(x))...};
+  tmem_st16(addr, w);
+}
+template <int... G>
+__device__ __forceinline__ void store_phiq(const float (&x)[kDqk], uint32_t addr0,
+                                           std::integer_sequence<int, G...>) {
+  (store_phiq_group<G>(x, addr0 + 16 * G, std::make_integer_sequence<int, 16>{}), ...);
+}
+
+struct Params {
+  __nv_bfloat16 *out;
+  const float *init_state;  // (bh, F, 65) or null
+  float *final_state;       // (bh, F, 65) or null (written by the last segment)
+  const float *seg_states;  // (bh, G, F, 65): states of earlier segments (output pass)
+  float *seg_out;           // (bh, G, F, 65): this segment's state (state pass)
+  int *err;                 // device error word
+  int64_t n;
+  int64_t seg_len;
+  int segments;
+  float eps;
+  int normalize;
+};
+
+__device__ __forceinline__ bool wait_teardown(uint64_t *bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - t0 > kWaitTimeoutNs) return false;
+  return true;
+}
+
+template <bool kStateOnly>
+__global__ void __launch_bounds__(kThreads, 1)
+chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const uint32_t sb = smem_u32(smem);
+  uint64_t *bars = (uint64_t *)(smem + kOffBar);
+  uint32_t *tmem_slot = (uint32_t *)(smem + kOffBar + 8 * kNumBars);
+  volatile int *abort_flag = (volatile int *)(smem + kOffBar + 8 * kNumBars + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int g = blockIdx.x;
+  const int64_t bh = blockIdx.y;
+  const int64_t t_begin = (int64_t)g * p.seg_len;
+  const int64_t t_end = min64(p.n, t_begin + p.seg_len);
+  const int n_chunks = (int)((t_end - t_begin + kT - 1) / kT);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[kFull0], 1);
+    mbar_init(&bars[kFull1], 1);
+    mbar_init(&bars[kEmpty0], 2);
+    mbar_init(&bars[kEmpty1], 2);
+    for (int i = kPhiReady; i < kNumBars; ++i) mbar_init(&bars[i], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  // constant "ones" block: A-operand rows 64..127 of [V 1 0]^T for 16 tokens;
+  // row 64 (element 0 of each token row, 128B-swizzled) is 1, the rest 0.
+  for (int i = threadIdx.x; i < 2048 / 4; i += kThreads) {
+    const int row = (i * 4) / 128, byte = (i * 4) % 128;
+    const uint32_t one = (byte == (row & 7) * 16) ? 0x3F80u : 0u;
+    *(uint32_t *)(smem + kOffOnes + i * 4) = one;
+  }
+  if (warp == kWarpMma) tmem_alloc(tmem_slot, kTmemCols);
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kWarpTma) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
+      if (!kStateOnly) prefetch_tmap(&tm_q);
+      int issued = 0;
+      for (int c = 0; c < n_chunks; ++c) {
+        const int s = c & 1;
+        if (c >= 2 && !mbar_wait(&bars[kEmpty0 + s], ((c >> 1) - 1) & 1, abort_flag)) break;
+        const uint32_t bytes = (kStateOnly ? kQBytes : 2 * kQBytes) + kVBytes;
+        mbar_arrive_expect_tx(&bars[kFull0 + s], bytes);
+        const int row = (int)(t_begin + (int64_t)c * kT);
+        if (!kStateOnly) tma_load_3d(smem + kOffQ + s * kQBytes, &tm_q, &bars[kFull0 + s], 0, row, (int)bh);
+        tma_load_3d(smem + kOffK + s * kQBytes, &tm_k, &bars[kFull0 + s], 0, row, (int)bh);
+        tma_load_3d(smem + kOffV + s * kVBytes, &tm_v, &bars[kFull0 + s], 0, row, (int)bh);
+        issued = c + 1;
+      }
+      // every issued copy must land before the CTA can exit
+      for (int c = issued - 2 < 0 ? 0 : issued - 2; c < issued; ++c)
+        wait_teardown(&bars[kFull0 + (c & 1)], (c >> 1) & 1);
+    }
+  } else if (warp == kWarpMma) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_sc = make_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t id_qs = make_idesc_bf16(128, kNO, false, false);
+      constexpr uint32_t id_pv = make_idesc_bf16(128, kDv, false, true);
+      constexpr uint32_t id_up = make_idesc_bf16(128, kFPad, true, true);
+      const uint32_t a_ones = sb + kOffOnes;
+      bool ok = mbar_wait(&bars[kSnapReady], 0, abort_flag);  // S_0 in TMEM (+ snapshot 0)
+      auto issue_scores = [&](int s) {
+        const uint64_t da = make_sdesc(sb + kOffQ + s * kQBytes, 16, 256, kSwizzle32B);
+        const uint64_t db = make_sdesc(sb + kOffK + s * kQBytes, 16, 256, kSwizzle32B);
+        umma_ss(tmem + kColSc, da, db, id_sc, 0);
+        umma_commit(&bars[kScReady]);
+      };
+      if (!kStateOnly && ok) {
+        ok = mbar_wait(&bars[kFull0], 0, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          issue_scores(0);
+        }
+      }
+      for (int c = 0; ok && c < n_chunks; ++c) {
+        const int s = c & 1;
+        if (!mbar_wait(&bars[kPhiReady], c & 1, abort_flag)) break;
+        const uint32_t v_base = sb + kOffV + s * kVBytes;
+        if (!kStateOnly) {
+          if (c > 0 && !mbar_wait(&bars[kSnapReady], c & 1, abort_flag)) break;
+          if (c > 0 && !mbar_wait(&bars[kOFree], (c - 1) & 1, abort_flag)) break;
+          tc_fence_after();
+          // O = phi(Q) S_c   (K = 160 features in 10 steps of 16)
+          const uint32_t snap = sb + kOffSnap + (c & 1) * kSnapBytes;
+#pragma unroll
+          for (int j = 0; j < kFPad / 16; ++j) {
+            const uint64_t db = make_sdesc(snap + (j >> 2) * kSnapKBlock + (j & 3) * 32, 16, 1024,
+                                           kSwizzle128B);
+            umma_ts(tmem + kColO, tmem + kColPhiQ + 8 * j, db, id_qs, j > 0 ? 1u : 0u);
+          }
+          if (!mbar_wait(&bars[kPReady], c & 1, abort_flag)) break;
+          tc_fence_after();
+          // O[:, :64] += P V   (K = 128 tokens in 8 steps)
+#pragma unroll
+          for (int j = 0; j < kT / 16; ++j) {
+            const uint64_t db = make_sdesc(v_base + j * 2048, 8192, 1024, kSwizzle128B);
+            umma_ts(tmem + kColO, tmem + kColSc + 8 * j, db, id_pv, 1u);
+          }
+          umma_commit(&bars[kOReady]);
+        } else {
+          tc_fence_after();
+        }
+        // S^T += [V 1 0]^T phi(K)   (K = 128 tokens in 8 steps)
+#pragma unroll
+        for (int j = 0; j < kT / 16; ++j) {
+          const uint32_t a_addr = v_base + j * 2048;
+          const uint64_t da = make_sdesc(a_addr, a_ones - a_addr, 1024, kSwizzle128B);
+          const uint64_t db = make_sdesc(sb + kOffPhiK + j * 2048, kPhiKBlock, 1024, kSwizzle128B);
+          umma_ss(tmem + kColS, da, db, id_up, 1u);
+        }
+        umma_commit(&bars[kSReady]);
+        umma_commit(&bars[kPhiFree]);
+        umma_commit(&bars[kEmpty0 + s]);
+        if (!kStateOnly && c + 1 < n_chunks) {
+          if (!mbar_wait(&bars[kFull0 + ((c + 1) & 1)], ((c + 1) >> 1) & 1, abort_flag)) break;
+          if (!mbar_wait(&bars[kOReady], c & 1, abort_flag)) break;  // P region free again
+          tc_fence_after();
+          issue_scores((c + 1) & 1);
+        }
+      }
+      umma_commit(&bars[kDone]);
+    }
+  } else if (warp < kWarpPoly) {
+    // ------------------------------------------------------------ features
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;  // token within the tile == TMEM lane
+    const bool leader = (warp == kWarpFeat && lane == 0);
+    for (int c = 0; c < n_chunks; ++c) {
+      const int s = c & 1;
+      mbar_wait(&bars[kFull0 + s], (c >> 1) & 1, abort_flag);
+      if (!wg_ok(1, abort_flag)) break;
+      const int valid = (int)min64(kT, t_end - (t_begin + (int64_t)c * kT));
+      const bool vrow = row < valid;
+      uint32_t kw[8], qw[8];
+      const uint32_t kt = sb + kOffK + s * kQBytes;
+      ld_shared_v4(kt + sw32_offset(row, 0), kw[0], kw[1], kw[2], kw[3]);
+      ld_shared_v4(kt + sw32_offset(row, 1), kw[4], kw[5], kw[6], kw[7]);
+      if (!kStateOnly) {
+        const uint32_t qt = sb + kOffQ + s * kQBytes;
+        ld_shared_v4(qt + sw32_offset(row, 0), qw[0], qw[1], qw[2], qw[3]);
+        ld_shared_v4(qt + sw32_offset(row, 1), qw[4], qw[5], qw[6], qw[7]);
+      }
+      named_barrier_sync(1, 128);
+      if (leader) mbar_arrive(&bars[kEmpty0 + s]);
+      if (c > 0) mbar_wait(&bars[kPhiFree], (c - 1) & 1, abort_flag);
+      if (!wg_ok(1, abort_flag)) break;
+      tc_fence_after();
+      float kx[kDqk];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        kx[2 * i] = vrow ? bf16lo(kw[i]) : 0.f;
+        kx[2 * i + 1] = vrow ? bf16hi(kw[i]) : 0.f;
+      }
+      // phi(K): 20 chunks of 8 features, 128B-swizzled, 64 features per block
+      store_phik(kx, vrow, sb + kOffPhiK, row, std::make_integer_sequence<int, kFPad / 8>{});
+      if (!kStateOnly) {
+        float qx[kDqk];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          qx[2 * i] = bf16lo(qw[i]);
+          qx[2 * i + 1] = bf16hi(qw[i]);
+        }
+        // phi(Q): 80 bf16 pairs into TMEM lane `row`
+        store_phiq(qx, taddr(tmem, wq * 32, kColPhiQ), std::make_integer_sequence<int, kFPad / 32>{});
+        tmem_wait_st();
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      named_barrier_sync(1, 128);
+      if (leader) mbar_arrive(&bars[kPhiReady]);
+    }
+  } else if (warp < kWarpState) {
+    // ------------------------------------------------------------ polynomial + epilogue
+    if (!kStateOnly) {
+      const int wq = warp & 3;
+      const int row = wq * 32 + lane;
+      const bool leader = (warp == kWarpPoly && lane == 0);
+      for (int c = 0; c < n_chunks; ++c) {
+        const int64_t t0 = t_begin + (int64_t)c * kT;
+        const int valid = (int)min64(kT, t_end - t0);
+        mbar_wait(&bars[kScReady], c & 1, abort_flag);
+        if (!wg_ok(2, abort_flag)) break;
+        tc_fence_after();
+        float rs = 0.f;
+#pragma unroll
+        for (int G = 0; G < kT / 32; ++G) {
+          uint32_t r0[16], r1[16], w[16];
+          tmem_ld16(taddr(tmem, wq * 32, kColSc + 32 * G), r0);
+          tmem_ld16(taddr(tmem, wq * 32, kColSc + 32 * G + 16), r1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int j0 = 32 * G + 2 * i;
+            const uint32_t x0 = i < 8 ? r0[2 * i] : r1[2 * i - 16];
+            const uint32_t x1 = i < 8 ? r0[2 * i + 1] : r1[2 * i - 15];
+            const float s0 = 0.25f * __uint_as_float(x0);
+            const float s1 = 0.25f * __uint_as_float(x1);
+            float p0 = fmaf(s0, fmaf(0.5f, s0, 1.f), 1.f);
+            float p1 = fmaf(s1, fmaf(0.5f, s1, 1.f), 1.f);
+            p0 = (j0 <= row && j0 < valid) ? p0 : 0.f;
+            p1 = (j0 + 1 <= row && j0 + 1 < valid) ? p1 : 0.f;
+            rs += p0 + p1;
+            w[i] = pack_bf16(p0, p1);
+          }
+          // P columns [16G, 16G + 16) hold keys [32G, 32G + 32); those
+          // score columns were all read above
+          tmem_st16(taddr(tmem, wq * 32, kColSc + 16 * G), w);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        named_barrier_sync(2, 128);
+        if (leader) mbar_arrive(&bars[kPReady]);
+
+        mbar_wait(&bars[kOReady], c & 1, abort_flag);
+        if (!wg_ok(2, abort_flag)) break;
+        tc_fence_after();
+        uint32_t dr[16];
+        tmem_ld16(taddr(tmem, wq * 32, kColO + 64), dr);
+        tmem_wait_ld();
+        const float den = __uint_as_float(dr[0]) + rs + p.eps;
+        const float inv = p.normalize ? 1.f / den : 1.f;
+        __nv_bfloat16 *orow = p.out + ((uint64_t)bh * p.n + t0 + row) * kDv;
+#pragma unroll
+        for (int G = 0; G < kDv / 16; ++G) {
+          uint32_t r[16];
+          tmem_ld16(taddr(tmem, wq * 32, kColO + 16 * G), r);
+          tmem_wait_ld();
+          if (row < valid) {
+            uint4 lo, hi;
+            lo.x = pack_bf16(__uint_as_float(r[0]) * inv, __uint_as_float(r[1]) * inv);
+            lo.y = pack_bf16(__uint_as_float(r[2]) * inv, __uint_as_float(r[3]) * inv);
+            lo.z = pack_bf16(__uint_as_float(r[4]) * inv, __uint_as_float(r[5]) * inv);
+            lo.w = pack_bf16(__uint_as_float(r[6]) * inv, __uint_as_float(r[7]) * inv);
+            hi.x = pack_bf16(__uint_as_float(r[8]) * inv, __uint_as_float(r[9]) * inv);
+            hi.y = pack_bf16(__uint_as_float(r[10]) * inv, __uint_as_float(r[11]) * inv);
+            hi.z = pack_bf16(__uint_as_float(r[12]) * inv, __uint_as_float(r[13]) * inv);
+            hi.w = pack_bf16(__uint_as_float(r[14]) * inv, __uint_as_float(r[15]) * inv);
+            *(uint4 *)(orow + 16 * G) = lo;
+            *(uint4 *)(orow + 16 * G + 8) = hi;
+          }
+        }
+        tc_fence_before();
+        named_barrier_sync(2, 128);
+        if (leader) mbar_arrive(&bars[kOFree]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ state
+    const int wq = warp & 3;
+    const int e = wq * 32 + lane;  // row of S^T: value column e (< 64), normaliser (64)
+    const bool leader = (warp == kWarpState && lane == 0);
+    const bool real = e < kSV;
+    // S_0 = init_state + states of the earlier segments (fixed order)
+    for (int grp = 0; grp < kFPad / 16; ++grp) {
+      uint32_t w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int f = 16 * grp + i;
+        float x = 0.f;
+        if (!kStateOnly && real && f < kF) {
+          if (p.init_state) x = p.init_state[((uint64_t)bh * kF + f) * kSV + e];
+          for (int gg = 0; gg < g; ++gg)
+            x += p.seg_states[(((uint64_t)bh * p.segments + gg) * kF + f) * kSV + e];
+        }
+        w[i] = __float_as_uint(x);
+      }
+      tmem_st16(taddr(tmem, wq * 32, kColS + 16 * grp), w);
+      if (!kStateOnly && e < kNO) {
+        const uint32_t snap = sb + kOffSnap;  // buffer 0
+        const int f0 = 16 * grp;
+        const uint32_t blk = snap + (f0 >> 6) * kSnapKBlock;
+        st_shared_v4(blk + sw128_offset(e, (f0 & 63) >> 3),
+                     pack_bf16(__uint_as_float(w[0]), __uint_as_float(w[1])),
+                     pack_bf16(__uint_as_float(w[2]), __uint_as_float(w[3])),
+                     pack_bf16(__uint_as_float(w[4]), __uint_as_float(w[5])),
+                     pack_bf16(__uint_as_float(w[6]), __uint_as_float(w[7])));
+        st_shared_v4(blk + sw128_offset(e, ((f0 & 63) >> 3) + 1),
+                     pack_bf16(__uint_as_float(w[8]), __uint_as_float(w[9])),
+                     pack_bf16(__uint_as_float(w[10]), __uint_as_float(w[11])),
+                     pack_bf16(__uint_as_float(w[12]), __uint_as_float(w[13])),
+                     pack_bf16(__uint_as_float(w[14]), __uint_as_float(w[15])));
+      }
+    }
+    tmem_wait_st();
+    fence_proxy_async_smem();
+    tc_fence_before();
+    named_barrier_sync(3, 128);
+    if (leader) mbar_arrive(&bars[kSnapReady]);
+
+    if (kStateOnly) {
+      // the segment's state, once every update has completed
+      mbar_wait(&bars[kDone], 0, abort_flag);
+      if (wg_ok(3, abort_flag)) {
+        tc_fence_after();
+        float *dst = p.seg_out + ((uint64_t)bh * p.segments + g) * kF * kSV;
+        for (int grp = 0; grp < kFPad / 16; ++grp) {
+          uint32_t r[16];
+          tmem_ld16(taddr(tmem, wq * 32, kColS + 16 * grp), r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int f = 16 * grp + i;
+            if (real && f < kF) dst[(uint64_t)f * kSV + e] = __uint_as_float(r[i]);
+          }
+        }
+      }
+    } else {
+      const bool write_final = p.final_state != nullptr && g == p.segments - 1;
+      for (int c = 0; c < n_chunks; ++c) {
+        mbar_wait(&bars[kSReady], c & 1, abort_flag);
+        if (!wg_ok(3, abort_flag)) break;
+        tc_fence_after();
+        const bool last = c == n_chunks - 1;
+        const uint32_t snap = sb + kOffSnap + ((c + 1) & 1) * kSnapBytes;
+        for (int grp = 0; grp < kFPad / 16; ++grp) {
+          uint32_t r[16];
+          tmem_ld16(taddr(tmem, wq * 32, kColS + 16 * grp), r);
+          tmem_wait_ld();
+          if (e < kNO) {
+            const int f0 = 16 * grp;
+            const uint32_t blk = snap + (f0 >> 6) * kSnapKBlock;
+            st_shared_v4(blk + sw128_offset(e, (f0 & 63) >> 3),
+                         pack_bf16(__uint_as_float(r[0]), __uint_as_float(r[1])),
+                         pack_bf16(__uint_as_float(r[2]), __uint_as_float(r[3])),
+                         pack_bf16(__uint_as_float(r[4]), __uint_as_float(r[5])),
+                         pack_bf16(__uint_as_float(r[6]), __uint_as_float(r[7])));
+            st_shared_v4(blk + sw128_offset(e, ((f0 & 63) >> 3) + 1),
+                         pack_bf16(__uint_as_float(r[8]), __uint_as_float(r[9])),
+                         pack_bf16(__uint_as_float(r[10]), __uint_as_float(r[11])),
+                         pack_bf16(__uint_as_float(r[12]), __uint_as_float(r[13])),
+                         pack_bf16(__uint_as_float(r[14]), __uint_as_float(r[15])));
+          }
+          if (last && write_final && real) {
+            float *dst = p.final_state + (uint64_t)bh * kF * kSV;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int f = 16 * grp + i;
+              if (f < kF) dst[(uint64_t)f * kSV + e] = __uint_as_float(r[i]);
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        named_barrier_sync(3, 128);
+        if (leader) mbar_arrive(&bars[kSnapReady]);
+      }
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    if (lane == 0) wait_teardown(&bars[kDone], 0);
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, kErrTimeout);
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)ptr;
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// 3-D map over (bh, n, d) bf16 with a (1, 128, d) box; rows past n read as zero.
+bool make_map(CUtensorMap *map, const void *base, int64_t bh, int64_t n, int d,
+              CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || ((uintptr_t)base & 15)) return false;
+  cuuint64_t gdim[3] = {(cuuint64_t)d, (cuuint64_t)n, (cuuint64_t)bh};
+  cuuint64_t gstride[2] = {(cuuint64_t)d * 2, (cuuint64_t)n * d * 2};
+  cuuint32_t box[3] = {(cuuint32_t)d, (cuuint32_t)kT, 1};
+  cuuint32_t estride[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), gdim, gstride,
+            box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool kStateOnly>
+int launch(const void *q, const void *k, const void *v, const Params &p, int64_t bh, int n_launch,
+           cudaStream_t s) {
+  if (bh > 65535 || p.n > INT32_MAX) return LA_ERR_UNSUPPORTED;
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mk, k, bh, p.n, kDqk, CU_TENSOR_MAP_SWIZZLE_32B) ||
+      !make_map(&mv, v, bh, p.n, kDv, CU_TENSOR_MAP_SWIZZLE_128B))
+    return LA_ERR_CUDA;
+  if (kStateOnly) {
+    mq = mk;
+  } else if (!make_map(&mq, q, bh, p.n, kDqk, CU_TENSOR_MAP_SWIZZLE_32B)) {
+    return LA_ERR_CUDA;
+  }
+  cudaError_t e = cudaFuncSetAttribute(chunked_tc_kernel<kStateOnly>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
+  if (e != cudaSuccess) return LA_ERR_CUDA;
+  dim3 grid((unsigned)n_launch, (unsigned)bh);
+  chunked_tc_kernel<kStateOnly><<<grid, kThreads, kSmemAlloc, s>>>(mq, mk, mv, p);
+  return check_launch();
+}
+
+}  // namespace
+
+int launch_chunked_state_tc(const void *k, const void *v, float *seg_states, int64_t bh,
+                            int64_t n, int segments, int n_launch, int64_t seg_len,
+                            const DeviceInfo &info, cudaStream_t s) {
+  (void)info;
+  Params p{};
+  p.seg_out = seg_states;
+  p.err = device_error_word();
+  p.n = n;
+  p.seg_len = seg_len;
+  p.segments = segments;
+  if (!p.err) return LA_ERR_CUDA;
+  return launch<true>(nullptr, k, v, p, bh, n_launch, s);
+}
+
+int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *out,
+                             const float *init_state, float *final_state,
+                             const float *seg_states, int64_t bh, int64_t n, float eps,
+                             bool normalize, int segments, int64_t seg_len,
+                             const DeviceInfo &info, cudaStream_t s) {
+  (void)info;
+  Params p{};
+  p.out = (__nv_bfloat16 *)out;
+  p.init_state = init_state;
+  p.final_state = final_state;
+  p.seg_states = seg_states;
+  p.err = device_error_word();
+  p.n = n;
+  p.seg_len = seg_len;
+  p.segments = segments;
+  p.eps = eps;
+  p.normalize = normalize ? 1 : 0;
+  if (!p.err) return LA_ERR_CUDA;
+  return launch<false>(q, k, v, p, bh, segments, s);
+}
+
+}  // namespace la

@@ -18,9 +18,7 @@ namespace tc {
 // barrier that will never flip); the kernel records an error and unwinds.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
 
-// Error word shared by every tensor-core kernel of this library.
-__device__ int g_device_error;
-
+// Value written to the library's device error word when a wait timed out.
 constexpr int kErrTimeout = 1;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -66,7 +64,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 
 // Waits for the phase with the given parity to complete.  Returns false if
 // the CTA is aborting (flag set by any thread) or the wait timed out, in
-// which case the flag is raised and the device error word is set.
+// which case the CTA's abort flag is raised.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
@@ -76,7 +74,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
       if (*abort_flag) return false;
       if (globaltimer() - t0 > kWaitTimeoutNs) {
         *abort_flag = 1;
-        atomicExch(&g_device_error, kErrTimeout);
         return false;
       }
     }
@@ -96,6 +93,13 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+// Warpgroup-uniform continuation check after a wait: every thread of the
+// group reaches the barrier, then all see the same abort flag, so no thread
+// is left waiting at a later barrier for peers that already gave up.
+__device__ __forceinline__ bool wg_ok(int id, volatile int *abort_flag) {
+  named_barrier_sync(id, 128);
+  return *abort_flag == 0;
 }
 
 // ---------------------------------------------------------------------- TMA ---

@@ -8,8 +8,14 @@
 
 namespace la {
 
-// True when this build contains the tensor-core kernels.
-bool tc_kernels_enabled();
+// Which tensor-core kernels this build contains.
+bool tc_chunked_enabled();
+bool tc_parallel_enabled();
+bool tc_sliding_enabled();
+
+// Device address of the library's error word on the current device (set by a
+// kernel whose bounded wait timed out); null if it cannot be resolved.
+int *device_error_word();
 
 int launch_parallel_tc(const void *q, const void *k, const void *v, void *out, int64_t bh,
                        int64_t n, float eps, const DeviceInfo &info, cudaStream_t s);

@@ -28,13 +28,14 @@ def _check_qkv(q, k, v, same_dv: bool = False):
     for name, t in (("q", q), ("k", k), ("v", v)):
         if not isinstance(t, torch.Tensor):
             raise TypeError(f"{name} must be a torch.Tensor")
-        if t.device.type != "cuda":
-            raise ValueError(f"{name} must be a CUDA tensor (got {t.device}); "
-                             "this library has no CPU implementation")
         if t.dim() != 4:
             raise ValueError(f"{name} must be (batch, heads, seq_len, dim), got shape {tuple(t.shape)}")
     if not (q.dtype == k.dtype == v.dtype):
         raise TypeError(f"q, k, v dtypes differ: {q.dtype}, {k.dtype}, {v.dtype}")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.device.type != "cuda":
+            raise ValueError(f"{name} must be a CUDA tensor (got {t.device}); "
+                             "this library has no CPU implementation")
     if not (q.device == k.device == v.device):
         raise ValueError("q, k, v are on different devices")
     if q.shape != k.shape:
