@@ -76,8 +76,23 @@ static_assert(kOffV % 1024 == 0 && kOffOnes % 1024 == 0 && kOffPhiK % 1024 == 0 
                   kOffSnap % 1024 == 0 && kSnapKBlock % 1024 == 0,
               "128B-swizzled regions need 1024-byte alignment");
 
-enum Bar { kFull0, kFull1, kEmpty0, kEmpty1, kPhiReady, kPhiFree, kScReady, kPReady, kOReady,
-           kOFree, kSReady, kSnapReady, kDone, kNumBars };
+enum Bar { kFull0, kFull1, kEmpty0, kEmpty1, kPhiQReady, kPhiKReady, kQSDone, kUpDone, kScReady,
+           kPReady, kOReady, kOFree, kSReady, kSnapReady, kDone, kNumBars };
+
+// Optional per-role timeline of CTA (0, 0), compiled in with -DLA_TRACE only.
+#ifdef LA_TRACE
+constexpr int kTraceChunks = 32, kTraceEvents = 8;
+__device__ long long la_trace_buf[4][kTraceChunks][kTraceEvents];
+#define LA_TRACE_AT(role, chunk, ev)                                                   \
+  do {                                                                                \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && (chunk) < kTraceChunks && (threadIdx.x & 31) == 0) \
+      la_trace_buf[role][chunk][ev] = clock64();                                      \
+  } while (0)
+#else
+#define LA_TRACE_AT(role, chunk, ev) \
+  do {                               \
+  } while (0)
+#endif
 
 // Feature f of the query/key-split basis ->
 //   kind 0: 1;  kind 1: x_a;  kind 2: x_a x_b (a < b);  kind 3: x_a^2;  kind 4: padding 0.
@@ -206,7 +221,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     mbar_init(&bars[kFull1], 1);
     mbar_init(&bars[kEmpty0], 2);
     mbar_init(&bars[kEmpty1], 2);
-    for (int i = kPhiReady; i < kNumBars; ++i) mbar_init(&bars[i], 1);
+    for (int i = kPhiQReady; i < kNumBars; ++i) mbar_init(&bars[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -248,6 +263,9 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     }
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
+    // Per tile c:  O = phi(Q) S_c;  S += [V 1 0]^T phi(K);  O += P V;  then the
+    // scores of tile c+1.  The update is issued before P V so the state
+    // snapshot of tile c+1 overlaps P V and the epilogue of tile c.
     if (lane == 0) {
       constexpr uint32_t id_sc = make_idesc_bf16(128, 128, false, false);
       constexpr uint32_t id_qs = make_idesc_bf16(128, kNO, false, false);
@@ -270,12 +288,13 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       }
       for (int c = 0; ok && c < n_chunks; ++c) {
         const int s = c & 1;
-        if (!mbar_wait(&bars[kPhiReady], c & 1, abort_flag)) break;
         const uint32_t v_base = sb + kOffV + s * kVBytes;
         if (!kStateOnly) {
+          if (!mbar_wait(&bars[kPhiQReady], c & 1, abort_flag)) break;
           if (c > 0 && !mbar_wait(&bars[kSnapReady], c & 1, abort_flag)) break;
           if (c > 0 && !mbar_wait(&bars[kOFree], (c - 1) & 1, abort_flag)) break;
           tc_fence_after();
+          LA_TRACE_AT(0, c, 0);
           // O = phi(Q) S_c   (K = 160 features in 10 steps of 16)
           const uint32_t snap = sb + kOffSnap + (c & 1) * kSnapBytes;
 #pragma unroll
@@ -284,18 +303,11 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
                                            kSwizzle128B);
             umma_ts(tmem + kColO, tmem + kColPhiQ + 8 * j, db, id_qs, j > 0 ? 1u : 0u);
           }
-          if (!mbar_wait(&bars[kPReady], c & 1, abort_flag)) break;
-          tc_fence_after();
-          // O[:, :64] += P V   (K = 128 tokens in 8 steps)
-#pragma unroll
-          for (int j = 0; j < kT / 16; ++j) {
-            const uint64_t db = make_sdesc(v_base + j * 2048, 8192, 1024, kSwizzle128B);
-            umma_ts(tmem + kColO, tmem + kColSc + 8 * j, db, id_pv, 1u);
-          }
-          umma_commit(&bars[kOReady]);
-        } else {
-          tc_fence_after();
+          umma_commit(&bars[kQSDone]);
         }
+        if (!mbar_wait(&bars[kPhiKReady], c & 1, abort_flag)) break;
+        tc_fence_after();
+        LA_TRACE_AT(0, c, 1);
         // S^T += [V 1 0]^T phi(K)   (K = 128 tokens in 8 steps)
 #pragma unroll
         for (int j = 0; j < kT / 16; ++j) {
@@ -305,12 +317,27 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           umma_ss(tmem + kColS, da, db, id_up, 1u);
         }
         umma_commit(&bars[kSReady]);
-        umma_commit(&bars[kPhiFree]);
+        umma_commit(&bars[kUpDone]);
+        if (kStateOnly) {
+          umma_commit(&bars[kEmpty0 + s]);
+          continue;
+        }
+        if (!mbar_wait(&bars[kPReady], c & 1, abort_flag)) break;
+        tc_fence_after();
+        LA_TRACE_AT(0, c, 2);
+        // O[:, :64] += P V   (K = 128 tokens in 8 steps)
+#pragma unroll
+        for (int j = 0; j < kT / 16; ++j) {
+          const uint64_t db = make_sdesc(v_base + j * 2048, 8192, 1024, kSwizzle128B);
+          umma_ts(tmem + kColO, tmem + kColSc + 8 * j, db, id_pv, 1u);
+        }
+        umma_commit(&bars[kOReady]);
         umma_commit(&bars[kEmpty0 + s]);
-        if (!kStateOnly && c + 1 < n_chunks) {
+        if (c + 1 < n_chunks) {
           if (!mbar_wait(&bars[kFull0 + ((c + 1) & 1)], ((c + 1) >> 1) & 1, abort_flag)) break;
           if (!mbar_wait(&bars[kOReady], c & 1, abort_flag)) break;  // P region free again
           tc_fence_after();
+          LA_TRACE_AT(0, c, 3);
           issue_scores((c + 1) & 1);
         }
       }
@@ -325,6 +352,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       const int s = c & 1;
       mbar_wait(&bars[kFull0 + s], (c >> 1) & 1, abort_flag);
       if (!wg_ok(1, abort_flag)) break;
+      LA_TRACE_AT(1, c, 0);
       const int valid = (int)min64(kT, t_end - (t_begin + (int64_t)c * kT));
       const bool vrow = row < valid;
       uint32_t kw[8], qw[8];
@@ -338,32 +366,38 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       }
       named_barrier_sync(1, 128);
       if (leader) mbar_arrive(&bars[kEmpty0 + s]);
-      if (c > 0) mbar_wait(&bars[kPhiFree], (c - 1) & 1, abort_flag);
-      if (!wg_ok(1, abort_flag)) break;
-      tc_fence_after();
-      float kx[kDqk];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        kx[2 * i] = vrow ? bf16lo(kw[i]) : 0.f;
-        kx[2 * i + 1] = vrow ? bf16hi(kw[i]) : 0.f;
-      }
-      // phi(K): 20 chunks of 8 features, 128B-swizzled, 64 features per block
-      store_phik(kx, vrow, sb + kOffPhiK, row, std::make_integer_sequence<int, kFPad / 8>{});
       if (!kStateOnly) {
+        // phi(Q) -> TMEM once phi(Q) S of the previous tile has read it
+        if (c > 0) mbar_wait(&bars[kQSDone], (c - 1) & 1, abort_flag);
+        if (!wg_ok(1, abort_flag)) break;
+        tc_fence_after();
         float qx[kDqk];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           qx[2 * i] = bf16lo(qw[i]);
           qx[2 * i + 1] = bf16hi(qw[i]);
         }
-        // phi(Q): 80 bf16 pairs into TMEM lane `row`
         store_phiq(qx, taddr(tmem, wq * 32, kColPhiQ), std::make_integer_sequence<int, kFPad / 32>{});
         tmem_wait_st();
+        tc_fence_before();
+        named_barrier_sync(1, 128);
+        if (leader) mbar_arrive(&bars[kPhiQReady]);
+        LA_TRACE_AT(1, c, 1);
       }
+      // phi(K) -> smem once the previous update has read it
+      if (c > 0) mbar_wait(&bars[kUpDone], (c - 1) & 1, abort_flag);
+      if (!wg_ok(1, abort_flag)) break;
+      float kx[kDqk];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        kx[2 * i] = vrow ? bf16lo(kw[i]) : 0.f;
+        kx[2 * i + 1] = vrow ? bf16hi(kw[i]) : 0.f;
+      }
+      store_phik(kx, vrow, sb + kOffPhiK, row, std::make_integer_sequence<int, kFPad / 8>{});
       fence_proxy_async_smem();
-      tc_fence_before();
       named_barrier_sync(1, 128);
-      if (leader) mbar_arrive(&bars[kPhiReady]);
+      if (leader) mbar_arrive(&bars[kPhiKReady]);
+      LA_TRACE_AT(1, c, 2);
     }
   } else if (warp < kWarpState) {
     // ------------------------------------------------------------ polynomial + epilogue
@@ -377,67 +411,68 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         mbar_wait(&bars[kScReady], c & 1, abort_flag);
         if (!wg_ok(2, abort_flag)) break;
         tc_fence_after();
+        LA_TRACE_AT(2, c, 0);
         float rs = 0.f;
 #pragma unroll
-        for (int G = 0; G < kT / 32; ++G) {
-          uint32_t r0[16], r1[16], w[16];
-          tmem_ld16(taddr(tmem, wq * 32, kColSc + 32 * G), r0);
-          tmem_ld16(taddr(tmem, wq * 32, kColSc + 32 * G + 16), r1);
+        for (int H = 0; H < 2; ++H) {  // two halves of 64 keys
+          uint32_t r[64];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            tmem_ld16(taddr(tmem, wq * 32, kColSc + 64 * H + 16 * q4), r + 16 * q4);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int j0 = 32 * G + 2 * i;
-            const uint32_t x0 = i < 8 ? r0[2 * i] : r1[2 * i - 16];
-            const uint32_t x1 = i < 8 ? r0[2 * i + 1] : r1[2 * i - 15];
-            const float s0 = 0.25f * __uint_as_float(x0);
-            const float s1 = 0.25f * __uint_as_float(x1);
-            float p0 = fmaf(s0, fmaf(0.5f, s0, 1.f), 1.f);
-            float p1 = fmaf(s1, fmaf(0.5f, s1, 1.f), 1.f);
-            p0 = (j0 <= row && j0 < valid) ? p0 : 0.f;
-            p1 = (j0 + 1 <= row && j0 + 1 < valid) ? p1 : 0.f;
-            rs += p0 + p1;
-            w[i] = pack_bf16(p0, p1);
+          for (int G = 0; G < 2; ++G) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int jl = 32 * G + 2 * i;  // key within the half
+              const int j0 = 64 * H + jl;
+              const float s0 = 0.25f * __uint_as_float(r[jl]);
+              const float s1 = 0.25f * __uint_as_float(r[jl + 1]);
+              float p0 = fmaf(s0, fmaf(0.5f, s0, 1.f), 1.f);
+              float p1 = fmaf(s1, fmaf(0.5f, s1, 1.f), 1.f);
+              p0 = (j0 <= row && j0 < valid) ? p0 : 0.f;
+              p1 = (j0 + 1 <= row && j0 + 1 < valid) ? p1 : 0.f;
+              rs += p0 + p1;
+              w[i] = pack_bf16(p0, p1);
+            }
+            // P columns [32H + 16G, +16) hold keys [64H + 32G, +32); those
+            // score columns were all read above
+            tmem_st16(taddr(tmem, wq * 32, kColSc + 32 * H + 16 * G), w);
           }
-          // P columns [16G, 16G + 16) hold keys [32G, 32G + 32); those
-          // score columns were all read above
-          tmem_st16(taddr(tmem, wq * 32, kColSc + 16 * G), w);
         }
         tmem_wait_st();
         tc_fence_before();
         named_barrier_sync(2, 128);
         if (leader) mbar_arrive(&bars[kPReady]);
+        LA_TRACE_AT(2, c, 1);
 
         mbar_wait(&bars[kOReady], c & 1, abort_flag);
         if (!wg_ok(2, abort_flag)) break;
         tc_fence_after();
-        uint32_t dr[16];
-        tmem_ld16(taddr(tmem, wq * 32, kColO + 64), dr);
-        tmem_wait_ld();
-        const float den = __uint_as_float(dr[0]) + rs + p.eps;
-        const float inv = p.normalize ? 1.f / den : 1.f;
-        __nv_bfloat16 *orow = p.out + ((uint64_t)bh * p.n + t0 + row) * kDv;
+        LA_TRACE_AT(2, c, 2);
+        uint32_t o[kNO];
 #pragma unroll
-        for (int G = 0; G < kDv / 16; ++G) {
-          uint32_t r[16];
-          tmem_ld16(taddr(tmem, wq * 32, kColO + 16 * G), r);
-          tmem_wait_ld();
-          if (row < valid) {
-            uint4 lo, hi;
-            lo.x = pack_bf16(__uint_as_float(r[0]) * inv, __uint_as_float(r[1]) * inv);
-            lo.y = pack_bf16(__uint_as_float(r[2]) * inv, __uint_as_float(r[3]) * inv);
-            lo.z = pack_bf16(__uint_as_float(r[4]) * inv, __uint_as_float(r[5]) * inv);
-            lo.w = pack_bf16(__uint_as_float(r[6]) * inv, __uint_as_float(r[7]) * inv);
-            hi.x = pack_bf16(__uint_as_float(r[8]) * inv, __uint_as_float(r[9]) * inv);
-            hi.y = pack_bf16(__uint_as_float(r[10]) * inv, __uint_as_float(r[11]) * inv);
-            hi.z = pack_bf16(__uint_as_float(r[12]) * inv, __uint_as_float(r[13]) * inv);
-            hi.w = pack_bf16(__uint_as_float(r[14]) * inv, __uint_as_float(r[15]) * inv);
-            *(uint4 *)(orow + 16 * G) = lo;
-            *(uint4 *)(orow + 16 * G + 8) = hi;
-          }
-        }
+        for (int G = 0; G < kNO / 16; ++G) tmem_ld16(taddr(tmem, wq * 32, kColO + 16 * G), o + 16 * G);
+        tmem_wait_ld();
         tc_fence_before();
         named_barrier_sync(2, 128);
-        if (leader) mbar_arrive(&bars[kOFree]);
+        if (leader) mbar_arrive(&bars[kOFree]);  // O is in registers: TMEM O reusable
+        const float den = __uint_as_float(o[kDv]) + rs + p.eps;
+        const float inv = p.normalize ? 1.f / den : 1.f;
+        if (row < valid) {
+          __nv_bfloat16 *orow = p.out + ((uint64_t)bh * p.n + t0 + row) * kDv;
+#pragma unroll
+          for (int G = 0; G < kDv / 8; ++G) {
+            uint4 w;
+            w.x = pack_bf16(__uint_as_float(o[8 * G + 0]) * inv, __uint_as_float(o[8 * G + 1]) * inv);
+            w.y = pack_bf16(__uint_as_float(o[8 * G + 2]) * inv, __uint_as_float(o[8 * G + 3]) * inv);
+            w.z = pack_bf16(__uint_as_float(o[8 * G + 4]) * inv, __uint_as_float(o[8 * G + 5]) * inv);
+            w.w = pack_bf16(__uint_as_float(o[8 * G + 6]) * inv, __uint_as_float(o[8 * G + 7]) * inv);
+            *(uint4 *)(orow + 8 * G) = w;
+          }
+        }
+        LA_TRACE_AT(2, c, 3);
       }
     }
   } else {
@@ -506,32 +541,37 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         mbar_wait(&bars[kSReady], c & 1, abort_flag);
         if (!wg_ok(3, abort_flag)) break;
         tc_fence_after();
+        LA_TRACE_AT(3, c, 0);
         const bool last = c == n_chunks - 1;
         const uint32_t snap = sb + kOffSnap + ((c + 1) & 1) * kSnapBytes;
-        for (int grp = 0; grp < kFPad / 16; ++grp) {
-          uint32_t r[16];
-          tmem_ld16(taddr(tmem, wq * 32, kColS + 16 * grp), r);
-          tmem_wait_ld();
-          if (e < kNO) {
-            const int f0 = 16 * grp;
-            const uint32_t blk = snap + (f0 >> 6) * kSnapKBlock;
-            st_shared_v4(blk + sw128_offset(e, (f0 & 63) >> 3),
-                         pack_bf16(__uint_as_float(r[0]), __uint_as_float(r[1])),
-                         pack_bf16(__uint_as_float(r[2]), __uint_as_float(r[3])),
-                         pack_bf16(__uint_as_float(r[4]), __uint_as_float(r[5])),
-                         pack_bf16(__uint_as_float(r[6]), __uint_as_float(r[7])));
-            st_shared_v4(blk + sw128_offset(e, ((f0 & 63) >> 3) + 1),
-                         pack_bf16(__uint_as_float(r[8]), __uint_as_float(r[9])),
-                         pack_bf16(__uint_as_float(r[10]), __uint_as_float(r[11])),
-                         pack_bf16(__uint_as_float(r[12]), __uint_as_float(r[13])),
-                         pack_bf16(__uint_as_float(r[14]), __uint_as_float(r[15])));
-          }
-          if (last && write_final && real) {
-            float *dst = p.final_state + (uint64_t)bh * kF * kSV;
+        // rows >= 80 are not part of the snapshot; their warp only joins the barriers
+        if (wq < 3) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int f = 16 * grp + i;
-              if (f < kF) dst[(uint64_t)f * kSV + e] = __uint_as_float(r[i]);
+          for (int B = 0; B < kFPad / 64 + 1; ++B) {  // 64 + 64 + 32 columns
+            const int cols = B < 2 ? 64 : 32;
+            uint32_t r[64];
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+              if (16 * q4 < cols) tmem_ld16(taddr(tmem, wq * 32, kColS + 64 * B + 16 * q4), r + 16 * q4);
+            tmem_wait_ld();
+            if (e < kNO) {
+              const uint32_t blk = snap + B * kSnapKBlock;
+#pragma unroll
+              for (int ch = 0; ch < 8; ++ch)
+                if (ch < cols / 8)
+                  st_shared_v4(blk + sw128_offset(e, ch),
+                             pack_bf16(__uint_as_float(r[8 * ch + 0]), __uint_as_float(r[8 * ch + 1])),
+                             pack_bf16(__uint_as_float(r[8 * ch + 2]), __uint_as_float(r[8 * ch + 3])),
+                             pack_bf16(__uint_as_float(r[8 * ch + 4]), __uint_as_float(r[8 * ch + 5])),
+                             pack_bf16(__uint_as_float(r[8 * ch + 6]), __uint_as_float(r[8 * ch + 7])));
+            }
+            if (last && write_final && real) {
+              float *dst = p.final_state + (uint64_t)bh * kF * kSV;
+#pragma unroll
+              for (int i = 0; i < 64; ++i) {
+                const int f = 64 * B + i;
+                if (i < cols && f < kF) dst[(uint64_t)f * kSV + e] = __uint_as_float(r[i]);
+              }
             }
           }
         }
@@ -539,6 +579,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         tc_fence_before();
         named_barrier_sync(3, 128);
         if (leader) mbar_arrive(&bars[kSnapReady]);
+        LA_TRACE_AT(3, c, 1);
       }
     }
   }
@@ -612,6 +653,14 @@ int launch(const void *q, const void *k, const void *v, const Params &p, int64_t
 }
 
 }  // namespace
+
+#ifdef LA_TRACE
+extern "C" int la_debug_read_trace(long long *dst, int count) {
+  const int n = 4 * kTraceChunks * kTraceEvents;
+  if (count < n) return -1;
+  return cudaMemcpyFromSymbol(dst, la_trace_buf, sizeof(long long) * n) == cudaSuccess ? n : -1;
+}
+#endif
 
 int launch_chunked_state_tc(const void *k, const void *v, float *seg_states, int64_t bh,
                             int64_t n, int segments, int n_launch, int64_t seg_len,

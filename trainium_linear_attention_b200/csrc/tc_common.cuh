@@ -134,7 +134,7 @@ __device__ __forceinline__ uint32_t taddr(uint32_t base, uint32_t lane, uint32_t
 }
 
 // 32 lanes x 32 bits, 16 consecutive columns per thread.
-__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&r)[16]) {
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t *r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32"
       " {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -143,7 +143,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&r)[16]) {
         "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(addr));
 }
-__device__ __forceinline__ void tmem_st16(uint32_t addr, const uint32_t (&r)[16]) {
+__device__ __forceinline__ void tmem_st16(uint32_t addr, const uint32_t *r) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32"
       " [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(addr),
