@@ -127,53 +127,84 @@ static_assert(feat_kind(17) == 3 && feat_a(18) == 0 && feat_b(18) == 1 && feat_k
                   feat_a(152) == 15 && feat_b(151) == 15 && feat_a(151) == 14 && feat_kind(153) == 4,
               "feature order: const, 16 linear, (a, b) a <= b row-major");
 
-// Key side: [1, k_a, k_a k_b]; the scale factors all live on the query side.
-template <int F>
-__device__ __forceinline__ float phi_k(const float (&x)[kDqk], bool valid) {
-  constexpr int kind = feat_kind(F), a = feat_a(F), b = feat_b(F);
-  if constexpr (kind == 0) return valid ? 1.f : 0.f;
-  else if constexpr (kind == 1) return x[a];
-  else if constexpr (kind == 4) return 0.f;
-  else return x[a] * x[b];
+// Features are produced two at a time as one bf16x2 product A * B, A and B
+// assembled (byte permutes) from the token's 16 inputs and their exact
+// power-of-two rescalings.  A bf16 product of bf16 operands rounds the exact
+// product once, so every feature equals the fp32 product rounded to bf16.
+//   key side   phi_k = [1, k_a, k_a k_b]                    (unscaled)
+//   query side phi_q = [1, q_a / 4, q_a q_b / 16 (a < b), q_a^2 / 32]   (d = 16)
+enum : int { kSrcRaw = 0, kSrcS4, kSrcS16, kSrcS32, kSrcOne, kSrcOneValid, kSrcZero };
+struct Op {
+  int src;
+  int idx;
+};
+template <bool kQ>
+__host__ __device__ constexpr Op op_a(int f) {
+  const int kind = feat_kind(f), a = feat_a(f);
+  return kind == 0   ? Op{kSrcOneValid, 0}
+         : kind == 1 ? Op{kQ ? kSrcS4 : kSrcRaw, a}
+         : kind == 2 ? Op{kQ ? kSrcS16 : kSrcRaw, a}
+         : kind == 3 ? Op{kQ ? kSrcS32 : kSrcRaw, a}
+                     : Op{kSrcZero, 0};
 }
-// Query side: [1, q_a / 4, q_a q_b / 16 (a < b), q_a^2 / 32]  (d = 16)
-template <int F>
-__device__ __forceinline__ float phi_q(const float (&x)[kDqk]) {
-  constexpr int kind = feat_kind(F), a = feat_a(F), b = feat_b(F);
-  if constexpr (kind == 0) return 1.f;
-  else if constexpr (kind == 1) return x[a] * 0.25f;
-  else if constexpr (kind == 2) return x[a] * x[b] * 0.0625f;
-  else if constexpr (kind == 3) return x[a] * x[a] * 0.03125f;
-  else return 0.f;
+__host__ __device__ constexpr Op op_b(int f) {
+  const int kind = feat_kind(f), b = feat_b(f);
+  return kind <= 1 ? Op{kSrcOne, 0} : kind <= 3 ? Op{kSrcRaw, b} : Op{kSrcZero, 0};
+}
+
+struct FeatSrc {
+  uint32_t raw[8], s4[8], s16[8], s32[8];  // bf16x2 words: values 2i (lo), 2i+1 (hi)
+  uint32_t one_valid;                      // bf16x2 {1, 1}, or {0, 0} for a padding token
+};
+template <int kSrc, int kIdx>
+__device__ __forceinline__ uint32_t src_word(const FeatSrc &s) {
+  if constexpr (kSrc == kSrcRaw) return s.raw[kIdx >> 1];
+  else if constexpr (kSrc == kSrcS4) return s.s4[kIdx >> 1];
+  else if constexpr (kSrc == kSrcS16) return s.s16[kIdx >> 1];
+  else if constexpr (kSrc == kSrcS32) return s.s32[kIdx >> 1];
+  else if constexpr (kSrc == kSrcOne) return 0x3F803F80u;
+  else if constexpr (kSrc == kSrcOneValid) return s.one_valid;
+  else return 0u;
+}
+template <int kSrc, int kIdx>
+__host__ __device__ constexpr int src_half() {
+  return kSrc <= kSrcS32 ? (kIdx & 1) : 0;
+}
+template <bool kQ, int F0>
+__device__ __forceinline__ uint32_t feat_pair(const FeatSrc &s) {
+  constexpr Op a0 = op_a<kQ>(F0), a1 = op_a<kQ>(F0 + 1);
+  constexpr Op b0 = op_b(F0), b1 = op_b(F0 + 1);
+  const uint32_t A = bf16_pair<src_half<a0.src, a0.idx>(), src_half<a1.src, a1.idx>()>(
+      src_word<a0.src, a0.idx>(s), src_word<a1.src, a1.idx>(s));
+  const uint32_t B = bf16_pair<src_half<b0.src, b0.idx>(), src_half<b1.src, b1.idx>()>(
+      src_word<b0.src, b0.idx>(s), src_word<b1.src, b1.idx>(s));
+  return hmul2_bf16(A, B);
 }
 
 // phi(K) chunk J (features 8J .. 8J+7) of token `row` -> 128B-swizzled smem
 template <int J>
-__device__ __forceinline__ void store_phik_chunk(const float (&x)[kDqk], bool valid, uint32_t base,
-                                                 int row) {
+__device__ __forceinline__ void store_phik_chunk(const FeatSrc &s, uint32_t base, int row) {
   st_shared_v4(base + (J >> 3) * (kT * 128) + sw128_offset(row, J & 7),
-               pack_bf16(phi_k<8 * J + 0>(x, valid), phi_k<8 * J + 1>(x, valid)),
-               pack_bf16(phi_k<8 * J + 2>(x, valid), phi_k<8 * J + 3>(x, valid)),
-               pack_bf16(phi_k<8 * J + 4>(x, valid), phi_k<8 * J + 5>(x, valid)),
-               pack_bf16(phi_k<8 * J + 6>(x, valid), phi_k<8 * J + 7>(x, valid)));
+               feat_pair<false, 8 * J + 0>(s), feat_pair<false, 8 * J + 2>(s),
+               feat_pair<false, 8 * J + 4>(s), feat_pair<false, 8 * J + 6>(s));
 }
 template <int... J>
-__device__ __forceinline__ void store_phik(const float (&x)[kDqk], bool valid, uint32_t base,
-                                           int row, std::integer_sequence<int, J...>) {
-  (store_phik_chunk<J>(x, valid, base, row), ...);
+__device__ __forceinline__ void store_phik(const FeatSrc &s, uint32_t base, int row,
+                                           std::integer_sequence<int, J...>) {
+  (store_phik_chunk<J>(s, base, row), ...);
 }
 
 // phi(Q) columns [16G, 16G+16) (features 32G .. 32G+31) of TMEM lane `row`
 template <int G, int... I>
-__device__ __forceinline__ void store_phiq_group(const float (&x)[kDqk], uint32_t addr,
+__device__ __forceinline__ void store_phiq_group(const FeatSrc &s, uint32_t addr,
                                                  std::integer_sequence<int, I...>) {
-  const uint32_t w[16] = {pack_bf16(phi_q<32 * G + 2 * I>(x), phi_q<32 * G + 2 * I + 1>(x))...};
+  const uint32_t w[16] = {feat_pair<true, 32 * G + 2 * I>(s)...};
   tmem_st16(addr, w);
 }
 template <int... G>
-__device__ __forceinline__ void store_phiq(const float (&x)[kDqk], uint32_t addr0,
+__device__ __forceinline__ void store_phiq(const FeatSrc &s, uint32_t addr0,
                                            std::integer_sequence<int, G...>) {
-  (store_phiq_group<G>(x, addr0 + 16 * G, std::make_integer_sequence<int, 16>{}), ...);
+  (store_phiq_group<G>(s, addr0 + 16 * G, std::make_integer_sequence<int, 16>{}), ...);
 }
 
 struct Params {
@@ -272,6 +303,9 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       constexpr uint32_t id_pv = make_idesc_bf16(128, kDv, false, true);
       constexpr uint32_t id_up = make_idesc_bf16(128, kFPad, true, true);
       const uint32_t a_ones = sb + kOffOnes;
+      const uint64_t qs_desc0 = make_sdesc(sb + kOffSnap, 16, 1024, kSwizzle128B);
+      const uint64_t qs_desc1 = make_sdesc(sb + kOffSnap + kSnapBytes, 16, 1024, kSwizzle128B);
+      const uint64_t up_b_desc = make_sdesc(sb + kOffPhiK, kPhiKBlock, 1024, kSwizzle128B);
       bool ok = mbar_wait(&bars[kSnapReady], 0, abort_flag);  // S_0 in TMEM (+ snapshot 0)
       auto issue_scores = [&](int s) {
         const uint64_t da = make_sdesc(sb + kOffQ + s * kQBytes, 16, 256, kSwizzle32B);
@@ -296,11 +330,10 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           tc_fence_after();
           LA_TRACE_AT(0, c, 0);
           // O = phi(Q) S_c   (K = 160 features in 10 steps of 16)
-          const uint32_t snap = sb + kOffSnap + (c & 1) * kSnapBytes;
+          const uint64_t snap_desc = (c & 1) ? qs_desc1 : qs_desc0;
 #pragma unroll
           for (int j = 0; j < kFPad / 16; ++j) {
-            const uint64_t db = make_sdesc(snap + (j >> 2) * kSnapKBlock + (j & 3) * 32, 16, 1024,
-                                           kSwizzle128B);
+            const uint64_t db = snap_desc + (((j >> 2) * kSnapKBlock + (j & 3) * 32) >> 4);
             umma_ts(tmem + kColO, tmem + kColPhiQ + 8 * j, db, id_qs, j > 0 ? 1u : 0u);
           }
           umma_commit(&bars[kQSDone]);
@@ -313,8 +346,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         for (int j = 0; j < kT / 16; ++j) {
           const uint32_t a_addr = v_base + j * 2048;
           const uint64_t da = make_sdesc(a_addr, a_ones - a_addr, 1024, kSwizzle128B);
-          const uint64_t db = make_sdesc(sb + kOffPhiK + j * 2048, kPhiKBlock, 1024, kSwizzle128B);
-          umma_ss(tmem + kColS, da, db, id_up, 1u);
+          umma_ss(tmem + kColS, da, up_b_desc + (uint64_t)((j * 2048) >> 4), id_up, 1u);
         }
         umma_commit(&bars[kSReady]);
         umma_commit(&bars[kUpDone]);
@@ -326,11 +358,10 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         tc_fence_after();
         LA_TRACE_AT(0, c, 2);
         // O[:, :64] += P V   (K = 128 tokens in 8 steps)
+        const uint64_t pv_desc = make_sdesc(v_base, 8192, 1024, kSwizzle128B);
 #pragma unroll
-        for (int j = 0; j < kT / 16; ++j) {
-          const uint64_t db = make_sdesc(v_base + j * 2048, 8192, 1024, kSwizzle128B);
-          umma_ts(tmem + kColO, tmem + kColSc + 8 * j, db, id_pv, 1u);
-        }
+        for (int j = 0; j < kT / 16; ++j)
+          umma_ts(tmem + kColO, tmem + kColSc + 8 * j, pv_desc + (uint64_t)((j * 2048) >> 4), id_pv, 1u);
         umma_commit(&bars[kOReady]);
         umma_commit(&bars[kEmpty0 + s]);
         if (c + 1 < n_chunks) {
@@ -371,13 +402,16 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         if (c > 0) mbar_wait(&bars[kQSDone], (c - 1) & 1, abort_flag);
         if (!wg_ok(1, abort_flag)) break;
         tc_fence_after();
-        float qx[kDqk];
+        FeatSrc fs;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          qx[2 * i] = bf16lo(qw[i]);
-          qx[2 * i + 1] = bf16hi(qw[i]);
+          fs.raw[i] = qw[i];
+          fs.s4[i] = hmul2_bf16(qw[i], 0x3E803E80u);   // x / 4   (exact)
+          fs.s16[i] = hmul2_bf16(qw[i], 0x3D803D80u);  // x / 16  (exact)
+          fs.s32[i] = hmul2_bf16(qw[i], 0x3D003D00u);  // x / 32  (exact)
         }
-        store_phiq(qx, taddr(tmem, wq * 32, kColPhiQ), std::make_integer_sequence<int, kFPad / 32>{});
+        fs.one_valid = 0x3F803F80u;
+        store_phiq(fs, taddr(tmem, wq * 32, kColPhiQ), std::make_integer_sequence<int, kFPad / 32>{});
         tmem_wait_st();
         tc_fence_before();
         named_barrier_sync(1, 128);
@@ -387,13 +421,11 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       // phi(K) -> smem once the previous update has read it
       if (c > 0) mbar_wait(&bars[kUpDone], (c - 1) & 1, abort_flag);
       if (!wg_ok(1, abort_flag)) break;
-      float kx[kDqk];
+      FeatSrc fk;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        kx[2 * i] = vrow ? bf16lo(kw[i]) : 0.f;
-        kx[2 * i + 1] = vrow ? bf16hi(kw[i]) : 0.f;
-      }
-      store_phik(kx, vrow, sb + kOffPhiK, row, std::make_integer_sequence<int, kFPad / 8>{});
+      for (int i = 0; i < 8; ++i) fk.raw[i] = vrow ? kw[i] : 0u;
+      fk.one_valid = vrow ? 0x3F803F80u : 0u;  // padding tokens add nothing to the state
+      store_phik(fk, sb + kOffPhiK, row, std::make_integer_sequence<int, kFPad / 8>{});
       fence_proxy_async_smem();
       named_barrier_sync(1, 128);
       if (leader) mbar_arrive(&bars[kPhiKReady]);
@@ -412,35 +444,65 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         if (!wg_ok(2, abort_flag)) break;
         tc_fence_after();
         LA_TRACE_AT(2, c, 0);
-        float rs = 0.f;
+        // P = tril(1 + s/4 + s^2/32) for raw scores s = q.k (d = 16).  Key group
+        // G (32 keys) is entirely below the diagonal for this warp's rows when
+        // G < wq, holds the diagonal when G == wq and is all zero when G > wq.
+        const uint64_t c32 = f2pack(0.03125f, 0.03125f), c4 = f2pack(0.25f, 0.25f);
+        const uint64_t one2 = f2pack(1.f, 1.f);
+        const bool full_tile = valid == kT;
+        uint64_t rs2 = f2pack(0.f, 0.f);
 #pragma unroll
         for (int H = 0; H < 2; ++H) {  // two halves of 64 keys
-          uint32_t r[64];
+          uint32_t w[2][16];
+          if (2 * H <= wq) {
+            uint32_t r[64];
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4)
-            tmem_ld16(taddr(tmem, wq * 32, kColSc + 64 * H + 16 * q4), r + 16 * q4);
-          tmem_wait_ld();
+            for (int q4 = 0; q4 < 4; ++q4)
+              tmem_ld16(taddr(tmem, wq * 32, kColSc + 64 * H + 16 * q4), r + 16 * q4);
+            tmem_wait_ld();
 #pragma unroll
-          for (int G = 0; G < 2; ++G) {
-            uint32_t w[16];
+            for (int G2 = 0; G2 < 2; ++G2) {
+              const int G = 2 * H + G2;
+              if (G > wq) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int jl = 32 * G + 2 * i;  // key within the half
-              const int j0 = 64 * H + jl;
-              const float s0 = 0.25f * __uint_as_float(r[jl]);
-              const float s1 = 0.25f * __uint_as_float(r[jl + 1]);
-              float p0 = fmaf(s0, fmaf(0.5f, s0, 1.f), 1.f);
-              float p1 = fmaf(s1, fmaf(0.5f, s1, 1.f), 1.f);
-              p0 = (j0 <= row && j0 < valid) ? p0 : 0.f;
-              p1 = (j0 + 1 <= row && j0 + 1 < valid) ? p1 : 0.f;
-              rs += p0 + p1;
-              w[i] = pack_bf16(p0, p1);
+                for (int i = 0; i < 16; ++i) w[G2][i] = 0u;
+              } else if (G < wq && full_tile) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const uint64_t s2 = f2pack(__uint_as_float(r[32 * G2 + 2 * i]),
+                                             __uint_as_float(r[32 * G2 + 2 * i + 1]));
+                  const uint64_t p2 = ffma2(s2, ffma2(s2, c32, c4), one2);
+                  rs2 = fadd2(rs2, p2);
+                  w[G2][i] = pack_bf16x2(p2);
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const int j0 = 32 * G + 2 * i;
+                  const uint64_t s2 = f2pack(__uint_as_float(r[32 * G2 + 2 * i]),
+                                             __uint_as_float(r[32 * G2 + 2 * i + 1]));
+                  float p0, p1;
+                  f2unpack(ffma2(s2, ffma2(s2, c32, c4), one2), p0, p1);
+                  p0 = (j0 <= row && j0 < valid) ? p0 : 0.f;
+                  p1 = (j0 + 1 <= row && j0 + 1 < valid) ? p1 : 0.f;
+                  const uint64_t p2 = f2pack(p0, p1);
+                  rs2 = fadd2(rs2, p2);
+                  w[G2][i] = pack_bf16x2(p2);
+                }
+              }
             }
-            // P columns [32H + 16G, +16) hold keys [64H + 32G, +32); those
-            // score columns were all read above
-            tmem_st16(taddr(tmem, wq * 32, kColSc + 32 * H + 16 * G), w);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) w[0][i] = w[1][i] = 0u;
           }
+          // P columns [32H, 32H + 32) hold keys [64H, 64H + 64); those score
+          // columns were all read above
+          tmem_st16(taddr(tmem, wq * 32, kColSc + 32 * H), w[0]);
+          tmem_st16(taddr(tmem, wq * 32, kColSc + 32 * H + 16), w[1]);
         }
+        float rs_lo, rs_hi;
+        f2unpack(rs2, rs_lo, rs_hi);
+        const float rs = rs_lo + rs_hi;
         tmem_wait_st();
         tc_fence_before();
         named_barrier_sync(2, 128);
@@ -460,16 +522,17 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         if (leader) mbar_arrive(&bars[kOFree]);  // O is in registers: TMEM O reusable
         const float den = __uint_as_float(o[kDv]) + rs + p.eps;
         const float inv = p.normalize ? 1.f / den : 1.f;
+        const uint64_t inv2 = f2pack(inv, inv);
         if (row < valid) {
           __nv_bfloat16 *orow = p.out + ((uint64_t)bh * p.n + t0 + row) * kDv;
 #pragma unroll
           for (int G = 0; G < kDv / 8; ++G) {
-            uint4 w;
-            w.x = pack_bf16(__uint_as_float(o[8 * G + 0]) * inv, __uint_as_float(o[8 * G + 1]) * inv);
-            w.y = pack_bf16(__uint_as_float(o[8 * G + 2]) * inv, __uint_as_float(o[8 * G + 3]) * inv);
-            w.z = pack_bf16(__uint_as_float(o[8 * G + 4]) * inv, __uint_as_float(o[8 * G + 5]) * inv);
-            w.w = pack_bf16(__uint_as_float(o[8 * G + 6]) * inv, __uint_as_float(o[8 * G + 7]) * inv);
-            *(uint4 *)(orow + 8 * G) = w;
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              w[i] = pack_bf16x2(fmul2(f2pack(__uint_as_float(o[8 * G + 2 * i]),
+                                              __uint_as_float(o[8 * G + 2 * i + 1])), inv2));
+            *(uint4 *)(orow + 8 * G) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
         LA_TRACE_AT(2, c, 3);

@@ -218,11 +218,56 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
       : "memory");
 }
 
+// ------------------------------------------------------- packed fp32 math ---
+// sm_100 executes two fp32 lanes per instruction (f32x2); operands are 64-bit
+// register pairs {lo, hi}.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // ---------------------------------------------------------------- packing ---
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(lo), "f"(hi));
   return r;
+}
+// {lo, hi} fp32 pair -> bf16x2 (round to nearest even)
+__device__ __forceinline__ uint32_t pack_bf16x2(uint64_t v) {
+  float lo, hi;
+  f2unpack(v, lo, hi);
+  return pack_bf16(lo, hi);
+}
+// bf16x2 product, rounded once (== the fp32 product of the bf16 operands, RN)
+__device__ __forceinline__ uint32_t hmul2_bf16(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// {half i of word a, half j of word b} as a bf16x2 word (i, j in {0 = lo, 1 = hi})
+template <int I, int J>
+__device__ __forceinline__ uint32_t bf16_pair(uint32_t a, uint32_t b) {
+  constexpr uint32_t sel = (I ? 0x0032u : 0x0010u) | (J ? 0x7600u : 0x5400u);
+  return __byte_perm(a, b, sel);
 }
 __device__ __forceinline__ float bf16lo(uint32_t x) { return __uint_as_float(x << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t x) { return __uint_as_float(x & 0xFFFF0000u); }
