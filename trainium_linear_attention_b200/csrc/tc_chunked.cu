@@ -5,26 +5,34 @@
 // the tile's rows, S_c the fp32 state of all earlier tokens, phi the Taylor
 // feature map in the query/key-split basis of include/la_attention.h):
 //
-//   scores = Q K^T                      tcgen05 M=128 N=128 K=16 -> TMEM
-//   P      = tril(1 + s + s^2/2)        s = scores/4, CUDA cores, P -> TMEM (bf16)
-//   O      = phi(Q) S_c                 tcgen05 M=128 N=80  K=160, A = phi(Q) in TMEM
-//   O     += P V                        tcgen05 M=128 N=64  K=128, A = P in TMEM
-//   S^T   += [V 1 0]^T phi(K)           tcgen05 M=128 N=160 K=128 (state in TMEM)
-//   out    = O[:, :64] / (O[:, 64] + rowsum(P) + eps)
+//   scores = Q K^T                  tcgen05 M=128 N=128 K=16   -> TMEM (2 buffers)
+//   P      = tril(1 + s/4 + s^2/32) CUDA cores, bf16 P written over its scores
+//   O      = phi(Q) S_c             tcgen05 M=128 N=80  K=160  (S_c: bf16 snapshot)
+//   S^T   += [V 1 0]^T phi(K)       tcgen05 M=128 N=160 K=128  (fp32 state in TMEM)
+//   O     += P [V 1]                tcgen05 M=128 N=80  K=128  (A = P in TMEM)
+//   out    = O[:, :64] / (O[:, 64] + eps)
 //
 // which is the reference recurrence of kernels/nki_attention_chunked.py:71-109
 // (acc_o = Q_phi S; scores = Q_phi K_phi^T; S += K_phi^T V; acc_o +=
 // tril(scores) V) with the intra-tile term evaluated in the equivalent
-// polynomial form 1 + s + s^2/2 and the normaliser carried as state row 64.
-// The 153 features never touch HBM: phi(Q) is written straight to TMEM and
-// phi(K) to shared memory by the thread that owns the token.
+// polynomial form 1 + s + s^2/2 and the normaliser carried both as state row
+// 64 (z = sum phi(k)) and as the ones column of [V 1] (the row sum of P).
+// The 153 features never touch HBM: each token's phi(Q) and phi(K) are
+// expanded in registers and written to shared memory by the thread that owns
+// the token.
 //
-// Warp roles (448 threads):
+// Warp roles (576 threads, one CTA per SM):
 //   warp 0      TMA producer (Q, K, V tiles; 2-stage ring)
 //   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2-5   feature warpgroup: phi(Q) -> TMEM, phi(K) -> smem
-//   warps 6-9   polynomial + epilogue warpgroup
-//   warps 10-13 state warpgroup: S^T (TMEM, fp32) -> bf16 snapshot in smem
+//   warps 2-5   features: phi(Q), phi(K) -> smem
+//   warps 6-9   polynomial: scores -> P (TMEM)
+//   warps 10-13 state: S^T (TMEM, fp32) -> bf16 snapshot in smem
+//   warps 14-17 epilogue: O (TMEM) -> normalised bf16 output rows
+//
+// The MMA chains into O and into S^T are issued interleaved so each hides the
+// other's accumulation latency, and the scores of tile c+1 are computed (into
+// the other buffer) before P V of tile c, so the polynomial runs concurrently
+// with the tensor core.
 //
 // The state-only variant (kStateOnly) runs just the phi(K) / update path and
 // writes the segment's state; it seeds the later segments of a head.
@@ -46,43 +54,46 @@ constexpr int kFPad = 160;    // padded feature count (K of phi(Q) S, N of the u
 constexpr int kSV = kDv + 1;  // state columns in global memory: values + normaliser
 constexpr int kNO = 80;       // N of phi(Q) S: 64 values, normaliser, 15 zero rows
 
-constexpr int kWarpTma = 0, kWarpMma = 1, kWarpFeat = 2, kWarpPoly = 6, kWarpState = 10;
-constexpr int kThreads = 14 * 32;
+constexpr int kWarpTma = 0, kWarpMma = 1, kWarpFeat = 2, kWarpPoly = 6, kWarpState = 10,
+              kWarpEpi = 14;
+constexpr int kThreads = 18 * 32;
 
 // TMEM columns (one CTA per SM owns all 512)
-constexpr uint32_t kColS = 0;       // S^T  128 lanes x 160 fp32
-constexpr uint32_t kColO = 160;     // O    128 lanes x 80 fp32
-constexpr uint32_t kColPhiQ = 256;  // phi(Q) bf16 pairs, 80 columns
-constexpr uint32_t kColSc = 384;    // scores fp32 (128) / P bf16 pairs (64)
+constexpr uint32_t kColS = 0;      // S^T  128 lanes x 160 fp32
+constexpr uint32_t kColO = 160;    // O    128 lanes x 80 fp32
+constexpr uint32_t kColSc = 256;   // 2 x (scores fp32 (128) / P bf16 pairs (64))
 constexpr uint32_t kTmemCols = 512;
 
 // Shared memory (offsets from a 1024-byte aligned base)
-constexpr uint32_t kQBytes = kT * kDqk * 2;     // 4 KB, 32B-swizzled rows
-constexpr uint32_t kVBytes = kT * kDv * 2;      // 16 KB, 128B-swizzled rows
-constexpr uint32_t kOffQ = 0;                   // 2 stages
+constexpr uint32_t kQBytes = kT * kDqk * 2;         // 4 KB, 32B-swizzled rows
+constexpr uint32_t kVBytes = kT * kDv * 2;          // 16 KB, 128B-swizzled rows
+constexpr uint32_t kOffQ = 0;                       // 2 stages
 constexpr uint32_t kOffK = kOffQ + 2 * kQBytes;
-constexpr uint32_t kOffV = kOffK + 2 * kQBytes;  // 16384
+constexpr uint32_t kOffV = kOffK + 2 * kQBytes;     // 16384
 constexpr uint32_t kOffOnes = kOffV + 2 * kVBytes;  // 49152: 16 rows x 128 B
-constexpr uint32_t kOffPhiK = kOffOnes + 2048;      // 51200: 3 feature blocks x 16 KB
-constexpr uint32_t kPhiKBlock = kT * 128;
-constexpr uint32_t kOffSnap = kOffPhiK + 3 * kPhiKBlock;  // 100352: 2 x 30 KB
-constexpr uint32_t kSnapKBlock = kNO * 128;               // 10 KB per 64-feature block
+constexpr uint32_t kPhiBlock = kT * 128;            // 64 features of 128 tokens
+constexpr uint32_t kPhiBytes = 3 * kPhiBlock;       // 160 features (3 blocks)
+constexpr uint32_t kOffPhiK = kOffOnes + 2048;      // 51200
+constexpr uint32_t kOffPhiQ = kOffPhiK + kPhiBytes; // 100352
+constexpr uint32_t kOffSnap = kOffPhiQ + kPhiBytes; // 149504: 2 x 30 KB
+constexpr uint32_t kSnapKBlock = kNO * 128;         // 10 KB per 64-feature block
 constexpr uint32_t kSnapBytes = 3 * kSnapKBlock;
-constexpr uint32_t kOffBar = kOffSnap + 2 * kSnapBytes;   // 161792
+constexpr uint32_t kOffBar = kOffSnap + 2 * kSnapBytes;  // 210944
 constexpr uint32_t kSmemBytes = kOffBar + 256;
-constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;        // alignment slack
+constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;       // alignment slack
 
 static_assert(kOffV % 1024 == 0 && kOffOnes % 1024 == 0 && kOffPhiK % 1024 == 0 &&
-                  kOffSnap % 1024 == 0 && kSnapKBlock % 1024 == 0,
+                  kOffPhiQ % 1024 == 0 && kOffSnap % 1024 == 0 && kSnapKBlock % 1024 == 0,
               "128B-swizzled regions need 1024-byte alignment");
+static_assert(kSmemAlloc <= 227 * 1024, "shared memory budget");
 
-enum Bar { kFull0, kFull1, kEmpty0, kEmpty1, kPhiQReady, kPhiKReady, kQSDone, kUpDone, kScReady,
-           kPReady, kOReady, kOFree, kSReady, kSnapReady, kDone, kNumBars };
+enum Bar { kFull0, kFull1, kEmpty0, kEmpty1, kPhiQReady, kPhiKReady, kQSDone, kUpDone, kScReady0,
+           kScReady1, kPReady0, kPReady1, kOReady, kOFree, kSReady, kSnapReady, kDone, kNumBars };
 
 // Optional per-role timeline of CTA (0, 0), compiled in with -DLA_TRACE only.
 #ifdef LA_TRACE
 constexpr int kTraceChunks = 32, kTraceEvents = 8;
-__device__ long long la_trace_buf[4][kTraceChunks][kTraceEvents];
+__device__ long long la_trace_buf[5][kTraceChunks][kTraceEvents];
 #define LA_TRACE_AT(role, chunk, ev)                                                   \
   do {                                                                                \
     if (blockIdx.x == 0 && blockIdx.y == 0 && (chunk) < kTraceChunks && (threadIdx.x & 31) == 0) \
@@ -181,30 +192,19 @@ __device__ __forceinline__ uint32_t feat_pair(const FeatSrc &s) {
   return hmul2_bf16(A, B);
 }
 
-// phi(K) chunk J (features 8J .. 8J+7) of token `row` -> 128B-swizzled smem
-template <int J>
-__device__ __forceinline__ void store_phik_chunk(const FeatSrc &s, uint32_t base, int row) {
-  st_shared_v4(base + (J >> 3) * (kT * 128) + sw128_offset(row, J & 7),
-               feat_pair<false, 8 * J + 0>(s), feat_pair<false, 8 * J + 2>(s),
-               feat_pair<false, 8 * J + 4>(s), feat_pair<false, 8 * J + 6>(s));
+// Features 8J .. 8J+7 of token `row` -> 128B-swizzled smem, 64 features per
+// 16 KB block: the K-major A layout of phi(Q) and the MN-major B layout of
+// phi(K) are the same bytes.
+template <bool kQ, int J>
+__device__ __forceinline__ void store_phi_chunk(const FeatSrc &s, uint32_t base, int row) {
+  st_shared_v4(base + (J >> 3) * kPhiBlock + sw128_offset(row, J & 7),
+               feat_pair<kQ, 8 * J + 0>(s), feat_pair<kQ, 8 * J + 2>(s),
+               feat_pair<kQ, 8 * J + 4>(s), feat_pair<kQ, 8 * J + 6>(s));
 }
-template <int... J>
-__device__ __forceinline__ void store_phik(const FeatSrc &s, uint32_t base, int row,
-                                           std::integer_sequence<int, J...>) {
-  (store_phik_chunk<J>(s, base, row), ...);
-}
-
-// phi(Q) columns [16G, 16G+16) (features 32G .. 32G+31) of TMEM lane `row`
-template <int G, int... I>
-__device__ __forceinline__ void store_phiq_group(const FeatSrc &s, uint32_t addr,
-                                                 std::integer_sequence<int, I...>) {
-  const uint32_t w[16] = {feat_pair<true, 32 * G + 2 * I>(s)...};
-  tmem_st16(addr, w);
-}
-template <int... G>
-__device__ __forceinline__ void store_phiq(const FeatSrc &s, uint32_t addr0,
-                                           std::integer_sequence<int, G...>) {
-  (store_phiq_group<G>(s, addr0 + 16 * G, std::make_integer_sequence<int, 16>{}), ...);
+template <bool kQ, int... J>
+__device__ __forceinline__ void store_phi(const FeatSrc &s, uint32_t base, int row,
+                                          std::integer_sequence<int, J...>) {
+  (store_phi_chunk<kQ, J>(s, base, row), ...);
 }
 
 struct Params {
@@ -294,25 +294,26 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     }
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
-    // Per tile c:  O = phi(Q) S_c;  S += [V 1 0]^T phi(K);  O += P V;  then the
-    // scores of tile c+1.  The update is issued before P V so the state
-    // snapshot of tile c+1 overlaps P V and the epilogue of tile c.
+    // Tile c:  O = phi(Q) S_c interleaved with S^T += [V 1 0]^T phi(K); the
+    // scores of tile c+1 into the other buffer; then O += P [V 1].
     if (lane == 0) {
       constexpr uint32_t id_sc = make_idesc_bf16(128, 128, false, false);
       constexpr uint32_t id_qs = make_idesc_bf16(128, kNO, false, false);
-      constexpr uint32_t id_pv = make_idesc_bf16(128, kDv, false, true);
+      constexpr uint32_t id_pv = make_idesc_bf16(128, kNO, false, true);
       constexpr uint32_t id_up = make_idesc_bf16(128, kFPad, true, true);
       const uint32_t a_ones = sb + kOffOnes;
-      const uint64_t qs_desc0 = make_sdesc(sb + kOffSnap, 16, 1024, kSwizzle128B);
-      const uint64_t qs_desc1 = make_sdesc(sb + kOffSnap + kSnapBytes, 16, 1024, kSwizzle128B);
-      const uint64_t up_b_desc = make_sdesc(sb + kOffPhiK, kPhiKBlock, 1024, kSwizzle128B);
-      bool ok = mbar_wait(&bars[kSnapReady], 0, abort_flag);  // S_0 in TMEM (+ snapshot 0)
-      auto issue_scores = [&](int s) {
+      const uint64_t qs_a_desc = make_sdesc(sb + kOffPhiQ, 16, 1024, kSwizzle128B);
+      const uint64_t qs_b_desc0 = make_sdesc(sb + kOffSnap, 16, 1024, kSwizzle128B);
+      const uint64_t qs_b_desc1 = make_sdesc(sb + kOffSnap + kSnapBytes, 16, 1024, kSwizzle128B);
+      const uint64_t up_b_desc = make_sdesc(sb + kOffPhiK, kPhiBlock, 1024, kSwizzle128B);
+      auto issue_scores = [&](int c) {  // into buffer c & 1 from stage c & 1
+        const int s = c & 1;
         const uint64_t da = make_sdesc(sb + kOffQ + s * kQBytes, 16, 256, kSwizzle32B);
         const uint64_t db = make_sdesc(sb + kOffK + s * kQBytes, 16, 256, kSwizzle32B);
-        umma_ss(tmem + kColSc, da, db, id_sc, 0);
-        umma_commit(&bars[kScReady]);
+        umma_ss(tmem + kColSc + 128 * s, da, db, id_sc, 0);
+        umma_commit(&bars[kScReady0 + s]);
       };
+      bool ok = mbar_wait(&bars[kSnapReady], 0, abort_flag);  // S_0 in TMEM (+ snapshot 0)
       if (!kStateOnly && ok) {
         ok = mbar_wait(&bars[kFull0], 0, abort_flag);
         if (ok) {
@@ -323,30 +324,30 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       for (int c = 0; ok && c < n_chunks; ++c) {
         const int s = c & 1;
         const uint32_t v_base = sb + kOffV + s * kVBytes;
+        if (!mbar_wait(&bars[kPhiKReady], c & 1, abort_flag)) break;
         if (!kStateOnly) {
           if (!mbar_wait(&bars[kPhiQReady], c & 1, abort_flag)) break;
           if (c > 0 && !mbar_wait(&bars[kSnapReady], c & 1, abort_flag)) break;
           if (c > 0 && !mbar_wait(&bars[kOFree], (c - 1) & 1, abort_flag)) break;
-          tc_fence_after();
-          LA_TRACE_AT(0, c, 0);
-          // O = phi(Q) S_c   (K = 160 features in 10 steps of 16)
-          const uint64_t snap_desc = (c & 1) ? qs_desc1 : qs_desc0;
-#pragma unroll
-          for (int j = 0; j < kFPad / 16; ++j) {
-            const uint64_t db = snap_desc + (((j >> 2) * kSnapKBlock + (j & 3) * 32) >> 4);
-            umma_ts(tmem + kColO, tmem + kColPhiQ + 8 * j, db, id_qs, j > 0 ? 1u : 0u);
-          }
-          umma_commit(&bars[kQSDone]);
         }
-        if (!mbar_wait(&bars[kPhiKReady], c & 1, abort_flag)) break;
         tc_fence_after();
-        LA_TRACE_AT(0, c, 1);
-        // S^T += [V 1 0]^T phi(K)   (K = 128 tokens in 8 steps)
+        LA_TRACE_AT(0, c, 0);
+        const uint64_t qs_b_desc = (c & 1) ? qs_b_desc1 : qs_b_desc0;
 #pragma unroll
-        for (int j = 0; j < kT / 16; ++j) {
-          const uint32_t a_addr = v_base + j * 2048;
-          const uint64_t da = make_sdesc(a_addr, a_ones - a_addr, 1024, kSwizzle128B);
-          umma_ss(tmem + kColS, da, up_b_desc + (uint64_t)((j * 2048) >> 4), id_up, 1u);
+        for (int j = 0; j < kFPad / 16; ++j) {
+          if (!kStateOnly) {
+            // O (+)= phi(Q)[:, 16j:16j+16] S_c[16j:16j+16, :]
+            const uint32_t koff = (j >> 2) * kPhiBlock + (j & 3) * 32;
+            const uint32_t boff = (j >> 2) * kSnapKBlock + (j & 3) * 32;
+            umma_ss(tmem + kColO, qs_a_desc + (koff >> 4), qs_b_desc + (boff >> 4), id_qs,
+                    j > 0 ? 1u : 0u);
+          }
+          if (j < kT / 16) {
+            // S^T += [V 1 0]^T[:, 16j:16j+16] phi(K)[16j:16j+16, :]
+            const uint32_t a_addr = v_base + j * 2048;
+            const uint64_t da = make_sdesc(a_addr, a_ones - a_addr, 1024, kSwizzle128B);
+            umma_ss(tmem + kColS, da, up_b_desc + (uint64_t)((j * 2048) >> 4), id_up, 1u);
+          }
         }
         umma_commit(&bars[kSReady]);
         umma_commit(&bars[kUpDone]);
@@ -354,30 +355,35 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           umma_commit(&bars[kEmpty0 + s]);
           continue;
         }
-        if (!mbar_wait(&bars[kPReady], c & 1, abort_flag)) break;
+        umma_commit(&bars[kQSDone]);
+        if (c + 1 < n_chunks) {
+          // buffer (c+1)&1 held P(c-1), consumed by P V of tile c-1 (done:
+          // its epilogue already released O)
+          if (!mbar_wait(&bars[kFull0 + ((c + 1) & 1)], ((c + 1) >> 1) & 1, abort_flag)) break;
+          tc_fence_after();
+          issue_scores(c + 1);
+        }
+        if (!mbar_wait(&bars[kPReady0 + s], (c >> 1) & 1, abort_flag)) break;
         tc_fence_after();
-        LA_TRACE_AT(0, c, 2);
-        // O[:, :64] += P V   (K = 128 tokens in 8 steps)
-        const uint64_t pv_desc = make_sdesc(v_base, 8192, 1024, kSwizzle128B);
+        LA_TRACE_AT(0, c, 1);
+        // O += P [V 1]: B = V (64 columns) with the ones block as its second
+        // 64-column block (LBO), so O[:, 64] also collects the row sum of P.
 #pragma unroll
-        for (int j = 0; j < kT / 16; ++j)
-          umma_ts(tmem + kColO, tmem + kColSc + 8 * j, pv_desc + (uint64_t)((j * 2048) >> 4), id_pv, 1u);
+        for (int j = 0; j < kT / 16; ++j) {
+          const uint32_t b_addr = v_base + j * 2048;
+          const uint64_t db = make_sdesc(b_addr, a_ones - b_addr, 1024, kSwizzle128B);
+          umma_ts(tmem + kColO, tmem + kColSc + 128 * s + 8 * j, db, id_pv, 1u);
+        }
         umma_commit(&bars[kOReady]);
         umma_commit(&bars[kEmpty0 + s]);
-        if (c + 1 < n_chunks) {
-          if (!mbar_wait(&bars[kFull0 + ((c + 1) & 1)], ((c + 1) >> 1) & 1, abort_flag)) break;
-          if (!mbar_wait(&bars[kOReady], c & 1, abort_flag)) break;  // P region free again
-          tc_fence_after();
-          LA_TRACE_AT(0, c, 3);
-          issue_scores((c + 1) & 1);
-        }
+        LA_TRACE_AT(0, c, 2);
       }
       umma_commit(&bars[kDone]);
     }
   } else if (warp < kWarpPoly) {
     // ------------------------------------------------------------ features
     const int wq = warp & 3;
-    const int row = wq * 32 + lane;  // token within the tile == TMEM lane
+    const int row = wq * 32 + lane;  // token within the tile
     const bool leader = (warp == kWarpFeat && lane == 0);
     for (int c = 0; c < n_chunks; ++c) {
       const int s = c & 1;
@@ -397,11 +403,24 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       }
       named_barrier_sync(1, 128);
       if (leader) mbar_arrive(&bars[kEmpty0 + s]);
+      // phi(K) once the previous update has read the buffer
+      if (c > 0) mbar_wait(&bars[kUpDone], (c - 1) & 1, abort_flag);
+      if (!wg_ok(1, abort_flag)) break;
+      {
+        FeatSrc fk;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) fk.raw[i] = vrow ? kw[i] : 0u;
+        fk.one_valid = vrow ? 0x3F803F80u : 0u;  // padding tokens add nothing to the state
+        store_phi<false>(fk, sb + kOffPhiK, row, std::make_integer_sequence<int, kFPad / 8>{});
+      }
+      fence_proxy_async_smem();
+      named_barrier_sync(1, 128);
+      if (leader) mbar_arrive(&bars[kPhiKReady]);
+      LA_TRACE_AT(1, c, 1);
       if (!kStateOnly) {
-        // phi(Q) -> TMEM once phi(Q) S of the previous tile has read it
+        // phi(Q) once phi(Q) S of the previous tile has read the buffer
         if (c > 0) mbar_wait(&bars[kQSDone], (c - 1) & 1, abort_flag);
         if (!wg_ok(1, abort_flag)) break;
-        tc_fence_after();
         FeatSrc fs;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -411,134 +430,76 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           fs.s32[i] = hmul2_bf16(qw[i], 0x3D003D00u);  // x / 32  (exact)
         }
         fs.one_valid = 0x3F803F80u;
-        store_phiq(fs, taddr(tmem, wq * 32, kColPhiQ), std::make_integer_sequence<int, kFPad / 32>{});
-        tmem_wait_st();
-        tc_fence_before();
+        store_phi<true>(fs, sb + kOffPhiQ, row, std::make_integer_sequence<int, kFPad / 8>{});
+        fence_proxy_async_smem();
         named_barrier_sync(1, 128);
         if (leader) mbar_arrive(&bars[kPhiQReady]);
-        LA_TRACE_AT(1, c, 1);
+        LA_TRACE_AT(1, c, 2);
       }
-      // phi(K) -> smem once the previous update has read it
-      if (c > 0) mbar_wait(&bars[kUpDone], (c - 1) & 1, abort_flag);
-      if (!wg_ok(1, abort_flag)) break;
-      FeatSrc fk;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) fk.raw[i] = vrow ? kw[i] : 0u;
-      fk.one_valid = vrow ? 0x3F803F80u : 0u;  // padding tokens add nothing to the state
-      store_phik(fk, sb + kOffPhiK, row, std::make_integer_sequence<int, kFPad / 8>{});
-      fence_proxy_async_smem();
-      named_barrier_sync(1, 128);
-      if (leader) mbar_arrive(&bars[kPhiKReady]);
-      LA_TRACE_AT(1, c, 2);
     }
   } else if (warp < kWarpState) {
-    // ------------------------------------------------------------ polynomial + epilogue
+    // ------------------------------------------------------------ polynomial
     if (!kStateOnly) {
       const int wq = warp & 3;
       const int row = wq * 32 + lane;
       const bool leader = (warp == kWarpPoly && lane == 0);
+      const uint64_t c32 = f2pack(0.03125f, 0.03125f), c4 = f2pack(0.25f, 0.25f);
+      const uint64_t one2 = f2pack(1.f, 1.f);
       for (int c = 0; c < n_chunks; ++c) {
+        const int s = c & 1;
         const int64_t t0 = t_begin + (int64_t)c * kT;
         const int valid = (int)min64(kT, t_end - t0);
-        mbar_wait(&bars[kScReady], c & 1, abort_flag);
+        const bool full_tile = valid == kT;
+        const uint32_t col0 = kColSc + 128 * s;
+        mbar_wait(&bars[kScReady0 + s], (c >> 1) & 1, abort_flag);
         if (!wg_ok(2, abort_flag)) break;
         tc_fence_after();
         LA_TRACE_AT(2, c, 0);
         // P = tril(1 + s/4 + s^2/32) for raw scores s = q.k (d = 16).  Key group
-        // G (32 keys) is entirely below the diagonal for this warp's rows when
-        // G < wq, holds the diagonal when G == wq and is all zero when G > wq.
-        const uint64_t c32 = f2pack(0.03125f, 0.03125f), c4 = f2pack(0.25f, 0.25f);
-        const uint64_t one2 = f2pack(1.f, 1.f);
-        const bool full_tile = valid == kT;
-        uint64_t rs2 = f2pack(0.f, 0.f);
+        // G (32 keys) lies below the diagonal for this warp's rows when G < wq,
+        // holds the diagonal when G == wq and is all zero when G > wq.
 #pragma unroll
-        for (int H = 0; H < 2; ++H) {  // two halves of 64 keys
-          uint32_t w[2][16];
-          if (2 * H <= wq) {
-            uint32_t r[64];
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4)
-              tmem_ld16(taddr(tmem, wq * 32, kColSc + 64 * H + 16 * q4), r + 16 * q4);
+        for (int G = 0; G < 4; ++G) {
+          uint32_t w[16];
+          if (G <= wq) {
+            uint32_t r[32];
+            tmem_ld16(taddr(tmem, wq * 32, col0 + 32 * G), r);
+            tmem_ld16(taddr(tmem, wq * 32, col0 + 32 * G + 16), r + 16);
             tmem_wait_ld();
+            if (G < wq && full_tile) {
 #pragma unroll
-            for (int G2 = 0; G2 < 2; ++G2) {
-              const int G = 2 * H + G2;
-              if (G > wq) {
+              for (int i = 0; i < 16; ++i) {
+                const uint64_t s2 = f2pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+                w[i] = pack_bf16x2(ffma2(s2, ffma2(s2, c32, c4), one2));
+              }
+            } else {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) w[G2][i] = 0u;
-              } else if (G < wq && full_tile) {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                  const uint64_t s2 = f2pack(__uint_as_float(r[32 * G2 + 2 * i]),
-                                             __uint_as_float(r[32 * G2 + 2 * i + 1]));
-                  const uint64_t p2 = ffma2(s2, ffma2(s2, c32, c4), one2);
-                  rs2 = fadd2(rs2, p2);
-                  w[G2][i] = pack_bf16x2(p2);
-                }
-              } else {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                  const int j0 = 32 * G + 2 * i;
-                  const uint64_t s2 = f2pack(__uint_as_float(r[32 * G2 + 2 * i]),
-                                             __uint_as_float(r[32 * G2 + 2 * i + 1]));
-                  float p0, p1;
-                  f2unpack(ffma2(s2, ffma2(s2, c32, c4), one2), p0, p1);
-                  p0 = (j0 <= row && j0 < valid) ? p0 : 0.f;
-                  p1 = (j0 + 1 <= row && j0 + 1 < valid) ? p1 : 0.f;
-                  const uint64_t p2 = f2pack(p0, p1);
-                  rs2 = fadd2(rs2, p2);
-                  w[G2][i] = pack_bf16x2(p2);
-                }
+              for (int i = 0; i < 16; ++i) {
+                const int j0 = 32 * G + 2 * i;
+                const uint64_t s2 = f2pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+                float p0, p1;
+                f2unpack(ffma2(s2, ffma2(s2, c32, c4), one2), p0, p1);
+                p0 = (j0 <= row && j0 < valid) ? p0 : 0.f;
+                p1 = (j0 + 1 <= row && j0 + 1 < valid) ? p1 : 0.f;
+                w[i] = pack_bf16(p0, p1);
               }
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) w[0][i] = w[1][i] = 0u;
+            for (int i = 0; i < 16; ++i) w[i] = 0u;
           }
-          // P columns [32H, 32H + 32) hold keys [64H, 64H + 64); those score
-          // columns were all read above
-          tmem_st16(taddr(tmem, wq * 32, kColSc + 32 * H), w[0]);
-          tmem_st16(taddr(tmem, wq * 32, kColSc + 32 * H + 16), w[1]);
+          // P columns [16G, 16G + 16) hold keys [32G, 32G + 32); those score
+          // columns were read above (or are never needed)
+          tmem_st16(taddr(tmem, wq * 32, col0 + 16 * G), w);
         }
-        float rs_lo, rs_hi;
-        f2unpack(rs2, rs_lo, rs_hi);
-        const float rs = rs_lo + rs_hi;
         tmem_wait_st();
         tc_fence_before();
         named_barrier_sync(2, 128);
-        if (leader) mbar_arrive(&bars[kPReady]);
+        if (leader) mbar_arrive(&bars[kPReady0 + s]);
         LA_TRACE_AT(2, c, 1);
-
-        mbar_wait(&bars[kOReady], c & 1, abort_flag);
-        if (!wg_ok(2, abort_flag)) break;
-        tc_fence_after();
-        LA_TRACE_AT(2, c, 2);
-        uint32_t o[kNO];
-#pragma unroll
-        for (int G = 0; G < kNO / 16; ++G) tmem_ld16(taddr(tmem, wq * 32, kColO + 16 * G), o + 16 * G);
-        tmem_wait_ld();
-        tc_fence_before();
-        named_barrier_sync(2, 128);
-        if (leader) mbar_arrive(&bars[kOFree]);  // O is in registers: TMEM O reusable
-        const float den = __uint_as_float(o[kDv]) + rs + p.eps;
-        const float inv = p.normalize ? 1.f / den : 1.f;
-        const uint64_t inv2 = f2pack(inv, inv);
-        if (row < valid) {
-          __nv_bfloat16 *orow = p.out + ((uint64_t)bh * p.n + t0 + row) * kDv;
-#pragma unroll
-          for (int G = 0; G < kDv / 8; ++G) {
-            uint32_t w[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              w[i] = pack_bf16x2(fmul2(f2pack(__uint_as_float(o[8 * G + 2 * i]),
-                                              __uint_as_float(o[8 * G + 2 * i + 1])), inv2));
-            *(uint4 *)(orow + 8 * G) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-        }
-        LA_TRACE_AT(2, c, 3);
       }
     }
-  } else {
+  } else if (warp < kWarpEpi) {
     // ------------------------------------------------------------ state
     const int wq = warp & 3;
     const int e = wq * 32 + lane;  // row of S^T: value column e (< 64), normaliser (64)
@@ -610,7 +571,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         // rows >= 80 are not part of the snapshot; their warp only joins the barriers
         if (wq < 3) {
 #pragma unroll
-          for (int B = 0; B < kFPad / 64 + 1; ++B) {  // 64 + 64 + 32 columns
+          for (int B = 0; B < 3; ++B) {  // 64 + 64 + 32 feature columns
             const int cols = B < 2 ? 64 : 32;
             uint32_t r[64];
 #pragma unroll
@@ -623,10 +584,10 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
               for (int ch = 0; ch < 8; ++ch)
                 if (ch < cols / 8)
                   st_shared_v4(blk + sw128_offset(e, ch),
-                             pack_bf16(__uint_as_float(r[8 * ch + 0]), __uint_as_float(r[8 * ch + 1])),
-                             pack_bf16(__uint_as_float(r[8 * ch + 2]), __uint_as_float(r[8 * ch + 3])),
-                             pack_bf16(__uint_as_float(r[8 * ch + 4]), __uint_as_float(r[8 * ch + 5])),
-                             pack_bf16(__uint_as_float(r[8 * ch + 6]), __uint_as_float(r[8 * ch + 7])));
+                               pack_bf16(__uint_as_float(r[8 * ch + 0]), __uint_as_float(r[8 * ch + 1])),
+                               pack_bf16(__uint_as_float(r[8 * ch + 2]), __uint_as_float(r[8 * ch + 3])),
+                               pack_bf16(__uint_as_float(r[8 * ch + 4]), __uint_as_float(r[8 * ch + 5])),
+                               pack_bf16(__uint_as_float(r[8 * ch + 6]), __uint_as_float(r[8 * ch + 7])));
             }
             if (last && write_final && real) {
               float *dst = p.final_state + (uint64_t)bh * kF * kSV;
@@ -643,6 +604,45 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         named_barrier_sync(3, 128);
         if (leader) mbar_arrive(&bars[kSnapReady]);
         LA_TRACE_AT(3, c, 1);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    if (!kStateOnly) {
+      const int wq = warp & 3;
+      const int row = wq * 32 + lane;
+      const bool leader = (warp == kWarpEpi && lane == 0);
+      for (int c = 0; c < n_chunks; ++c) {
+        const int64_t t0 = t_begin + (int64_t)c * kT;
+        const int valid = (int)min64(kT, t_end - t0);
+        mbar_wait(&bars[kOReady], c & 1, abort_flag);
+        if (!wg_ok(4, abort_flag)) break;
+        tc_fence_after();
+        LA_TRACE_AT(4, c, 0);
+        uint32_t o[kNO];
+#pragma unroll
+        for (int G = 0; G < kNO / 16; ++G) tmem_ld16(taddr(tmem, wq * 32, kColO + 16 * G), o + 16 * G);
+        tmem_wait_ld();
+        tc_fence_before();
+        named_barrier_sync(4, 128);
+        if (leader) mbar_arrive(&bars[kOFree]);  // O is in registers: TMEM O reusable
+        // O[:, 64] = phi(q).z + rowsum(P): the full denominator before eps
+        const float den = __uint_as_float(o[kDv]) + p.eps;
+        const float inv = p.normalize ? 1.f / den : 1.f;
+        const uint64_t inv2 = f2pack(inv, inv);
+        if (row < valid) {
+          __nv_bfloat16 *orow = p.out + ((uint64_t)bh * p.n + t0 + row) * kDv;
+#pragma unroll
+          for (int G = 0; G < kDv / 8; ++G) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              w[i] = pack_bf16x2(fmul2(f2pack(__uint_as_float(o[8 * G + 2 * i]),
+                                              __uint_as_float(o[8 * G + 2 * i + 1])), inv2));
+            *(uint4 *)(orow + 8 * G) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+        LA_TRACE_AT(4, c, 1);
       }
     }
   }
@@ -719,7 +719,7 @@ int launch(const void *q, const void *k, const void *v, const Params &p, int64_t
 
 #ifdef LA_TRACE
 extern "C" int la_debug_read_trace(long long *dst, int count) {
-  const int n = 4 * kTraceChunks * kTraceEvents;
+  const int n = 5 * kTraceChunks * kTraceEvents;
   if (count < n) return -1;
   return cudaMemcpyFromSymbol(dst, la_trace_buf, sizeof(long long) * n) == cudaSuccess ? n : -1;
 }
