@@ -5,10 +5,11 @@
 // the tile's rows, S_c the fp32 state of all earlier tokens, phi the Taylor
 // feature map in the query/key-split basis of include/la_attention.h):
 //
-//   scores = Q K^T                  tcgen05 M=128 N=128 K=16   -> TMEM (2 buffers)
-//   P      = tril(1 + s/4 + s^2/32) CUDA cores, bf16 P written over its scores
-//   O      = phi(Q) S_c             tcgen05 M=128 N=80  K=160  (S_c: bf16 snapshot)
 //   S^T   += [V 1 0]^T phi(K)       tcgen05 M=128 N=160 K=128  (fp32 state in TMEM)
+//   O      = phi(Q) S_c             tcgen05 M=128 N=80  K=160  (A = phi(Q) in TMEM,
+//                                                               B = bf16 snapshot of S_c)
+//   scores = Q K^T                  tcgen05 M=128 N=128 K=16   -> TMEM
+//   P      = tril(1 + s/4 + s^2/32) CUDA cores, bf16 P written over its scores
 //   O     += P [V 1]                tcgen05 M=128 N=80  K=128  (A = P in TMEM)
 //   out    = O[:, :64] / (O[:, 64] + eps)
 //
@@ -17,22 +18,24 @@
 // tril(scores) V) with the intra-tile term evaluated in the equivalent
 // polynomial form 1 + s + s^2/2 and the normaliser carried both as state row
 // 64 (z = sum phi(k)) and as the ones column of [V 1] (the row sum of P).
-// The 153 features never touch HBM: each token's phi(Q) and phi(K) are
-// expanded in registers and written to shared memory by the thread that owns
-// the token.
+// The 153 features never touch HBM: each token's phi(Q) is expanded in
+// registers and stored to TMEM, its phi(K) to shared memory, by the thread
+// that owns the token.
+//
+// Every M=128, K=16 tcgen05.mma costs about 100 cycles whatever its N up to
+// 160, so a tile is ~27 MMAs (~2,800 cycles) of tensor-pipe time.  The issue
+// order  UP(c), QS(c), PV(c), scores(c+1), UP(c+1), ...  keeps that pipe busy:
+// the state snapshot and phi(K) of tile c+1 are produced while QS(c) and PV(c)
+// run, phi(Q) of tile c+1 while PV(c) and UP(c+1) run, and P of tile c+1 while
+// UP(c+1) and QS(c+1) run.
 //
 // Warp roles (576 threads, one CTA per SM):
 //   warp 0      TMA producer (Q, K, V tiles; 2-stage ring)
 //   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2-5   features: phi(Q), phi(K) -> smem
+//   warps 2-5   features: phi(K) -> smem (2 buffers), phi(Q) -> TMEM
 //   warps 6-9   polynomial: scores -> P (TMEM)
-//   warps 10-13 state: S^T (TMEM, fp32) -> bf16 snapshot in smem
+//   warps 10-13 state: S^T (TMEM, fp32) -> bf16 snapshot in smem (2 buffers)
 //   warps 14-17 epilogue: O (TMEM) -> normalised bf16 output rows
-//
-// The MMA chains into O and into S^T are issued interleaved so each hides the
-// other's accumulation latency, and the scores of tile c+1 are computed (into
-// the other buffer) before P V of tile c, so the polynomial runs concurrently
-// with the tensor core.
 //
 // The state-only variant (kStateOnly) runs just the phi(K) / update path and
 // writes the segment's state; it seeds the later segments of a head.
@@ -59,9 +62,10 @@ constexpr int kWarpTma = 0, kWarpMma = 1, kWarpFeat = 2, kWarpPoly = 6, kWarpSta
 constexpr int kThreads = 18 * 32;
 
 // TMEM columns (one CTA per SM owns all 512)
-constexpr uint32_t kColS = 0;      // S^T  128 lanes x 160 fp32
-constexpr uint32_t kColO = 160;    // O    128 lanes x 80 fp32
-constexpr uint32_t kColSc = 256;   // 2 x (scores fp32 (128) / P bf16 pairs (64))
+constexpr uint32_t kColS = 0;       // S^T    128 lanes x 160 fp32
+constexpr uint32_t kColO = 160;     // O      128 lanes x 80 fp32
+constexpr uint32_t kColPhiQ = 256;  // phi(Q) 128 lanes x 80 bf16 pairs
+constexpr uint32_t kColSc = 384;    // scores 128 fp32 / P 64 bf16 pairs
 constexpr uint32_t kTmemCols = 512;
 
 // Shared memory (offsets from a 1024-byte aligned base)
@@ -73,9 +77,8 @@ constexpr uint32_t kOffV = kOffK + 2 * kQBytes;     // 16384
 constexpr uint32_t kOffOnes = kOffV + 2 * kVBytes;  // 49152: 16 rows x 128 B
 constexpr uint32_t kPhiBlock = kT * 128;            // 64 features of 128 tokens
 constexpr uint32_t kPhiBytes = 3 * kPhiBlock;       // 160 features (3 blocks)
-constexpr uint32_t kOffPhiK = kOffOnes + 2048;      // 51200
-constexpr uint32_t kOffPhiQ = kOffPhiK + kPhiBytes; // 100352
-constexpr uint32_t kOffSnap = kOffPhiQ + kPhiBytes; // 149504: 2 x 30 KB
+constexpr uint32_t kOffPhiK = kOffOnes + 2048;      // 51200: 2 buffers
+constexpr uint32_t kOffSnap = kOffPhiK + 2 * kPhiBytes;  // 149504: 2 x 30 KB
 constexpr uint32_t kSnapKBlock = kNO * 128;         // 10 KB per 64-feature block
 constexpr uint32_t kSnapBytes = 3 * kSnapKBlock;
 constexpr uint32_t kOffBar = kOffSnap + 2 * kSnapBytes;  // 210944
@@ -83,12 +86,15 @@ constexpr uint32_t kSmemBytes = kOffBar + 256;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;       // alignment slack
 
 static_assert(kOffV % 1024 == 0 && kOffOnes % 1024 == 0 && kOffPhiK % 1024 == 0 &&
-                  kOffPhiQ % 1024 == 0 && kOffSnap % 1024 == 0 && kSnapKBlock % 1024 == 0,
+                  kPhiBytes % 1024 == 0 && kOffSnap % 1024 == 0 && kSnapKBlock % 1024 == 0,
               "128B-swizzled regions need 1024-byte alignment");
 static_assert(kSmemAlloc <= 227 * 1024, "shared memory budget");
 
-enum Bar { kFull0, kFull1, kEmpty0, kEmpty1, kPhiQReady, kPhiKReady, kQSDone, kUpDone, kScReady0,
-           kScReady1, kPReady0, kPReady1, kOReady, kOFree, kSReady, kSnapReady, kDone, kNumBars };
+// Barriers.  Per-buffer pairs (..0/..1) complete once per two tiles; a
+// producer that may run two tiles ahead of its consumer needs them.
+enum Bar { kFull0, kFull1, kEmpty0, kEmpty1, kPhiKReady0, kPhiKReady1, kUpDone0, kUpDone1,
+           kPhiQReady, kQSDone, kScReady, kPReady, kOReady, kOFree, kSReady, kSnapReady, kDone,
+           kNumBars };
 
 // Optional per-role timeline of CTA (0, 0), compiled in with -DLA_TRACE only.
 #ifdef LA_TRACE
@@ -207,6 +213,19 @@ __device__ __forceinline__ void store_phi(const FeatSrc &s, uint32_t base, int r
   (store_phi_chunk<kQ, J>(s, base, row), ...);
 }
 
+// phi(Q) columns [16G, 16G+16) (features 32G .. 32G+31) of TMEM lane `row`
+template <int G, int... I>
+__device__ __forceinline__ void store_phiq_group(const FeatSrc &s, uint32_t addr,
+                                                 std::integer_sequence<int, I...>) {
+  const uint32_t w[16] = {feat_pair<true, 32 * G + 2 * I>(s)...};
+  tmem_st16(addr, w);
+}
+template <int... G>
+__device__ __forceinline__ void store_phiq(const FeatSrc &s, uint32_t addr0,
+                                           std::integer_sequence<int, G...>) {
+  (store_phiq_group<G>(s, addr0 + 16 * G, std::make_integer_sequence<int, 16>{}), ...);
+}
+
 struct Params {
   __nv_bfloat16 *out;
   const float *init_state;  // (bh, F, 65) or null
@@ -294,26 +313,45 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     }
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
-    // Tile c:  O = phi(Q) S_c interleaved with S^T += [V 1 0]^T phi(K); the
-    // scores of tile c+1 into the other buffer; then O += P [V 1].
+    // Tensor-pipe order: UP(0), [sc(0)], then per tile c: QS(c), PV(c),
+    // sc(c+1), UP(c+1).
     if (lane == 0) {
       constexpr uint32_t id_sc = make_idesc_bf16(128, 128, false, false);
       constexpr uint32_t id_qs = make_idesc_bf16(128, kNO, false, false);
       constexpr uint32_t id_pv = make_idesc_bf16(128, kNO, false, true);
       constexpr uint32_t id_up = make_idesc_bf16(128, kFPad, true, true);
       const uint32_t a_ones = sb + kOffOnes;
-      const uint64_t qs_a_desc = make_sdesc(sb + kOffPhiQ, 16, 1024, kSwizzle128B);
       const uint64_t qs_b_desc0 = make_sdesc(sb + kOffSnap, 16, 1024, kSwizzle128B);
       const uint64_t qs_b_desc1 = make_sdesc(sb + kOffSnap + kSnapBytes, 16, 1024, kSwizzle128B);
-      const uint64_t up_b_desc = make_sdesc(sb + kOffPhiK, kPhiBlock, 1024, kSwizzle128B);
-      auto issue_scores = [&](int c) {  // into buffer c & 1 from stage c & 1
+      // S^T += [V 1 0]^T phi(K) of tile c (8 K-steps of 16 tokens)
+      auto issue_update = [&](int c) {
+        const int b = c & 1;
+        const uint32_t v_base = sb + kOffV + b * kVBytes;
+        const uint64_t db0 = make_sdesc(sb + kOffPhiK + b * kPhiBytes, kPhiBlock, 1024, kSwizzle128B);
+        const uint64_t da0 = make_sdesc(v_base, a_ones - v_base, 1024, kSwizzle128B);
+        // each step: start address +2048 B, LBO (distance to the ones block) -2048 B
+        constexpr uint64_t kStep = (uint64_t)(2048 >> 4) - ((uint64_t)(2048 >> 4) << 16);
+#pragma unroll
+        for (int j = 0; j < kT / 16; ++j)
+          umma_ss(tmem + kColS, da0 + kStep * j, db0 + (uint64_t)((j * 2048) >> 4), id_up, 1u);
+        umma_commit(&bars[kSReady]);
+        umma_commit(&bars[kUpDone0 + b]);
+      };
+      auto issue_scores = [&](int c) {
         const int s = c & 1;
         const uint64_t da = make_sdesc(sb + kOffQ + s * kQBytes, 16, 256, kSwizzle32B);
         const uint64_t db = make_sdesc(sb + kOffK + s * kQBytes, 16, 256, kSwizzle32B);
-        umma_ss(tmem + kColSc + 128 * s, da, db, id_sc, 0);
-        umma_commit(&bars[kScReady0 + s]);
+        umma_ss(tmem + kColSc, da, db, id_sc, 0);
+        umma_commit(&bars[kScReady]);
       };
-      bool ok = mbar_wait(&bars[kSnapReady], 0, abort_flag);  // S_0 in TMEM (+ snapshot 0)
+      bool ok = mbar_wait(&bars[kSnapReady], 0, abort_flag)  // S_0 in TMEM (+ snapshot 0)
+                && mbar_wait(&bars[kPhiKReady0], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        LA_TRACE_AT(0, 0, 0);
+        issue_update(0);
+        if (kStateOnly) umma_commit(&bars[kEmpty0]);
+      }
       if (!kStateOnly && ok) {
         ok = mbar_wait(&bars[kFull0], 0, abort_flag);
         if (ok) {
@@ -323,67 +361,58 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       }
       for (int c = 0; ok && c < n_chunks; ++c) {
         const int s = c & 1;
-        const uint32_t v_base = sb + kOffV + s * kVBytes;
-        if (!mbar_wait(&bars[kPhiKReady], c & 1, abort_flag)) break;
+        const int c1 = c + 1;
         if (!kStateOnly) {
+          // O = phi(Q) S_c   (K = 160 features in 10 steps; S_c is snapshot c&1)
           if (!mbar_wait(&bars[kPhiQReady], c & 1, abort_flag)) break;
-          if (c > 0 && !mbar_wait(&bars[kSnapReady], c & 1, abort_flag)) break;
           if (c > 0 && !mbar_wait(&bars[kOFree], (c - 1) & 1, abort_flag)) break;
-        }
-        tc_fence_after();
-        LA_TRACE_AT(0, c, 0);
-        const uint64_t qs_b_desc = (c & 1) ? qs_b_desc1 : qs_b_desc0;
+          tc_fence_after();
+          LA_TRACE_AT(0, c, 1);
+          const uint64_t qs_b_desc = (c & 1) ? qs_b_desc1 : qs_b_desc0;
 #pragma unroll
-        for (int j = 0; j < kFPad / 16; ++j) {
-          if (!kStateOnly) {
-            // O (+)= phi(Q)[:, 16j:16j+16] S_c[16j:16j+16, :]
-            const uint32_t koff = (j >> 2) * kPhiBlock + (j & 3) * 32;
+          for (int j = 0; j < kFPad / 16; ++j) {
             const uint32_t boff = (j >> 2) * kSnapKBlock + (j & 3) * 32;
-            umma_ss(tmem + kColO, qs_a_desc + (koff >> 4), qs_b_desc + (boff >> 4), id_qs,
+            umma_ts(tmem + kColO, tmem + kColPhiQ + 8 * j, qs_b_desc + (boff >> 4), id_qs,
                     j > 0 ? 1u : 0u);
           }
-          if (j < kT / 16) {
-            // S^T += [V 1 0]^T[:, 16j:16j+16] phi(K)[16j:16j+16, :]
-            const uint32_t a_addr = v_base + j * 2048;
-            const uint64_t da = make_sdesc(a_addr, a_ones - a_addr, 1024, kSwizzle128B);
-            umma_ss(tmem + kColS, da, up_b_desc + (uint64_t)((j * 2048) >> 4), id_up, 1u);
+          umma_commit(&bars[kQSDone]);
+          // O += P [V 1]: B = V (64 columns) with the ones block as its second
+          // 64-column block (LBO), so O[:, 64] also collects the row sum of P.
+          if (!mbar_wait(&bars[kPReady], c & 1, abort_flag)) break;
+          tc_fence_after();
+          LA_TRACE_AT(0, c, 2);
+          const uint32_t v_base = sb + kOffV + s * kVBytes;
+          const uint64_t db0 = make_sdesc(v_base, a_ones - v_base, 1024, kSwizzle128B);
+          constexpr uint64_t kStep = (uint64_t)(2048 >> 4) - ((uint64_t)(2048 >> 4) << 16);
+#pragma unroll
+          for (int j = 0; j < kT / 16; ++j)
+            umma_ts(tmem + kColO, tmem + kColSc + 8 * j, db0 + kStep * j, id_pv, 1u);
+          umma_commit(&bars[kOReady]);
+          umma_commit(&bars[kEmpty0 + s]);
+          if (c1 < n_chunks) {
+            // scores of tile c+1 overwrite P(c): wait for P V to finish
+            if (!mbar_wait(&bars[kFull0 + (c1 & 1)], (c1 >> 1) & 1, abort_flag)) break;
+            if (!mbar_wait(&bars[kOReady], c & 1, abort_flag)) break;
+            tc_fence_after();
+            issue_scores(c1);
           }
         }
-        umma_commit(&bars[kSReady]);
-        umma_commit(&bars[kUpDone]);
-        if (kStateOnly) {
-          umma_commit(&bars[kEmpty0 + s]);
-          continue;
-        }
-        umma_commit(&bars[kQSDone]);
-        if (c + 1 < n_chunks) {
-          // buffer (c+1)&1 held P(c-1), consumed by P V of tile c-1 (done:
-          // its epilogue already released O)
-          if (!mbar_wait(&bars[kFull0 + ((c + 1) & 1)], ((c + 1) >> 1) & 1, abort_flag)) break;
+        if (c1 < n_chunks) {
+          // S^T may change once the snapshot of S_{c+1} has been read out
+          if (!mbar_wait(&bars[kPhiKReady0 + (c1 & 1)], (c1 >> 1) & 1, abort_flag)) break;
+          if (!kStateOnly && !mbar_wait(&bars[kSnapReady], c1 & 1, abort_flag)) break;
           tc_fence_after();
-          issue_scores(c + 1);
+          LA_TRACE_AT(0, c1, 0);
+          issue_update(c1);
+          if (kStateOnly) umma_commit(&bars[kEmpty0 + (c1 & 1)]);
         }
-        if (!mbar_wait(&bars[kPReady0 + s], (c >> 1) & 1, abort_flag)) break;
-        tc_fence_after();
-        LA_TRACE_AT(0, c, 1);
-        // O += P [V 1]: B = V (64 columns) with the ones block as its second
-        // 64-column block (LBO), so O[:, 64] also collects the row sum of P.
-#pragma unroll
-        for (int j = 0; j < kT / 16; ++j) {
-          const uint32_t b_addr = v_base + j * 2048;
-          const uint64_t db = make_sdesc(b_addr, a_ones - b_addr, 1024, kSwizzle128B);
-          umma_ts(tmem + kColO, tmem + kColSc + 128 * s + 8 * j, db, id_pv, 1u);
-        }
-        umma_commit(&bars[kOReady]);
-        umma_commit(&bars[kEmpty0 + s]);
-        LA_TRACE_AT(0, c, 2);
       }
       umma_commit(&bars[kDone]);
     }
   } else if (warp < kWarpPoly) {
     // ------------------------------------------------------------ features
     const int wq = warp & 3;
-    const int row = wq * 32 + lane;  // token within the tile
+    const int row = wq * 32 + lane;  // token within the tile == TMEM lane
     const bool leader = (warp == kWarpFeat && lane == 0);
     for (int c = 0; c < n_chunks; ++c) {
       const int s = c & 1;
@@ -403,24 +432,26 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       }
       named_barrier_sync(1, 128);
       if (leader) mbar_arrive(&bars[kEmpty0 + s]);
-      // phi(K) once the previous update has read the buffer
-      if (c > 0) mbar_wait(&bars[kUpDone], (c - 1) & 1, abort_flag);
+      // phi(K) into buffer c&1 once the update of tile c-2 has read it
+      if (c >= 2) mbar_wait(&bars[kUpDone0 + s], ((c >> 1) - 1) & 1, abort_flag);
       if (!wg_ok(1, abort_flag)) break;
       {
         FeatSrc fk;
 #pragma unroll
         for (int i = 0; i < 8; ++i) fk.raw[i] = vrow ? kw[i] : 0u;
         fk.one_valid = vrow ? 0x3F803F80u : 0u;  // padding tokens add nothing to the state
-        store_phi<false>(fk, sb + kOffPhiK, row, std::make_integer_sequence<int, kFPad / 8>{});
+        store_phi<false>(fk, sb + kOffPhiK + s * kPhiBytes, row,
+                         std::make_integer_sequence<int, kFPad / 8>{});
       }
       fence_proxy_async_smem();
       named_barrier_sync(1, 128);
-      if (leader) mbar_arrive(&bars[kPhiKReady]);
+      if (leader) mbar_arrive(&bars[kPhiKReady0 + s]);
       LA_TRACE_AT(1, c, 1);
       if (!kStateOnly) {
-        // phi(Q) once phi(Q) S of the previous tile has read the buffer
+        // phi(Q) -> TMEM once phi(Q) S of the previous tile has read it
         if (c > 0) mbar_wait(&bars[kQSDone], (c - 1) & 1, abort_flag);
         if (!wg_ok(1, abort_flag)) break;
+        tc_fence_after();
         FeatSrc fs;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -430,8 +461,9 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           fs.s32[i] = hmul2_bf16(qw[i], 0x3D003D00u);  // x / 32  (exact)
         }
         fs.one_valid = 0x3F803F80u;
-        store_phi<true>(fs, sb + kOffPhiQ, row, std::make_integer_sequence<int, kFPad / 8>{});
-        fence_proxy_async_smem();
+        store_phiq(fs, taddr(tmem, wq * 32, kColPhiQ), std::make_integer_sequence<int, kFPad / 32>{});
+        tmem_wait_st();
+        tc_fence_before();
         named_barrier_sync(1, 128);
         if (leader) mbar_arrive(&bars[kPhiQReady]);
         LA_TRACE_AT(1, c, 2);
@@ -446,12 +478,10 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       const uint64_t c32 = f2pack(0.03125f, 0.03125f), c4 = f2pack(0.25f, 0.25f);
       const uint64_t one2 = f2pack(1.f, 1.f);
       for (int c = 0; c < n_chunks; ++c) {
-        const int s = c & 1;
         const int64_t t0 = t_begin + (int64_t)c * kT;
         const int valid = (int)min64(kT, t_end - t0);
         const bool full_tile = valid == kT;
-        const uint32_t col0 = kColSc + 128 * s;
-        mbar_wait(&bars[kScReady0 + s], (c >> 1) & 1, abort_flag);
+        mbar_wait(&bars[kScReady], c & 1, abort_flag);
         if (!wg_ok(2, abort_flag)) break;
         tc_fence_after();
         LA_TRACE_AT(2, c, 0);
@@ -463,8 +493,8 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           uint32_t w[16];
           if (G <= wq) {
             uint32_t r[32];
-            tmem_ld16(taddr(tmem, wq * 32, col0 + 32 * G), r);
-            tmem_ld16(taddr(tmem, wq * 32, col0 + 32 * G + 16), r + 16);
+            tmem_ld16(taddr(tmem, wq * 32, kColSc + 32 * G), r);
+            tmem_ld16(taddr(tmem, wq * 32, kColSc + 32 * G + 16), r + 16);
             tmem_wait_ld();
             if (G < wq && full_tile) {
 #pragma unroll
@@ -490,12 +520,12 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           }
           // P columns [16G, 16G + 16) hold keys [32G, 32G + 32); those score
           // columns were read above (or are never needed)
-          tmem_st16(taddr(tmem, wq * 32, col0 + 16 * G), w);
+          tmem_st16(taddr(tmem, wq * 32, kColSc + 16 * G), w);
         }
         tmem_wait_st();
         tc_fence_before();
         named_barrier_sync(2, 128);
-        if (leader) mbar_arrive(&bars[kPReady0 + s]);
+        if (leader) mbar_arrive(&bars[kPReady]);
         LA_TRACE_AT(2, c, 1);
       }
     }
