@@ -267,11 +267,10 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   const int n_chunks = (int)((t_end - t_begin + kT - 1) / kT);
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars[kFull0], 1);
-    mbar_init(&bars[kFull1], 1);
-    mbar_init(&bars[kEmpty0], 2);
-    mbar_init(&bars[kEmpty1], 2);
-    for (int i = kPhiQReady; i < kNumBars; ++i) mbar_init(&bars[i], 1);
+    // every barrier: one arrival (a leader thread, a TMA expect-tx or a
+    // tcgen05.commit), except the TMA stage-empty pair (features + MMA)
+    for (int i = 0; i < kNumBars; ++i)
+      mbar_init(&bars[i], (i == kEmpty0 || i == kEmpty1) ? 2 : 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
