@@ -24,18 +24,21 @@
 //
 // Every M=128, K=16 tcgen05.mma costs about 100 cycles whatever its N up to
 // 160, so a tile is ~27 MMAs (~2,800 cycles) of tensor-pipe time.  The issue
-// order  UP(c), QS(c), PV(c), scores(c+1), UP(c+1), ...  keeps that pipe busy:
-// the state snapshot and phi(K) of tile c+1 are produced while QS(c) and PV(c)
-// run, phi(Q) of tile c+1 while PV(c) and UP(c+1) run, and P of tile c+1 while
-// UP(c+1) and QS(c+1) run.
+// issue cost of one MMA (~70 cycles) and of a tcgen05.commit (~140) is paid by
+// the issuing thread, so two threads issue: one the state updates UP(c), the
+// other QS(c), PV(c) and the scores of tile c+1.  The state snapshot and
+// phi(K) of tile c+1 are produced while QS(c) and PV(c) run, phi(Q) of tile
+// c+1 while PV(c) and UP(c+1) run, and P of tile c+1 while UP(c+1) and
+// QS(c+1) run.
 //
-// Warp roles (576 threads, one CTA per SM):
+// Warp roles (640 threads, one CTA per SM):
 //   warp 0      TMA producer (Q, K, V tiles; 2-stage ring)
-//   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2-5   features: phi(K) -> smem (2 buffers), phi(Q) -> TMEM
-//   warps 6-9   polynomial: scores -> P (TMEM)
-//   warps 10-13 state: S^T (TMEM, fp32) -> bf16 snapshot in smem (2 buffers)
-//   warps 14-17 epilogue: O (TMEM) -> normalised bf16 output rows
+//   warp 1      TMEM allocator + update MMA issuer (S^T += ...)
+//   warp 2      output MMA issuer (phi(Q) S, P [V 1], scores)
+//   warps 4-7   features: phi(K) -> smem (2 buffers), phi(Q) -> TMEM
+//   warps 8-11  polynomial: scores -> P (TMEM)
+//   warps 12-15 state: S^T (TMEM, fp32) -> bf16 snapshot in smem (2 buffers)
+//   warps 16-19 epilogue: O (TMEM) -> normalised bf16 output rows
 //
 // The state-only variant (kStateOnly) runs just the phi(K) / update path and
 // writes the segment's state; it seeds the later segments of a head.
@@ -57,9 +60,9 @@ constexpr int kFPad = 160;    // padded feature count (K of phi(Q) S, N of the u
 constexpr int kSV = kDv + 1;  // state columns in global memory: values + normaliser
 constexpr int kNO = 80;       // N of phi(Q) S: 64 values, normaliser, 15 zero rows
 
-constexpr int kWarpTma = 0, kWarpMma = 1, kWarpFeat = 2, kWarpPoly = 6, kWarpState = 10,
-              kWarpEpi = 14;
-constexpr int kThreads = 18 * 32;
+constexpr int kWarpTma = 0, kWarpUpd = 1, kWarpOut = 2, kWarpFeat = 4, kWarpPoly = 8,
+              kWarpState = 12, kWarpEpi = 16;
+constexpr int kThreads = 20 * 32;
 
 // TMEM columns (one CTA per SM owns all 512)
 constexpr uint32_t kColS = 0;       // S^T    128 lanes x 160 fp32
@@ -93,8 +96,8 @@ static_assert(kSmemAlloc <= 227 * 1024, "shared memory budget");
 // Barriers.  Per-buffer pairs (..0/..1) complete once per two tiles; a
 // producer that may run two tiles ahead of its consumer needs them.
 enum Bar { kFull0, kFull1, kEmpty0, kEmpty1, kPhiKReady0, kPhiKReady1, kUpDone0, kUpDone1,
-           kPhiQReady, kQSDone, kScReady, kPReady, kOReady, kOFree, kSReady, kSnapReady, kDone,
-           kNumBars };
+           kQSDone0, kQSDone1, kSnapReady0, kSnapReady1, kPhiQReady, kScReady, kPReady, kOReady,
+           kOFree, kSReady, kDone, kNumBars };
 
 // Optional per-role timeline of CTA (0, 0), compiled in with -DLA_TRACE only.
 #ifdef LA_TRACE
@@ -268,9 +271,14 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
 
   if (threadIdx.x == 0) {
     // every barrier: one arrival (a leader thread, a TMA expect-tx or a
-    // tcgen05.commit), except the TMA stage-empty pair (features + MMA)
-    for (int i = 0; i < kNumBars; ++i)
-      mbar_init(&bars[i], (i == kEmpty0 || i == kEmpty1) ? 2 : 1);
+    // tcgen05.commit), except: a TMA stage is released by the features, the
+    // update issuer and (full kernel) the output issuer; `done` by both issuers
+    for (int i = 0; i < kNumBars; ++i) {
+      uint32_t count = 1;
+      if (i == kEmpty0 || i == kEmpty1) count = kStateOnly ? 2 : 3;
+      if (i == kDone) count = 2;
+      mbar_init(&bars[i], count);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -281,7 +289,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     const uint32_t one = (byte == (row & 7) * 16) ? 0x3F80u : 0u;
     *(uint32_t *)(smem + kOffOnes + i * 4) = one;
   }
-  if (warp == kWarpMma) tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == kWarpUpd) tmem_alloc(tmem_slot, kTmemCols);
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -310,104 +318,99 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       for (int c = issued - 2 < 0 ? 0 : issued - 2; c < issued; ++c)
         wait_teardown(&bars[kFull0 + (c & 1)], (c >> 1) & 1);
     }
-  } else if (warp == kWarpMma) {
-    // ------------------------------------------------------------ MMA issuer
-    // Tensor-pipe order: UP(0), [sc(0)], then per tile c: QS(c), PV(c),
-    // sc(c+1), UP(c+1).
-    if (lane == 0) {
-      constexpr uint32_t id_sc = make_idesc_bf16(128, 128, false, false);
-      constexpr uint32_t id_qs = make_idesc_bf16(128, kNO, false, false);
-      constexpr uint32_t id_pv = make_idesc_bf16(128, kNO, false, true);
-      constexpr uint32_t id_up = make_idesc_bf16(128, kFPad, true, true);
-      const uint32_t a_ones = sb + kOffOnes;
-      const uint64_t qs_b_desc0 = make_sdesc(sb + kOffSnap, 16, 1024, kSwizzle128B);
-      const uint64_t qs_b_desc1 = make_sdesc(sb + kOffSnap + kSnapBytes, 16, 1024, kSwizzle128B);
-      // S^T += [V 1 0]^T phi(K) of tile c (8 K-steps of 16 tokens)
-      auto issue_update = [&](int c) {
+  } else if (warp == kWarpUpd || warp == kWarpOut) {
+    // ------------------------------------------------------------ MMA issuers
+    // Two threads issue into the same tensor pipe so each one's commits and
+    // waits hide behind the other's MMAs:
+    //   update issuer (warp 1): S^T += [V 1 0]^T phi(K) for every tile;
+    //   output issuer (warp 2): per tile O = phi(Q) S_c, O += P [V 1], then
+    //                           the scores of the next tile.
+    constexpr uint32_t id_sc = make_idesc_bf16(128, 128, false, false);
+    constexpr uint32_t id_qs = make_idesc_bf16(128, kNO, false, false);
+    constexpr uint32_t id_pv = make_idesc_bf16(128, kNO, false, true);
+    constexpr uint32_t id_up = make_idesc_bf16(128, kFPad, true, true);
+    // a K-step of 16 tokens: start address +2048 B, LBO (distance to the ones block) -2048 B
+    constexpr uint64_t kStep = (uint64_t)(2048 >> 4) - ((uint64_t)(2048 >> 4) << 16);
+    const uint32_t a_ones = sb + kOffOnes;
+    if (lane == 0 && warp == kWarpUpd) {
+      for (int c = 0; c < n_chunks; ++c) {
         const int b = c & 1;
+        if (!mbar_wait(&bars[kPhiKReady0 + b], (c >> 1) & 1, abort_flag)) break;
+        // S^T may change once the snapshot of S_c has been read out
+        if ((c == 0 || !kStateOnly) && !mbar_wait(&bars[kSnapReady0 + b], (c >> 1) & 1, abort_flag))
+          break;
+        tc_fence_after();
+        LA_TRACE_AT(0, c, 0);
         const uint32_t v_base = sb + kOffV + b * kVBytes;
         const uint64_t db0 = make_sdesc(sb + kOffPhiK + b * kPhiBytes, kPhiBlock, 1024, kSwizzle128B);
         const uint64_t da0 = make_sdesc(v_base, a_ones - v_base, 1024, kSwizzle128B);
-        // each step: start address +2048 B, LBO (distance to the ones block) -2048 B
-        constexpr uint64_t kStep = (uint64_t)(2048 >> 4) - ((uint64_t)(2048 >> 4) << 16);
 #pragma unroll
         for (int j = 0; j < kT / 16; ++j)
           umma_ss(tmem + kColS, da0 + kStep * j, db0 + (uint64_t)((j * 2048) >> 4), id_up, 1u);
         umma_commit(&bars[kSReady]);
         umma_commit(&bars[kUpDone0 + b]);
-      };
-      auto issue_scores = [&](int c) {
-        const int s = c & 1;
-        const uint64_t da = make_sdesc(sb + kOffQ + s * kQBytes, 16, 256, kSwizzle32B);
-        const uint64_t db = make_sdesc(sb + kOffK + s * kQBytes, 16, 256, kSwizzle32B);
-        umma_ss(tmem + kColSc, da, db, id_sc, 0);
-        umma_commit(&bars[kScReady]);
-      };
-      bool ok = mbar_wait(&bars[kSnapReady], 0, abort_flag)  // S_0 in TMEM (+ snapshot 0)
-                && mbar_wait(&bars[kPhiKReady0], 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        LA_TRACE_AT(0, 0, 0);
-        issue_update(0);
-        if (kStateOnly) umma_commit(&bars[kEmpty0]);
+        umma_commit(&bars[kEmpty0 + b]);
       }
-      if (!kStateOnly && ok) {
-        ok = mbar_wait(&bars[kFull0], 0, abort_flag);
+      umma_commit(&bars[kDone]);
+    } else if (lane == 0) {
+      if (!kStateOnly) {
+        const uint64_t qs_b_desc0 = make_sdesc(sb + kOffSnap, 16, 1024, kSwizzle128B);
+        const uint64_t qs_b_desc1 = make_sdesc(sb + kOffSnap + kSnapBytes, 16, 1024, kSwizzle128B);
+        auto issue_scores = [&](int c) {
+          const int s = c & 1;
+          const uint64_t da = make_sdesc(sb + kOffQ + s * kQBytes, 16, 256, kSwizzle32B);
+          const uint64_t db = make_sdesc(sb + kOffK + s * kQBytes, 16, 256, kSwizzle32B);
+          umma_ss(tmem + kColSc, da, db, id_sc, 0);
+          umma_commit(&bars[kScReady]);
+        };
+        bool ok = mbar_wait(&bars[kFull0], 0, abort_flag);
         if (ok) {
           tc_fence_after();
           issue_scores(0);
         }
-      }
-      for (int c = 0; ok && c < n_chunks; ++c) {
-        const int s = c & 1;
-        const int c1 = c + 1;
-        if (!kStateOnly) {
-          // O = phi(Q) S_c   (K = 160 features in 10 steps; S_c is snapshot c&1)
+        for (int c = 0; ok && c < n_chunks; ++c) {
+          const int b = c & 1;
+          // O = phi(Q) S_c   (K = 160 features in 10 steps; S_c is snapshot b)
           if (!mbar_wait(&bars[kPhiQReady], c & 1, abort_flag)) break;
+          if (!mbar_wait(&bars[kSnapReady0 + b], (c >> 1) & 1, abort_flag)) break;
           if (c > 0 && !mbar_wait(&bars[kOFree], (c - 1) & 1, abort_flag)) break;
           tc_fence_after();
           LA_TRACE_AT(0, c, 1);
-          const uint64_t qs_b_desc = (c & 1) ? qs_b_desc1 : qs_b_desc0;
+          const uint64_t qs_b_desc = b ? qs_b_desc1 : qs_b_desc0;
 #pragma unroll
           for (int j = 0; j < kFPad / 16; ++j) {
             const uint32_t boff = (j >> 2) * kSnapKBlock + (j & 3) * 32;
             umma_ts(tmem + kColO, tmem + kColPhiQ + 8 * j, qs_b_desc + (boff >> 4), id_qs,
                     j > 0 ? 1u : 0u);
           }
-          umma_commit(&bars[kQSDone]);
+          umma_commit(&bars[kQSDone0 + b]);
           // O += P [V 1]: B = V (64 columns) with the ones block as its second
           // 64-column block (LBO), so O[:, 64] also collects the row sum of P.
           if (!mbar_wait(&bars[kPReady], c & 1, abort_flag)) break;
           tc_fence_after();
           LA_TRACE_AT(0, c, 2);
-          const uint32_t v_base = sb + kOffV + s * kVBytes;
+          const uint32_t v_base = sb + kOffV + b * kVBytes;
           const uint64_t db0 = make_sdesc(v_base, a_ones - v_base, 1024, kSwizzle128B);
-          constexpr uint64_t kStep = (uint64_t)(2048 >> 4) - ((uint64_t)(2048 >> 4) << 16);
 #pragma unroll
           for (int j = 0; j < kT / 16; ++j)
             umma_ts(tmem + kColO, tmem + kColSc + 8 * j, db0 + kStep * j, id_pv, 1u);
           umma_commit(&bars[kOReady]);
-          umma_commit(&bars[kEmpty0 + s]);
-          if (c1 < n_chunks) {
-            // scores of tile c+1 overwrite P(c): wait for P V to finish
-            if (!mbar_wait(&bars[kFull0 + (c1 & 1)], (c1 >> 1) & 1, abort_flag)) break;
-            if (!mbar_wait(&bars[kOReady], c & 1, abort_flag)) break;
+          // the scores of tile c+1 overwrite P(c): wait for P V to finish;
+          // that also ends this issuer's use of TMA stage b
+          if (!mbar_wait(&bars[kOReady], c & 1, abort_flag)) break;
+          mbar_arrive(&bars[kEmpty0 + b]);
+          LA_TRACE_AT(0, c, 3);
+          if (c + 1 < n_chunks) {
+            if (!mbar_wait(&bars[kFull0 + ((c + 1) & 1)], ((c + 1) >> 1) & 1, abort_flag)) break;
             tc_fence_after();
-            issue_scores(c1);
+            issue_scores(c + 1);
           }
-        }
-        if (c1 < n_chunks) {
-          // S^T may change once the snapshot of S_{c+1} has been read out
-          if (!mbar_wait(&bars[kPhiKReady0 + (c1 & 1)], (c1 >> 1) & 1, abort_flag)) break;
-          if (!kStateOnly && !mbar_wait(&bars[kSnapReady], c1 & 1, abort_flag)) break;
-          tc_fence_after();
-          LA_TRACE_AT(0, c1, 0);
-          issue_update(c1);
-          if (kStateOnly) umma_commit(&bars[kEmpty0 + (c1 & 1)]);
         }
       }
       umma_commit(&bars[kDone]);
     }
+  } else if (warp < kWarpFeat) {
+    // warp 3 has no role; it only joins the final CTA barrier
   } else if (warp < kWarpPoly) {
     // ------------------------------------------------------------ features
     const int wq = warp & 3;
@@ -448,7 +451,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       LA_TRACE_AT(1, c, 1);
       if (!kStateOnly) {
         // phi(Q) -> TMEM once phi(Q) S of the previous tile has read it
-        if (c > 0) mbar_wait(&bars[kQSDone], (c - 1) & 1, abort_flag);
+        if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
         if (!wg_ok(1, abort_flag)) break;
         tc_fence_after();
         FeatSrc fs;
@@ -569,7 +572,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     fence_proxy_async_smem();
     tc_fence_before();
     named_barrier_sync(3, 128);
-    if (leader) mbar_arrive(&bars[kSnapReady]);
+    if (leader) mbar_arrive(&bars[kSnapReady0]);
 
     if (kStateOnly) {
       // the segment's state, once every update has completed
@@ -591,7 +594,10 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     } else {
       const bool write_final = p.final_state != nullptr && g == p.segments - 1;
       for (int c = 0; c < n_chunks; ++c) {
+        // S^T holds S_{c+1} once the update of tile c is done; its snapshot
+        // goes to buffer (c+1)&1, last read by phi(Q) S of tile c-1
         mbar_wait(&bars[kSReady], c & 1, abort_flag);
+        if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
         if (!wg_ok(3, abort_flag)) break;
         tc_fence_after();
         LA_TRACE_AT(3, c, 0);
@@ -631,7 +637,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         fence_proxy_async_smem();
         tc_fence_before();
         named_barrier_sync(3, 128);
-        if (leader) mbar_arrive(&bars[kSnapReady]);
+        if (leader) mbar_arrive(&bars[kSnapReady0 + ((c + 1) & 1)]);
         LA_TRACE_AT(3, c, 1);
       }
     }
@@ -655,6 +661,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         tc_fence_before();
         named_barrier_sync(4, 128);
         if (leader) mbar_arrive(&bars[kOFree]);  // O is in registers: TMEM O reusable
+        LA_TRACE_AT(4, c, 1);
         // O[:, 64] = phi(q).z + rowsum(P): the full denominator before eps
         const float den = __uint_as_float(o[kDv]) + p.eps;
         const float inv = p.normalize ? 1.f / den : 1.f;
@@ -671,7 +678,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
             *(uint4 *)(orow + 8 * G) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
-        LA_TRACE_AT(4, c, 1);
+        LA_TRACE_AT(4, c, 2);
       }
     }
   }
@@ -679,7 +686,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
-  if (warp == kWarpMma) {
+  if (warp == kWarpUpd) {
     if (lane == 0) wait_teardown(&bars[kDone], 0);
     __syncwarp();
     tc_fence_after();
