@@ -31,14 +31,14 @@
 // c+1 while PV(c) and UP(c+1) run, and P of tile c+1 while UP(c+1) and
 // QS(c+1) run.
 //
-// Warp roles (640 threads, one CTA per SM):
+// Warp roles (768 threads, one CTA per SM):
 //   warp 0      TMA producer (Q, K, V tiles; 2-stage ring)
 //   warp 1      TMEM allocator + update MMA issuer (S^T += ...)
 //   warp 2      output MMA issuer (phi(Q) S, P [V 1], scores)
 //   warps 4-7   features: phi(K) -> smem (2 buffers), phi(Q) -> TMEM
-//   warps 8-11  polynomial: scores -> P (TMEM)
-//   warps 12-15 state: S^T (TMEM, fp32) -> bf16 snapshot in smem (2 buffers)
-//   warps 16-19 epilogue: O (TMEM) -> normalised bf16 output rows
+//   warps 8-15  polynomial: scores -> P (TMEM); two warps per TMEM lane quarter
+//   warps 16-19 state: S^T (TMEM, fp32) -> bf16 snapshot in smem (2 buffers)
+//   warps 20-23 epilogue: O (TMEM) -> normalised bf16 output rows
 //
 // The state-only variant (kStateOnly) runs just the phi(K) / update path and
 // writes the segment's state; it seeds the later segments of a head.
@@ -61,8 +61,8 @@ constexpr int kSV = kDv + 1;  // state columns in global memory: values + normal
 constexpr int kNO = 80;       // N of phi(Q) S: 64 values, normaliser, 15 zero rows
 
 constexpr int kWarpTma = 0, kWarpUpd = 1, kWarpOut = 2, kWarpFeat = 4, kWarpPoly = 8,
-              kWarpState = 12, kWarpEpi = 16;
-constexpr int kThreads = 20 * 32;
+              kWarpState = 16, kWarpEpi = 20;
+constexpr int kThreads = 24 * 32;
 
 // TMEM columns (one CTA per SM owns all 512)
 constexpr uint32_t kColS = 0;       // S^T    128 lanes x 160 fp32
@@ -474,7 +474,8 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   } else if (warp < kWarpState) {
     // ------------------------------------------------------------ polynomial
     if (!kStateOnly) {
-      const int wq = warp & 3;
+      const int wq = warp & 3;              // TMEM lane quarter: query rows 32wq ..
+      const int half = (warp - kWarpPoly) >> 2;  // this warp's key groups: G = half, half + 2
       const int row = wq * 32 + lane;
       const bool leader = (warp == kWarpPoly && lane == 0);
       const uint64_t c32 = f2pack(0.03125f, 0.03125f), c4 = f2pack(0.25f, 0.25f);
@@ -484,14 +485,15 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         const int valid = (int)min64(kT, t_end - t0);
         const bool full_tile = valid == kT;
         mbar_wait(&bars[kScReady], c & 1, abort_flag);
-        if (!wg_ok(2, abort_flag)) break;
+        if (!wg_ok(2, abort_flag, 256)) break;
         tc_fence_after();
         LA_TRACE_AT(2, c, 0);
         // P = tril(1 + s/4 + s^2/32) for raw scores s = q.k (d = 16).  Key group
         // G (32 keys) lies below the diagonal for this warp's rows when G < wq,
         // holds the diagonal when G == wq and is all zero when G > wq.
 #pragma unroll
-        for (int G = 0; G < 4; ++G) {
+        for (int G2 = 0; G2 < 2; ++G2) {
+          const int G = 2 * G2 + half;
           uint32_t w[16];
           if (G <= wq) {
             uint32_t r[32];
@@ -520,13 +522,18 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
 #pragma unroll
             for (int i = 0; i < 16; ++i) w[i] = 0u;
           }
-          // P columns [16G, 16G + 16) hold keys [32G, 32G + 32); those score
-          // columns were read above (or are never needed)
+          // P columns [16G, 16G + 16) hold keys [32G, 32G + 32).  They
+          // overwrite score columns [16G, 16G + 16), i.e. keys of group G/2,
+          // which the other warp of this quarter may still be reading: store
+          // only after both warps have loaded their groups (barrier below).
+          if (G2 == 0) {
+            named_barrier_sync(5 + wq, 64);
+          }
           tmem_st16(taddr(tmem, wq * 32, kColSc + 16 * G), w);
         }
         tmem_wait_st();
         tc_fence_before();
-        named_barrier_sync(2, 128);
+        named_barrier_sync(2, 256);
         if (leader) mbar_arrive(&bars[kPReady]);
         LA_TRACE_AT(2, c, 1);
       }
@@ -654,28 +661,33 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         if (!wg_ok(4, abort_flag)) break;
         tc_fence_after();
         LA_TRACE_AT(4, c, 0);
-        uint32_t o[kNO];
-#pragma unroll
-        for (int G = 0; G < kNO / 16; ++G) tmem_ld16(taddr(tmem, wq * 32, kColO + 16 * G), o + 16 * G);
+        // the denominator column first, then the values 16 columns at a time
+        uint32_t dr[16];
+        tmem_ld16(taddr(tmem, wq * 32, kColO + kDv), dr);
         tmem_wait_ld();
-        tc_fence_before();
-        named_barrier_sync(4, 128);
-        if (leader) mbar_arrive(&bars[kOFree]);  // O is in registers: TMEM O reusable
-        LA_TRACE_AT(4, c, 1);
         // O[:, 64] = phi(q).z + rowsum(P): the full denominator before eps
-        const float den = __uint_as_float(o[kDv]) + p.eps;
+        const float den = __uint_as_float(dr[0]) + p.eps;
         const float inv = p.normalize ? 1.f / den : 1.f;
         const uint64_t inv2 = f2pack(inv, inv);
-        if (row < valid) {
-          __nv_bfloat16 *orow = p.out + ((uint64_t)bh * p.n + t0 + row) * kDv;
+        __nv_bfloat16 *orow = p.out + ((uint64_t)bh * p.n + t0 + row) * kDv;
 #pragma unroll
-          for (int G = 0; G < kDv / 8; ++G) {
-            uint32_t w[4];
+        for (int G = 0; G < kDv / 16; ++G) {
+          uint32_t o[16];
+          tmem_ld16(taddr(tmem, wq * 32, kColO + 16 * G), o);
+          tmem_wait_ld();
+          if (G == kDv / 16 - 1) {
+            tc_fence_before();
+            named_barrier_sync(4, 128);
+            if (leader) mbar_arrive(&bars[kOFree]);  // O is in registers: TMEM O reusable
+            LA_TRACE_AT(4, c, 1);
+          }
+          uint32_t w[8];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              w[i] = pack_bf16x2(fmul2(f2pack(__uint_as_float(o[8 * G + 2 * i]),
-                                              __uint_as_float(o[8 * G + 2 * i + 1])), inv2));
-            *(uint4 *)(orow + 8 * G) = make_uint4(w[0], w[1], w[2], w[3]);
+          for (int i = 0; i < 8; ++i)
+            w[i] = pack_bf16x2(fmul2(f2pack(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), inv2));
+          if (row < valid) {
+            *(uint4 *)(orow + 16 * G) = make_uint4(w[0], w[1], w[2], w[3]);
+            *(uint4 *)(orow + 16 * G + 8) = make_uint4(w[4], w[5], w[6], w[7]);
           }
         }
         LA_TRACE_AT(4, c, 2);

@@ -97,8 +97,8 @@ __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
 // Warpgroup-uniform continuation check after a wait: every thread of the
 // group reaches the barrier, then all see the same abort flag, so no thread
 // is left waiting at a later barrier for peers that already gave up.
-__device__ __forceinline__ bool wg_ok(int id, volatile int *abort_flag) {
-  named_barrier_sync(id, 128);
+__device__ __forceinline__ bool wg_ok(int id, volatile int *abort_flag, int nthreads = 128) {
+  named_barrier_sync(id, nthreads);
   return *abort_flag == 0;
 }
 
