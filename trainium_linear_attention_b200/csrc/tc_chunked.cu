@@ -31,14 +31,15 @@
 // c+1 while PV(c) and UP(c+1) run, and P of tile c+1 while UP(c+1) and
 // QS(c+1) run.
 //
-// Warp roles (768 threads, one CTA per SM):
+// Warp roles (896 threads, one CTA per SM):
 //   warp 0      TMA producer (Q, K, V tiles; 2-stage ring)
 //   warp 1      TMEM allocator + update MMA issuer (S^T += ...)
 //   warp 2      output MMA issuer (phi(Q) S, P [V 1], scores)
 //   warps 4-7   features: phi(K) -> smem (2 buffers), phi(Q) -> TMEM
 //   warps 8-15  polynomial: scores -> P (TMEM); two warps per TMEM lane quarter
-//   warps 16-19 state: S^T (TMEM, fp32) -> bf16 snapshot in smem (2 buffers)
-//   warps 20-23 epilogue: O (TMEM) -> normalised bf16 output rows
+//   warps 16-23 state: S^T (TMEM, fp32) -> bf16 snapshot in smem (2 buffers);
+//               two warps per lane quarter, 80 feature columns each
+//   warps 24-27 epilogue: O (TMEM) -> normalised bf16 output rows
 //
 // The state-only variant (kStateOnly) runs just the phi(K) / update path and
 // writes the segment's state; it seeds the later segments of a head.
@@ -61,8 +62,8 @@ constexpr int kSV = kDv + 1;  // state columns in global memory: values + normal
 constexpr int kNO = 80;       // N of phi(Q) S: 64 values, normaliser, 15 zero rows
 
 constexpr int kWarpTma = 0, kWarpUpd = 1, kWarpOut = 2, kWarpFeat = 4, kWarpPoly = 8,
-              kWarpState = 16, kWarpEpi = 20;
-constexpr int kThreads = 24 * 32;
+              kWarpState = 16, kWarpEpi = 24;
+constexpr int kThreads = 28 * 32;
 
 // TMEM columns (one CTA per SM owns all 512)
 constexpr uint32_t kColS = 0;       // S^T    128 lanes x 160 fp32
@@ -260,6 +261,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   uint64_t *bars = (uint64_t *)(smem + kOffBar);
   uint32_t *tmem_slot = (uint32_t *)(smem + kOffBar + 8 * kNumBars);
   volatile int *abort_flag = (volatile int *)(smem + kOffBar + 8 * kNumBars + 4);
+  volatile int *up_issued = (volatile int *)(smem + kOffBar + 8 * kNumBars + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -280,6 +282,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       mbar_init(&bars[i], count);
     }
     *abort_flag = 0;
+    *up_issued = 0;
     fence_barrier_init();
   }
   // constant "ones" block: A-operand rows 64..127 of [V 1 0]^T for 16 tokens;
@@ -350,6 +353,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         umma_commit(&bars[kSReady]);
         umma_commit(&bars[kUpDone0 + b]);
         umma_commit(&bars[kEmpty0 + b]);
+        *up_issued = c + 1;  // the state update of tile c is in the pipe
       }
       umma_commit(&bars[kDone]);
     } else if (lane == 0) {
@@ -374,6 +378,9 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           if (!mbar_wait(&bars[kPhiQReady], c & 1, abort_flag)) break;
           if (!mbar_wait(&bars[kSnapReady0 + b], (c >> 1) & 1, abort_flag)) break;
           if (c > 0 && !mbar_wait(&bars[kOFree], (c - 1) & 1, abort_flag)) break;
+          // let the update of tile c enter the pipe first: the next snapshot,
+          // and so the next tile, waits on it
+          if (!spin_until_at_least(up_issued, c + 1, abort_flag)) break;
           tc_fence_after();
           LA_TRACE_AT(0, c, 1);
           const uint64_t qs_b_desc = b ? qs_b_desc1 : qs_b_desc0;
@@ -541,15 +548,20 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   } else if (warp < kWarpEpi) {
     // ------------------------------------------------------------ state
     const int wq = warp & 3;
+    const int half = (warp - kWarpState) >> 2;
     const int e = wq * 32 + lane;  // row of S^T: value column e (< 64), normaliser (64)
+    const int col0 = 80 * half;    // this warp's 80 feature columns
     const bool leader = (warp == kWarpState && lane == 0);
     const bool real = e < kSV;
-    // S_0 = init_state + states of the earlier segments (fixed order)
-    for (int grp = 0; grp < kFPad / 16; ++grp) {
+    // S_0 = init_state + states of the earlier segments (fixed order).  Rows
+    // 65..79 of both snapshot buffers are zero for good (S^T rows >= 65 never
+    // change: their rows of [V 1 0]^T are zero).
+    for (int grp = 0; grp < 5; ++grp) {
+      const int f0 = col0 + 16 * grp;
       uint32_t w[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const int f = 16 * grp + i;
+        const int f = f0 + i;
         float x = 0.f;
         if (!kStateOnly && real && f < kF) {
           if (p.init_state) x = p.init_state[((uint64_t)bh * kF + f) * kSV + e];
@@ -558,92 +570,103 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         }
         w[i] = __float_as_uint(x);
       }
-      tmem_st16(taddr(tmem, wq * 32, kColS + 16 * grp), w);
+      tmem_st16(taddr(tmem, wq * 32, kColS + f0), w);
       if (!kStateOnly && e < kNO) {
-        const uint32_t snap = sb + kOffSnap;  // buffer 0
-        const int f0 = 16 * grp;
-        const uint32_t blk = snap + (f0 >> 6) * kSnapKBlock;
-        st_shared_v4(blk + sw128_offset(e, (f0 & 63) >> 3),
-                     pack_bf16(__uint_as_float(w[0]), __uint_as_float(w[1])),
-                     pack_bf16(__uint_as_float(w[2]), __uint_as_float(w[3])),
-                     pack_bf16(__uint_as_float(w[4]), __uint_as_float(w[5])),
-                     pack_bf16(__uint_as_float(w[6]), __uint_as_float(w[7])));
-        st_shared_v4(blk + sw128_offset(e, ((f0 & 63) >> 3) + 1),
-                     pack_bf16(__uint_as_float(w[8]), __uint_as_float(w[9])),
-                     pack_bf16(__uint_as_float(w[10]), __uint_as_float(w[11])),
-                     pack_bf16(__uint_as_float(w[12]), __uint_as_float(w[13])),
-                     pack_bf16(__uint_as_float(w[14]), __uint_as_float(w[15])));
+#pragma unroll
+        for (int buf = 0; buf < 2; ++buf) {
+          if (buf == 1 && e <= kDv) continue;  // buffer 1: only the zero rows now
+          const uint32_t blk = sb + kOffSnap + buf * kSnapBytes + (f0 >> 6) * kSnapKBlock;
+          const int ch = (f0 & 63) >> 3;
+          st_shared_v4(blk + sw128_offset(e, ch),
+                       pack_bf16(__uint_as_float(w[0]), __uint_as_float(w[1])),
+                       pack_bf16(__uint_as_float(w[2]), __uint_as_float(w[3])),
+                       pack_bf16(__uint_as_float(w[4]), __uint_as_float(w[5])),
+                       pack_bf16(__uint_as_float(w[6]), __uint_as_float(w[7])));
+          st_shared_v4(blk + sw128_offset(e, ch + 1),
+                       pack_bf16(__uint_as_float(w[8]), __uint_as_float(w[9])),
+                       pack_bf16(__uint_as_float(w[10]), __uint_as_float(w[11])),
+                       pack_bf16(__uint_as_float(w[12]), __uint_as_float(w[13])),
+                       pack_bf16(__uint_as_float(w[14]), __uint_as_float(w[15])));
+        }
       }
     }
     tmem_wait_st();
     fence_proxy_async_smem();
     tc_fence_before();
-    named_barrier_sync(3, 128);
+    named_barrier_sync(3, 256);
     if (leader) mbar_arrive(&bars[kSnapReady0]);
 
     if (kStateOnly) {
       // the segment's state, once every update has completed
       mbar_wait(&bars[kDone], 0, abort_flag);
-      if (wg_ok(3, abort_flag)) {
+      if (wg_ok(3, abort_flag, 256)) {
         tc_fence_after();
         float *dst = p.seg_out + ((uint64_t)bh * p.segments + g) * kF * kSV;
-        for (int grp = 0; grp < kFPad / 16; ++grp) {
+        for (int grp = 0; grp < 5; ++grp) {
           uint32_t r[16];
-          tmem_ld16(taddr(tmem, wq * 32, kColS + 16 * grp), r);
+          tmem_ld16(taddr(tmem, wq * 32, kColS + col0 + 16 * grp), r);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int f = 16 * grp + i;
+            const int f = col0 + 16 * grp + i;
             if (real && f < kF) dst[(uint64_t)f * kSV + e] = __uint_as_float(r[i]);
           }
         }
       }
     } else {
       const bool write_final = p.final_state != nullptr && g == p.segments - 1;
+      // snapshot a group of 16 columns of row e (rows <= 64 carry data)
+      auto put = [&](uint32_t snap, int f0, const uint32_t *r) {
+        if (e <= kDv) {
+          const uint32_t blk = snap + (f0 >> 6) * kSnapKBlock;
+          const int ch = (f0 & 63) >> 3;
+          st_shared_v4(blk + sw128_offset(e, ch),
+                       pack_bf16(__uint_as_float(r[0]), __uint_as_float(r[1])),
+                       pack_bf16(__uint_as_float(r[2]), __uint_as_float(r[3])),
+                       pack_bf16(__uint_as_float(r[4]), __uint_as_float(r[5])),
+                       pack_bf16(__uint_as_float(r[6]), __uint_as_float(r[7])));
+          st_shared_v4(blk + sw128_offset(e, ch + 1),
+                       pack_bf16(__uint_as_float(r[8]), __uint_as_float(r[9])),
+                       pack_bf16(__uint_as_float(r[10]), __uint_as_float(r[11])),
+                       pack_bf16(__uint_as_float(r[12]), __uint_as_float(r[13])),
+                       pack_bf16(__uint_as_float(r[14]), __uint_as_float(r[15])));
+        }
+      };
+      auto put_final = [&](int f0, const uint32_t *r) {
+        float *dst = p.final_state + (uint64_t)bh * kF * kSV;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (real && f0 + i < kF) dst[(uint64_t)(f0 + i) * kSV + e] = __uint_as_float(r[i]);
+      };
       for (int c = 0; c < n_chunks; ++c) {
         // S^T holds S_{c+1} once the update of tile c is done; its snapshot
         // goes to buffer (c+1)&1, last read by phi(Q) S of tile c-1
         mbar_wait(&bars[kSReady], c & 1, abort_flag);
         if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
-        if (!wg_ok(3, abort_flag)) break;
+        if (!wg_ok(3, abort_flag, 256)) break;
         tc_fence_after();
         LA_TRACE_AT(3, c, 0);
-        const bool last = c == n_chunks - 1;
+        const bool last = write_final && c == n_chunks - 1;
         const uint32_t snap = sb + kOffSnap + ((c + 1) & 1) * kSnapBytes;
-        // rows >= 80 are not part of the snapshot; their warp only joins the barriers
-        if (wq < 3) {
+        if (wq < 3) {  // rows 96..127 carry nothing
+          // five 16-column groups; each group's load overlaps the stores of
+          // the previous one
+          uint32_t r0[16], r1[16];
+          const uint32_t base = taddr(tmem, wq * 32, kColS + col0);
+          tmem_ld16(base, r0);
 #pragma unroll
-          for (int B = 0; B < 3; ++B) {  // 64 + 64 + 32 feature columns
-            const int cols = B < 2 ? 64 : 32;
-            uint32_t r[64];
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4)
-              if (16 * q4 < cols) tmem_ld16(taddr(tmem, wq * 32, kColS + 64 * B + 16 * q4), r + 16 * q4);
+          for (int grp = 0; grp < 5; ++grp) {
+            uint32_t *cur = (grp & 1) ? r1 : r0;
+            uint32_t *nxt = (grp & 1) ? r0 : r1;
             tmem_wait_ld();
-            if (e < kNO) {
-              const uint32_t blk = snap + B * kSnapKBlock;
-#pragma unroll
-              for (int ch = 0; ch < 8; ++ch)
-                if (ch < cols / 8)
-                  st_shared_v4(blk + sw128_offset(e, ch),
-                               pack_bf16(__uint_as_float(r[8 * ch + 0]), __uint_as_float(r[8 * ch + 1])),
-                               pack_bf16(__uint_as_float(r[8 * ch + 2]), __uint_as_float(r[8 * ch + 3])),
-                               pack_bf16(__uint_as_float(r[8 * ch + 4]), __uint_as_float(r[8 * ch + 5])),
-                               pack_bf16(__uint_as_float(r[8 * ch + 6]), __uint_as_float(r[8 * ch + 7])));
-            }
-            if (last && write_final && real) {
-              float *dst = p.final_state + (uint64_t)bh * kF * kSV;
-#pragma unroll
-              for (int i = 0; i < 64; ++i) {
-                const int f = 64 * B + i;
-                if (i < cols && f < kF) dst[(uint64_t)f * kSV + e] = __uint_as_float(r[i]);
-              }
-            }
+            if (grp + 1 < 5) tmem_ld16(base + 16 * (grp + 1), nxt);
+            put(snap, col0 + 16 * grp, cur);
+            if (last) put_final(col0 + 16 * grp, cur);
           }
         }
         fence_proxy_async_smem();
         tc_fence_before();
-        named_barrier_sync(3, 128);
+        named_barrier_sync(3, 256);
         if (leader) mbar_arrive(&bars[kSnapReady0 + ((c + 1) & 1)]);
         LA_TRACE_AT(3, c, 1);
       }

@@ -81,6 +81,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   return true;
 }
 
+// Bounded spin until a shared counter written by another thread of the CTA
+// reaches `target`.  Returns false on abort or timeout (flag raised).
+__device__ __forceinline__ bool spin_until_at_least(volatile int *counter, int target,
+                                                    volatile int *abort_flag) {
+  if (*counter >= target) return true;
+  const uint64_t t0 = globaltimer();
+  uint32_t spins = 0;
+  while (*counter < target) {
+    if ((++spins & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kWaitTimeoutNs) {
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
 // ------------------------------------------------------------------- fences ---
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
