@@ -32,7 +32,8 @@
 // QS(c+1) run.
 //
 // Warp roles (896 threads, one CTA per SM):
-//   warp 0      TMA producer (Q, K, V tiles; 2-stage ring)
+//   warp 0      TMA producer: Q/K tiles (3-stage ring)
+//   warp 3      TMA producer: V tiles (2-stage ring)
 //   warp 1      TMEM allocator + update MMA issuer (S^T += ...)
 //   warp 2      output MMA issuer (phi(Q) S, P [V 1], scores)
 //   warps 4-7   features: phi(K) -> smem (2 buffers), phi(Q) -> TMEM
@@ -61,7 +62,7 @@ constexpr int kFPad = 160;    // padded feature count (K of phi(Q) S, N of the u
 constexpr int kSV = kDv + 1;  // state columns in global memory: values + normaliser
 constexpr int kNO = 80;       // N of phi(Q) S: 64 values, normaliser, 15 zero rows
 
-constexpr int kWarpTma = 0, kWarpUpd = 1, kWarpOut = 2, kWarpFeat = 4, kWarpPoly = 8,
+constexpr int kWarpTma = 0, kWarpUpd = 1, kWarpOut = 2, kWarpTmaV = 3, kWarpFeat = 4, kWarpPoly = 8,
               kWarpState = 16, kWarpEpi = 24;
 constexpr int kThreads = 28 * 32;
 
@@ -75,17 +76,19 @@ constexpr uint32_t kTmemCols = 512;
 // Shared memory (offsets from a 1024-byte aligned base)
 constexpr uint32_t kQBytes = kT * kDqk * 2;         // 4 KB, 32B-swizzled rows
 constexpr uint32_t kVBytes = kT * kDv * 2;          // 16 KB, 128B-swizzled rows
-constexpr uint32_t kOffQ = 0;                       // 2 stages
-constexpr uint32_t kOffK = kOffQ + 2 * kQBytes;
-constexpr uint32_t kOffV = kOffK + 2 * kQBytes;     // 16384
-constexpr uint32_t kOffOnes = kOffV + 2 * kVBytes;  // 49152: 16 rows x 128 B
+constexpr int kQKStages = 3;                        // Q/K ring
+constexpr int kVStages = 2;                         // V ring
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffK = kOffQ + kQKStages * kQBytes;
+constexpr uint32_t kOffV = kOffK + kQKStages * kQBytes;     // 24576
+constexpr uint32_t kOffOnes = kOffV + kVStages * kVBytes;   // 57344: 16 rows x 128 B
 constexpr uint32_t kPhiBlock = kT * 128;            // 64 features of 128 tokens
 constexpr uint32_t kPhiBytes = 3 * kPhiBlock;       // 160 features (3 blocks)
-constexpr uint32_t kOffPhiK = kOffOnes + 2048;      // 51200: 2 buffers
-constexpr uint32_t kOffSnap = kOffPhiK + 2 * kPhiBytes;  // 149504: 2 x 30 KB
+constexpr uint32_t kOffPhiK = kOffOnes + 2048;      // 59392: 2 buffers
+constexpr uint32_t kOffSnap = kOffPhiK + 2 * kPhiBytes;  // 157696: 2 x 30 KB
 constexpr uint32_t kSnapKBlock = kNO * 128;         // 10 KB per 64-feature block
 constexpr uint32_t kSnapBytes = 3 * kSnapKBlock;
-constexpr uint32_t kOffBar = kOffSnap + 2 * kSnapBytes;  // 210944
+constexpr uint32_t kOffBar = kOffSnap + 2 * kSnapBytes;  // 219136
 constexpr uint32_t kSmemBytes = kOffBar + 256;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;       // alignment slack
 
@@ -96,7 +99,8 @@ static_assert(kSmemAlloc <= 227 * 1024, "shared memory budget");
 
 // Barriers.  Per-buffer pairs (..0/..1) complete once per two tiles; a
 // producer that may run two tiles ahead of its consumer needs them.
-enum Bar { kFull0, kFull1, kEmpty0, kEmpty1, kPhiKReady0, kPhiKReady1, kUpDone0, kUpDone1,
+enum Bar { kQKFull0, kQKFull1, kQKFull2, kQKEmpty0, kQKEmpty1, kQKEmpty2, kVFull0, kVFull1,
+           kVEmpty0, kVEmpty1, kPhiKReady0, kPhiKReady1, kUpDone0, kUpDone1,
            kQSDone0, kQSDone1, kSnapReady0, kSnapReady1, kPhiQReady, kScReady, kPReady, kOReady,
            kOFree, kSReady, kDone, kNumBars };
 
@@ -273,11 +277,13 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
 
   if (threadIdx.x == 0) {
     // every barrier: one arrival (a leader thread, a TMA expect-tx or a
-    // tcgen05.commit), except: a TMA stage is released by the features, the
-    // update issuer and (full kernel) the output issuer; `done` by both issuers
+    // tcgen05.commit), except: a Q/K stage is released by the features and
+    // (full kernel) the scores MMA, a V stage by the update and (full kernel)
+    // P V, `done` by both MMA issuers
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t count = 1;
-      if (i == kEmpty0 || i == kEmpty1) count = kStateOnly ? 2 : 3;
+      if (i >= kQKEmpty0 && i <= kQKEmpty2) count = kStateOnly ? 1 : 2;
+      if (i == kVEmpty0 || i == kVEmpty1) count = kStateOnly ? 1 : 2;
       if (i == kDone) count = 2;
       mbar_init(&bars[i], count);
     }
@@ -299,27 +305,41 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kWarpTma) {
-    // ------------------------------------------------------------ TMA producer
+  if (warp == kWarpTma || warp == kWarpTmaV) {
+    // ------------------------------------------------------------ TMA producers
+    // warp 0 streams the Q/K tiles (3 stages), warp 3 the V tiles (2 stages);
+    // each ring is released by its own consumers, so K can run ahead of V.
     if (lane == 0) {
-      prefetch_tmap(&tm_k);
-      prefetch_tmap(&tm_v);
-      if (!kStateOnly) prefetch_tmap(&tm_q);
+      const bool is_v = warp == kWarpTmaV;
+      const int stages = is_v ? kVStages : kQKStages;
+      const int full0 = is_v ? kVFull0 : kQKFull0;
+      const int empty0 = is_v ? kVEmpty0 : kQKEmpty0;
+      if (is_v) {
+        prefetch_tmap(&tm_v);
+      } else {
+        prefetch_tmap(&tm_k);
+        if (!kStateOnly) prefetch_tmap(&tm_q);
+      }
       int issued = 0;
       for (int c = 0; c < n_chunks; ++c) {
-        const int s = c & 1;
-        if (c >= 2 && !mbar_wait(&bars[kEmpty0 + s], ((c >> 1) - 1) & 1, abort_flag)) break;
-        const uint32_t bytes = (kStateOnly ? kQBytes : 2 * kQBytes) + kVBytes;
-        mbar_arrive_expect_tx(&bars[kFull0 + s], bytes);
+        const int st = c % stages;
+        const int round = c / stages;
+        if (round > 0 && !mbar_wait(&bars[empty0 + st], (round - 1) & 1, abort_flag)) break;
         const int row = (int)(t_begin + (int64_t)c * kT);
-        if (!kStateOnly) tma_load_3d(smem + kOffQ + s * kQBytes, &tm_q, &bars[kFull0 + s], 0, row, (int)bh);
-        tma_load_3d(smem + kOffK + s * kQBytes, &tm_k, &bars[kFull0 + s], 0, row, (int)bh);
-        tma_load_3d(smem + kOffV + s * kVBytes, &tm_v, &bars[kFull0 + s], 0, row, (int)bh);
+        if (is_v) {
+          mbar_arrive_expect_tx(&bars[full0 + st], kVBytes);
+          tma_load_3d(smem + kOffV + st * kVBytes, &tm_v, &bars[full0 + st], 0, row, (int)bh);
+        } else {
+          mbar_arrive_expect_tx(&bars[full0 + st], kStateOnly ? kQBytes : 2 * kQBytes);
+          if (!kStateOnly)
+            tma_load_3d(smem + kOffQ + st * kQBytes, &tm_q, &bars[full0 + st], 0, row, (int)bh);
+          tma_load_3d(smem + kOffK + st * kQBytes, &tm_k, &bars[full0 + st], 0, row, (int)bh);
+        }
         issued = c + 1;
       }
       // every issued copy must land before the CTA can exit
-      for (int c = issued - 2 < 0 ? 0 : issued - 2; c < issued; ++c)
-        wait_teardown(&bars[kFull0 + (c & 1)], (c >> 1) & 1);
+      for (int c = issued - stages < 0 ? 0 : issued - stages; c < issued; ++c)
+        wait_teardown(&bars[full0 + c % stages], (c / stages) & 1);
     }
   } else if (warp == kWarpUpd || warp == kWarpOut) {
     // ------------------------------------------------------------ MMA issuers
@@ -338,6 +358,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     if (lane == 0 && warp == kWarpUpd) {
       for (int c = 0; c < n_chunks; ++c) {
         const int b = c & 1;
+        if (!mbar_wait(&bars[kVFull0 + b], (c >> 1) & 1, abort_flag)) break;
         if (!mbar_wait(&bars[kPhiKReady0 + b], (c >> 1) & 1, abort_flag)) break;
         // S^T may change once the snapshot of S_c has been read out
         if ((c == 0 || !kStateOnly) && !mbar_wait(&bars[kSnapReady0 + b], (c >> 1) & 1, abort_flag))
@@ -352,7 +373,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           umma_ss(tmem + kColS, da0 + kStep * j, db0 + (uint64_t)((j * 2048) >> 4), id_up, 1u);
         umma_commit(&bars[kSReady]);
         umma_commit(&bars[kUpDone0 + b]);
-        umma_commit(&bars[kEmpty0 + b]);
+        umma_commit(&bars[kVEmpty0 + b]);
         *up_issued = c + 1;  // the state update of tile c is in the pipe
       }
       umma_commit(&bars[kDone]);
@@ -361,13 +382,14 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         const uint64_t qs_b_desc0 = make_sdesc(sb + kOffSnap, 16, 1024, kSwizzle128B);
         const uint64_t qs_b_desc1 = make_sdesc(sb + kOffSnap + kSnapBytes, 16, 1024, kSwizzle128B);
         auto issue_scores = [&](int c) {
-          const int s = c & 1;
+          const int s = c % kQKStages;
           const uint64_t da = make_sdesc(sb + kOffQ + s * kQBytes, 16, 256, kSwizzle32B);
           const uint64_t db = make_sdesc(sb + kOffK + s * kQBytes, 16, 256, kSwizzle32B);
           umma_ss(tmem + kColSc, da, db, id_sc, 0);
           umma_commit(&bars[kScReady]);
+          umma_commit(&bars[kQKEmpty0 + s]);
         };
-        bool ok = mbar_wait(&bars[kFull0], 0, abort_flag);
+        bool ok = mbar_wait(&bars[kQKFull0], 0, abort_flag);
         if (ok) {
           tc_fence_after();
           issue_scores(0);
@@ -394,6 +416,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           // O += P [V 1]: B = V (64 columns) with the ones block as its second
           // 64-column block (LBO), so O[:, 64] also collects the row sum of P.
           if (!mbar_wait(&bars[kPReady], c & 1, abort_flag)) break;
+          if (!mbar_wait(&bars[kVFull0 + b], (c >> 1) & 1, abort_flag)) break;
           tc_fence_after();
           LA_TRACE_AT(0, c, 2);
           const uint32_t v_base = sb + kOffV + b * kVBytes;
@@ -405,10 +428,11 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           // the scores of tile c+1 overwrite P(c): wait for P V to finish;
           // that also ends this issuer's use of TMA stage b
           if (!mbar_wait(&bars[kOReady], c & 1, abort_flag)) break;
-          mbar_arrive(&bars[kEmpty0 + b]);
+          mbar_arrive(&bars[kVEmpty0 + b]);
           LA_TRACE_AT(0, c, 3);
           if (c + 1 < n_chunks) {
-            if (!mbar_wait(&bars[kFull0 + ((c + 1) & 1)], ((c + 1) >> 1) & 1, abort_flag)) break;
+            const int c1 = c + 1;
+            if (!mbar_wait(&bars[kQKFull0 + c1 % kQKStages], (c1 / kQKStages) & 1, abort_flag)) break;
             tc_fence_after();
             issue_scores(c + 1);
           }
@@ -416,31 +440,30 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       }
       umma_commit(&bars[kDone]);
     }
-  } else if (warp < kWarpFeat) {
-    // warp 3 has no role; it only joins the final CTA barrier
   } else if (warp < kWarpPoly) {
     // ------------------------------------------------------------ features
     const int wq = warp & 3;
     const int row = wq * 32 + lane;  // token within the tile == TMEM lane
     const bool leader = (warp == kWarpFeat && lane == 0);
     for (int c = 0; c < n_chunks; ++c) {
-      const int s = c & 1;
-      mbar_wait(&bars[kFull0 + s], (c >> 1) & 1, abort_flag);
+      const int s = c & 1;           // phi(K) buffer
+      const int sq = c % kQKStages;  // Q/K stage
+      mbar_wait(&bars[kQKFull0 + sq], (c / kQKStages) & 1, abort_flag);
       if (!wg_ok(1, abort_flag)) break;
       LA_TRACE_AT(1, c, 0);
       const int valid = (int)min64(kT, t_end - (t_begin + (int64_t)c * kT));
       const bool vrow = row < valid;
       uint32_t kw[8], qw[8];
-      const uint32_t kt = sb + kOffK + s * kQBytes;
+      const uint32_t kt = sb + kOffK + sq * kQBytes;
       ld_shared_v4(kt + sw32_offset(row, 0), kw[0], kw[1], kw[2], kw[3]);
       ld_shared_v4(kt + sw32_offset(row, 1), kw[4], kw[5], kw[6], kw[7]);
       if (!kStateOnly) {
-        const uint32_t qt = sb + kOffQ + s * kQBytes;
+        const uint32_t qt = sb + kOffQ + sq * kQBytes;
         ld_shared_v4(qt + sw32_offset(row, 0), qw[0], qw[1], qw[2], qw[3]);
         ld_shared_v4(qt + sw32_offset(row, 1), qw[4], qw[5], qw[6], qw[7]);
       }
       named_barrier_sync(1, 128);
-      if (leader) mbar_arrive(&bars[kEmpty0 + s]);
+      if (leader) mbar_arrive(&bars[kQKEmpty0 + sq]);
       // phi(K) into buffer c&1 once the update of tile c-2 has read it
       if (c >= 2) mbar_wait(&bars[kUpDone0 + s], ((c >> 1) - 1) & 1, abort_flag);
       if (!wg_ok(1, abort_flag)) break;
@@ -684,35 +707,40 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         if (!wg_ok(4, abort_flag)) break;
         tc_fence_after();
         LA_TRACE_AT(4, c, 0);
-        // the denominator column first, then the values 16 columns at a time
-        uint32_t dr[16];
-        tmem_ld16(taddr(tmem, wq * 32, kColO + kDv), dr);
+        // O leaves TMEM in two round trips: (denominator, values 0..31), then
+        // values 32..63
+        uint32_t o[32];
+        const uint32_t obase = taddr(tmem, wq * 32, kColO);
+        const uint32_t dbits = tmem_ld1(obase + kDv);
+        tmem_ld16(obase, o);
+        tmem_ld16(obase + 16, o + 16);
         tmem_wait_ld();
         // O[:, 64] = phi(q).z + rowsum(P): the full denominator before eps
-        const float den = __uint_as_float(dr[0]) + p.eps;
+        const float den = __uint_as_float(dbits) + p.eps;
         const float inv = p.normalize ? 1.f / den : 1.f;
         const uint64_t inv2 = f2pack(inv, inv);
         __nv_bfloat16 *orow = p.out + ((uint64_t)bh * p.n + t0 + row) * kDv;
+        auto store32 = [&](int col) {
 #pragma unroll
-        for (int G = 0; G < kDv / 16; ++G) {
-          uint32_t o[16];
-          tmem_ld16(taddr(tmem, wq * 32, kColO + 16 * G), o);
-          tmem_wait_ld();
-          if (G == kDv / 16 - 1) {
-            tc_fence_before();
-            named_barrier_sync(4, 128);
-            if (leader) mbar_arrive(&bars[kOFree]);  // O is in registers: TMEM O reusable
-            LA_TRACE_AT(4, c, 1);
-          }
-          uint32_t w[8];
+          for (int v4 = 0; v4 < 4; ++v4) {
+            uint32_t w[4];
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            w[i] = pack_bf16x2(fmul2(f2pack(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), inv2));
-          if (row < valid) {
-            *(uint4 *)(orow + 16 * G) = make_uint4(w[0], w[1], w[2], w[3]);
-            *(uint4 *)(orow + 16 * G + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+            for (int i = 0; i < 4; ++i) {
+              const int k = 8 * v4 + 2 * i;
+              w[i] = pack_bf16x2(fmul2(f2pack(__uint_as_float(o[k]), __uint_as_float(o[k + 1])), inv2));
+            }
+            if (row < valid) *(uint4 *)(orow + col + 8 * v4) = make_uint4(w[0], w[1], w[2], w[3]);
           }
-        }
+        };
+        store32(0);
+        tmem_ld16(obase + 32, o);
+        tmem_ld16(obase + 48, o + 16);
+        tmem_wait_ld();
+        tc_fence_before();
+        named_barrier_sync(4, 128);
+        if (leader) mbar_arrive(&bars[kOFree]);  // O is in registers: TMEM O reusable
+        LA_TRACE_AT(4, c, 1);
+        store32(32);
         LA_TRACE_AT(4, c, 2);
       }
     }

@@ -162,6 +162,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t *r) {
         "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(addr));
 }
+// One 32-bit column per lane.
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t addr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(addr));
+  return r;
+}
 __device__ __forceinline__ void tmem_st16(uint32_t addr, const uint32_t *r) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32"
