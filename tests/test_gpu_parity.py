@@ -181,6 +181,24 @@ def test_deterministic():
     assert torch.equal(T.solution_nki(q, k, v), T.solution_nki(q, k, v))
 
 
+def test_deterministic_segment_states_lightly_loaded():
+    """Few CTAs run far ahead of the memory system: the segment-state pass
+    must still give bit-identical states on every run."""
+    q, k, v = cuda(*inputs((1, 2, 4096, 16), 64, seed=6))
+    g, ws_bytes = ops.chunked_plan(2, 4096, 16, 64, torch.bfloat16, segments=3)
+    runs = []
+    for _ in range(8):
+        ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=DEV)
+        ops.based_chunked_state(k, v, segments=g, workspace=ws)
+        runs.append(ws)
+    for ws in runs[1:]:
+        assert torch.equal(ws, runs[0])
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    for _ in range(4):
+        y = ops.based_chunked(q, k, v, segments=g)
+        assert O.rel_l2(np64(y), want) <= 5e-3
+
+
 # ----------------------------------------------------------------- sliding ---
 
 @pytest.mark.parametrize("case", ["slide_w64", "slide_w16_odd", "slide_w1", "slide_wbig",

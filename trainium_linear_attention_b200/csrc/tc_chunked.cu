@@ -462,8 +462,6 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         ld_shared_v4(qt + sw32_offset(row, 0), qw[0], qw[1], qw[2], qw[3]);
         ld_shared_v4(qt + sw32_offset(row, 1), qw[4], qw[5], qw[6], qw[7]);
       }
-      named_barrier_sync(1, 128);
-      if (leader) mbar_arrive(&bars[kQKEmpty0 + sq]);
       // phi(K) into buffer c&1 once the update of tile c-2 has read it
       if (c >= 2) mbar_wait(&bars[kUpDone0 + s], ((c >> 1) - 1) & 1, abort_flag);
       if (!wg_ok(1, abort_flag)) break;
@@ -477,7 +475,12 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       }
       fence_proxy_async_smem();
       named_barrier_sync(1, 128);
-      if (leader) mbar_arrive(&bars[kPhiKReady0 + s]);
+      if (leader) {
+        mbar_arrive(&bars[kPhiKReady0 + s]);
+        // kw has been consumed (and, in the state pass, the stage is done):
+        // the next TMA copy may overwrite it
+        if (kStateOnly) mbar_arrive(&bars[kQKEmpty0 + sq]);
+      }
       LA_TRACE_AT(1, c, 1);
       if (!kStateOnly) {
         // phi(Q) -> TMEM once phi(Q) S of the previous tile has read it
@@ -496,8 +499,12 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         store_phiq(fs, taddr(tmem, wq * 32, kColPhiQ), std::make_integer_sequence<int, kFPad / 32>{});
         tmem_wait_st();
         tc_fence_before();
+        fence_proxy_async_smem();
         named_barrier_sync(1, 128);
-        if (leader) mbar_arrive(&bars[kPhiQReady]);
+        if (leader) {
+          mbar_arrive(&bars[kPhiQReady]);
+          mbar_arrive(&bars[kQKEmpty0 + sq]);  // qw consumed too: release the stage
+        }
         LA_TRACE_AT(1, c, 2);
       }
     }
