@@ -124,6 +124,25 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
                          void *workspace, size_t workspace_bytes, int segments,
                          void *stream);
 
+/* The chunked forward for callers that cannot allocate device memory (a
+ * plugin whose host framework owns all device memory and gives it no
+ * allocation hook, or a latency-critical path that must not call cudaMalloc).
+ * Same arguments and results as la_based_chunked_fwd without the workspace:
+ * the segment scratch comes from an 8 MiB array compiled into the library
+ * (held on every device that loads it until exit), enough for 210 (head,
+ * segment) states at d_qk = 16, d_v = 64.  Allocates nothing.  A request
+ * needing more scratch returns LA_ERR_WORKSPACE; LA_CHUNKED_REUSE_SEGMENTS is
+ * rejected (LA_ERR_INVALID_ARGUMENT).  All calls on a device share the array
+ * and leave its contents behind: calls whose kernels overlap on the GPU race
+ * on it.  The first call on a device resolves the array's address; make it
+ * before any stream capture.  The reference has no counterpart. */
+int la_based_chunked_fwd_noalloc(const void *q, const void *k, const void *v, void *out,
+                                 int64_t batch, int64_t heads, int64_t seq_len,
+                                 int64_t d_qk, int64_t d_v, int dtype,
+                                 int64_t chunk_size, float eps, unsigned flags,
+                                 const float *init_state, float *final_state,
+                                 int segments, void *stream);
+
 /* Total state sum_j phi_k(k_j) [v_j, 1]^T of every head over all seq_len
  * tokens, written to state_out (fp32, (batch*heads, F, d_v + 1)).  This is the
  * per-rank contribution exchanged by the sequence-parallel mode.  With a

@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "la_based_chunked_plan",
     "la_based_chunked_workspace_size",
     "la_based_chunked_fwd",
+    "la_based_chunked_fwd_noalloc",
     "la_based_chunked_state",
     "la_sliding_window_fwd",
 )
@@ -79,6 +80,9 @@ def _declare(lib) -> None:
     lib.la_based_chunked_fwd.argtypes = [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int,
                                          _i64, _f, ctypes.c_uint, _p, _p, _p, _sz, _int, _p]
     lib.la_based_chunked_fwd.restype = _int
+    lib.la_based_chunked_fwd_noalloc.argtypes = [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,
+                                                 _int, _i64, _f, ctypes.c_uint, _p, _p, _int, _p]
+    lib.la_based_chunked_fwd_noalloc.restype = _int
     lib.la_based_chunked_state.argtypes = [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int,
                                            _p, _sz, _int, _p]
     lib.la_based_chunked_state.restype = _int

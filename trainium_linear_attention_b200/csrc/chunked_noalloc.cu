@@ -1,0 +1,84 @@
+// la_based_chunked_fwd_noalloc: the chunked BASED forward for callers that
+// cannot allocate device memory.
+//
+// A segmented chunked forward needs scratch for the per-segment states
+// (la_based_chunked_workspace_size bytes).  Some callers cannot provide it:
+// code loaded as a plugin by a host framework that owns all device memory
+// and hands its plugins no allocation hook, or latency-critical paths that
+// must not call cudaMalloc (which can synchronise the device).  This entry
+// point takes its scratch from a fixed array compiled into the library
+// instead, and otherwise behaves exactly like la_based_chunked_fwd, which it
+// calls.  It calls no cudaMalloc, cudaFree or allocating library routine.
+//
+// Limits and sharing:
+//   * the array holds kNoAllocScratchBytes (8 MiB) on every device that loads
+//     the library, until the process exits: 210 (head, segment) states of the
+//     d_qk = 16, d_v = 64 fast path (39,780 bytes each);
+//   * a request whose scratch would exceed it fails with LA_ERR_WORKSPACE;
+//   * every call on a device shares the one array and leaves its contents
+//     behind; calls whose kernels overlap on the GPU (e.g. on two streams
+//     without ordering) race on it.  The forward writes every scratch byte it
+//     reads before reading it, so nothing needs clearing between calls.
+//   * the first call on a device resolves the array's device address (a
+//     cudaGetSymbolAddress with that device current); make that first call
+//     before any stream capture.
+#include <mutex>
+
+#include "common.cuh"
+
+namespace la {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+
+// The scratch itself.  In host code this name is only a stand-in for the
+// symbol, not a device address: the address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device (resolved once
+// per device), or null if it cannot be resolved.
+void *noalloc_scratch_ptr() {
+  static std::mutex mu;
+  static void *cache[64] = {};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    void *ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    cache[dev] = ptr;
+  }
+  return cache[dev];
+}
+
+}  // namespace
+}  // namespace la
+
+extern "C" int la_based_chunked_fwd_noalloc(const void *q, const void *k, const void *v,
+                                            void *out, int64_t batch, int64_t heads,
+                                            int64_t seq_len, int64_t d_qk, int64_t d_v,
+                                            int dtype, int64_t chunk_size, float eps,
+                                            unsigned flags, const float *init_state,
+                                            float *final_state, int segments, void *stream) {
+  // The scratch never holds states this caller wrote with la_based_chunked_state.
+  if (flags & LA_CHUNKED_REUSE_SEGMENTS) return LA_ERR_INVALID_ARGUMENT;
+  if (batch < 0 || heads < 0 || seq_len < 0 || d_qk < 1 || d_v < 1 || segments < 0)
+    return LA_ERR_INVALID_ARGUMENT;
+  int g = segments;
+  size_t need = 0;
+  const int st = la_based_chunked_plan(batch * heads, seq_len, d_qk, d_v, dtype, segments, &g,
+                                       &need);
+  if (st != LA_OK) return st;
+  if (need > la::kNoAllocScratchBytes) return LA_ERR_WORKSPACE;
+  void *scratch = la::noalloc_scratch_ptr();
+  if (!scratch) return LA_ERR_CUDA;
+  return la_based_chunked_fwd(q, k, v, out, batch, heads, seq_len, d_qk, d_v, dtype, chunk_size,
+                              eps, flags, init_state, final_state, scratch,
+                              la::kNoAllocScratchBytes, g, stream);
+}
