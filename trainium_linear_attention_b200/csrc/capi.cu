@@ -95,10 +95,12 @@ int effective_segments(int64_t n, int segments) {
   return (int)((n + len - 1) / len);
 }
 
+// Segments per head for one wave of CTAs: the largest g with bh * g <= SMs
+// (a second partial wave would cost more than the idle SMs of one wave), and
+// at least kMinSegmentTokens tokens per segment.
 int auto_segments(int64_t bh, int64_t n, int sm_count) {
   if (bh <= 0 || n <= 0) return 1;
-  if (bh * 4 >= (int64_t)sm_count * 3) return 1;  // >= 75% of the SMs busy already
-  int64_t g = (sm_count + bh - 1) / bh;
+  int64_t g = sm_count / bh;
   const int64_t max_g = (n + kMinSegmentTokens - 1) / kMinSegmentTokens;
   if (g > max_g) g = max_g;
   if (g < 1) g = 1;
