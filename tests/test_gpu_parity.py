@@ -100,6 +100,25 @@ def test_chunked_other_widths(dqk, dv, dtype):
     assert O.rel_l2(np64(y), want) <= tol
 
 
+def test_chunked_unaligned_pointers():
+    """bf16 tensors whose data is not 16-byte aligned (TMA cannot address
+    them) run on the CUDA-core kernels with the same result."""
+    q, k, v = cuda(*inputs((1, 2, 500, 16), 64, seed=21))
+
+    def shifted(x):
+        buf = torch.empty(x.numel() + 1, dtype=x.dtype, device=DEV)
+        y = buf[1:].view(x.shape)
+        y.copy_(x)
+        return y
+
+    qs, ks, vs = shifted(q), shifted(k), shifted(v)
+    assert qs.data_ptr() % 16 != 0
+    y = ops.based_chunked(qs, ks, vs)
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+    assert O.rel_l2(np64(y), np64(ops.based_chunked(q, k, v))) <= 1e-2
+
+
 @pytest.mark.parametrize("segments", [2, 3, 8])
 def test_chunked_segments_agree(segments):
     q, k, v = cuda(*inputs((1, 4, 3000, 16), 64, seed=7))

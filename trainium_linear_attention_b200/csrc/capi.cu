@@ -111,6 +111,9 @@ bool use_tensor_cores(int dtype, int64_t dqk, int64_t dv) {
   return dtype == LA_DTYPE_BFLOAT16 && dqk == 16 && dv == 64;
 }
 
+// TMA needs 16-byte aligned tensors; other pointers take the SIMT kernels
+bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
 size_t state_floats(int64_t bh, int64_t dqk, int64_t dv) {
   return (size_t)bh * (size_t)feature_dim(dqk) * (size_t)(dv + 1);
 }
@@ -215,7 +218,8 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
   DeviceInfo info;
   if ((st = require_sm100(&info)) != LA_OK) return st;
   cudaStream_t s = (cudaStream_t)stream;
-  const bool tc = use_tensor_cores(dtype, d_qk, d_v) && tc_chunked_enabled();
+  const bool tc = use_tensor_cores(dtype, d_qk, d_v) && tc_chunked_enabled() && aligned16(q) &&
+                  aligned16(k) && aligned16(v) && aligned16(out);
   if (!tc && !chunked_simt_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
   if (seq_len == 0) {
     // no tokens: the final state is the initial state (or zero)
@@ -272,7 +276,8 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
   cudaStream_t s = (cudaStream_t)stream;
   const size_t state_bytes = state_floats(bh, d_qk, d_v) * sizeof(float);
   if (seq_len == 0) return cuda_status(cudaMemsetAsync(state_out, 0, state_bytes, s));
-  const bool tc = use_tensor_cores(dtype, d_qk, d_v) && tc_chunked_enabled();
+  const bool tc = use_tensor_cores(dtype, d_qk, d_v) && tc_chunked_enabled() && aligned16(k) &&
+                  aligned16(v);
   if (!tc && !chunked_simt_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
   int g = segments == 0 ? auto_segments(bh, seq_len, info.sm_count)
                         : effective_segments(seq_len, segments);

@@ -85,9 +85,13 @@ constexpr uint32_t kOffOnes = kOffV + kVStages * kVBytes;   // 57344: 16 rows x 
 constexpr uint32_t kPhiBlock = kT * 128;            // 64 features of 128 tokens
 constexpr uint32_t kPhiBytes = 3 * kPhiBlock;       // 160 features (3 blocks)
 constexpr uint32_t kOffPhiK = kOffOnes + 2048;      // 59392: 2 buffers
-constexpr uint32_t kOffSnap = kOffPhiK + 2 * kPhiBytes;  // 157696: 2 x 30 KB
+// Snapshots of S: the K-major B operand of phi(Q) S, 80 rows x 160 features
+// in three 64-feature blocks of 80 x 128 B.  (Letting the two buffers share
+// their half-used third block was measured 19% slower: the state warps then
+// store into 128-byte rows the tensor core is reading.)
 constexpr uint32_t kSnapKBlock = kNO * 128;         // 10 KB per 64-feature block
 constexpr uint32_t kSnapBytes = 3 * kSnapKBlock;
+constexpr uint32_t kOffSnap = kOffPhiK + 2 * kPhiBytes;  // 157696: 2 x 30 KB
 constexpr uint32_t kOffBar = kOffSnap + 2 * kSnapBytes;  // 219136
 constexpr uint32_t kSmemBytes = kOffBar + 256;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;       // alignment slack
@@ -107,11 +111,14 @@ enum Bar { kQKFull0, kQKFull1, kQKFull2, kQKEmpty0, kQKEmpty1, kQKEmpty2, kVFull
 // Optional per-role timeline of CTA (0, 0), compiled in with -DLA_TRACE only.
 #ifdef LA_TRACE
 constexpr int kTraceChunks = 32, kTraceEvents = 8;
-__device__ long long la_trace_buf[5][kTraceChunks][kTraceEvents];
+constexpr int kTraceMaxCtas = 128;
+__device__ long long la_trace_buf[kTraceMaxCtas][6][kTraceChunks][kTraceEvents];
+constexpr int kTraceCtas = 4096;
+__device__ long long la_trace_cta[kTraceCtas][5];  // start ns, end ns, SM id, start clk, end clk
 #define LA_TRACE_AT(role, chunk, ev)                                                   \
   do {                                                                                \
-    if (blockIdx.x == 0 && blockIdx.y == 0 && (chunk) < kTraceChunks && (threadIdx.x & 31) == 0) \
-      la_trace_buf[role][chunk][ev] = clock64();                                      \
+    if (blockIdx.x == 0 && blockIdx.y < kTraceMaxCtas && (chunk) < kTraceChunks && (threadIdx.x & 31) == 0) \
+      la_trace_buf[blockIdx.y][role][chunk][ev] = clock64();                          \
   } while (0)
 #else
 #define LA_TRACE_AT(role, chunk, ev) \
@@ -119,119 +126,148 @@ __device__ long long la_trace_buf[5][kTraceChunks][kTraceEvents];
   } while (0)
 #endif
 
-// Feature f of the query/key-split basis ->
-//   kind 0: 1;  kind 1: x_a;  kind 2: x_a x_b (a < b);  kind 3: x_a^2;  kind 4: padding 0.
-// Evaluated at compile time: every caller indexes with an unrolled constant.
-__host__ __device__ constexpr int feat_quad_row(int r) {  // row a of quadratic index r
-  int a = 0;
-  while (a < kDqk - 1 && r >= kDqk - a) {
-    r -= kDqk - a;
-    ++a;
-  }
-  return a;
-}
-__host__ __device__ constexpr int feat_quad_col(int r) {
-  int a = 0;
-  while (a < kDqk - 1 && r >= kDqk - a) {
-    r -= kDqk - a;
-    ++a;
-  }
-  return a + r;
-}
-__host__ __device__ constexpr int feat_kind(int f) {
-  return f == 0 ? 0 : f <= kDqk ? 1 : f >= kF ? 4
-                : (feat_quad_row(f - 1 - kDqk) == feat_quad_col(f - 1 - kDqk) ? 3 : 2);
-}
-__host__ __device__ constexpr int feat_a(int f) {
-  return f == 0 || f >= kF ? 0 : f <= kDqk ? f - 1 : feat_quad_row(f - 1 - kDqk);
-}
-__host__ __device__ constexpr int feat_b(int f) {
-  return f == 0 || f >= kF ? 0 : f <= kDqk ? f - 1 : feat_quad_col(f - 1 - kDqk);
-}
-static_assert(feat_kind(17) == 3 && feat_a(18) == 0 && feat_b(18) == 1 && feat_kind(152) == 3 &&
-                  feat_a(152) == 15 && feat_b(151) == 15 && feat_a(151) == 14 && feat_kind(153) == 4,
-              "feature order: const, 16 linear, (a, b) a <= b row-major");
-
-// Features are produced two at a time as one bf16x2 product A * B, A and B
-// assembled (byte permutes) from the token's 16 inputs and their exact
-// power-of-two rescalings.  A bf16 product of bf16 operands rounds the exact
-// product once, so every feature equals the fp32 product rounded to bf16.
-//   key side   phi_k = [1, k_a, k_a k_b]                    (unscaled)
-//   query side phi_q = [1, q_a / 4, q_a q_b / 16 (a < b), q_a^2 / 32]   (d = 16)
-enum : int { kSrcRaw = 0, kSrcS4, kSrcS16, kSrcS32, kSrcOne, kSrcOneValid, kSrcZero };
-struct Op {
-  int src;
-  int idx;
+// Feature slots.  S^T's columns, phi(K)'s smem columns and phi(Q)'s TMEM
+// columns hold the 153 features of the query/key-split basis in the order
+// below ("slots", two per bf16x2 pair), chosen so that almost every pair is a
+// single bf16x2 product of an input word (x_b, x_b+1) and a broadcast x_a:
+//   pairs 0..7    x_2i, x_2i+1                      (linear)
+//   pair  8       1, 0                              (constant, padding)
+//   pairs 9..44   x_a x_2j, x_a x_2j+1   a even, 2j >= a      (36 pairs)
+//   pairs 45..72  x_a x_2j, x_a x_2j+1   a odd,  2j >  a      (28 pairs)
+//   pairs 73..76  x_a^2, x_a'^2          a, a' = (1,3) (5,7) (9,11) (13,15)
+//   pairs 77..79  0, 0                                        (padding)
+// In HBM the state keeps the documented order [1, x_0..x_15, x_a x_b (a <= b)
+// row-major]; slot_feature() maps a slot to it.
+// Scales: key side unscaled; query side x_a / 4 (linear), x_a x_b / 16
+// (a < b), x_a^2 / 32.  All are exact power-of-two rescalings of bf16 inputs,
+// and a bf16 product of bf16 operands rounds the exact product once, so every
+// feature equals the fp32 product rounded to bf16.
+enum : int { kPairLin, kPairConst, kPairEven, kPairOdd, kPairDiag, kPairPad };
+struct PairDesc {
+  int type, a, b;  // kPairEven / kPairOdd: row a, word b; kPairDiag: rows a, b; kPairLin: word a
 };
-template <bool kQ>
-__host__ __device__ constexpr Op op_a(int f) {
-  const int kind = feat_kind(f), a = feat_a(f);
-  return kind == 0   ? Op{kSrcOneValid, 0}
-         : kind == 1 ? Op{kQ ? kSrcS4 : kSrcRaw, a}
-         : kind == 2 ? Op{kQ ? kSrcS16 : kSrcRaw, a}
-         : kind == 3 ? Op{kQ ? kSrcS32 : kSrcRaw, a}
-                     : Op{kSrcZero, 0};
+__host__ __device__ constexpr PairDesc pair_desc(int p) {
+  if (p < 8) return {kPairLin, p, 0};
+  if (p == 8) return {kPairConst, 0, 0};
+  int q = p - 9;
+  for (int a = 0; a < kDqk; a += 2) {  // even rows: words a/2 .. 7
+    const int n = 8 - a / 2;
+    if (q < n) return {kPairEven, a, a / 2 + q};
+    q -= n;
+  }
+  for (int a = 1; a < kDqk; a += 2) {  // odd rows: words (a+1)/2 .. 7
+    const int n = 8 - (a + 1) / 2;
+    if (q < n) return {kPairOdd, a, (a + 1) / 2 + q};
+    q -= n;
+  }
+  if (q < 4) return {kPairDiag, 4 * q + 1, 4 * q + 3};
+  return {kPairPad, 0, 0};
 }
-__host__ __device__ constexpr Op op_b(int f) {
-  const int kind = feat_kind(f), b = feat_b(f);
-  return kind <= 1 ? Op{kSrcOne, 0} : kind <= 3 ? Op{kSrcRaw, b} : Op{kSrcZero, 0};
+// index of x_a x_b (a <= b) in the documented order
+__host__ __device__ constexpr int quad_feature(int a, int b) {
+  return 1 + kDqk + a * kDqk - a * (a - 1) / 2 + (b - a);
 }
-
-struct FeatSrc {
-  uint32_t raw[8], s4[8], s16[8], s32[8];  // bf16x2 words: values 2i (lo), 2i+1 (hi)
-  uint32_t one_valid;                      // bf16x2 {1, 1}, or {0, 0} for a padding token
+// documented feature index of slot s, or -1 for a padding slot
+__host__ __device__ constexpr int slot_feature(int s) {
+  const PairDesc d = pair_desc(s >> 1);
+  const int h = s & 1;
+  switch (d.type) {
+    case kPairLin: return 1 + 2 * d.a + h;
+    case kPairConst: return h ? -1 : 0;
+    case kPairEven:
+    case kPairOdd: return quad_feature(d.a, 2 * d.b + h);
+    case kPairDiag: return h ? quad_feature(d.b, d.b) : quad_feature(d.a, d.a);
+    default: return -1;
+  }
+}
+struct SlotMap {
+  short f[kFPad];
 };
-template <int kSrc, int kIdx>
-__device__ __forceinline__ uint32_t src_word(const FeatSrc &s) {
-  if constexpr (kSrc == kSrcRaw) return s.raw[kIdx >> 1];
-  else if constexpr (kSrc == kSrcS4) return s.s4[kIdx >> 1];
-  else if constexpr (kSrc == kSrcS16) return s.s16[kIdx >> 1];
-  else if constexpr (kSrc == kSrcS32) return s.s32[kIdx >> 1];
-  else if constexpr (kSrc == kSrcOne) return 0x3F803F80u;
-  else if constexpr (kSrc == kSrcOneValid) return s.one_valid;
-  else return 0u;
+__host__ __device__ constexpr SlotMap make_slot_map() {
+  SlotMap m{};
+  for (int s = 0; s < kFPad; ++s) m.f[s] = (short)slot_feature(s);
+  return m;
 }
-template <int kSrc, int kIdx>
-__host__ __device__ constexpr int src_half() {
-  return kSrc <= kSrcS32 ? (kIdx & 1) : 0;
+__host__ __device__ constexpr bool slot_map_is_bijection() {
+  int seen[kF] = {};
+  for (int s = 0; s < kFPad; ++s) {
+    const int f = slot_feature(s);
+    if (f >= kF) return false;
+    if (f >= 0) ++seen[f];
+  }
+  for (int f = 0; f < kF; ++f)
+    if (seen[f] != 1) return false;
+  return pair_desc(79).type == kPairPad && pair_desc(76).type == kPairDiag &&
+         pair_desc(77).type == kPairPad;
 }
-template <bool kQ, int F0>
-__device__ __forceinline__ uint32_t feat_pair(const FeatSrc &s) {
-  constexpr Op a0 = op_a<kQ>(F0), a1 = op_a<kQ>(F0 + 1);
-  constexpr Op b0 = op_b(F0), b1 = op_b(F0 + 1);
-  const uint32_t A = bf16_pair<src_half<a0.src, a0.idx>(), src_half<a1.src, a1.idx>()>(
-      src_word<a0.src, a0.idx>(s), src_word<a1.src, a1.idx>(s));
-  const uint32_t B = bf16_pair<src_half<b0.src, b0.idx>(), src_half<b1.src, b1.idx>()>(
-      src_word<b0.src, b0.idx>(s), src_word<b1.src, b1.idx>(s));
-  return hmul2_bf16(A, B);
+static_assert(slot_map_is_bijection(), "every feature has exactly one slot");
+__constant__ SlotMap c_slot_map = make_slot_map();
+
+// A token's inputs as bf16x2 words (x_2i lo, x_2i+1 hi): raw, and (query side)
+// divided by 16 and by 32.  `one` is {1, 0}, or 0 for a padding key.
+struct FeatIn {
+  uint32_t w[8], s16[8], s32[8];
+  uint32_t one;
+};
+template <bool kQ, int P>
+__device__ __forceinline__ uint32_t pair_val(const FeatIn &s) {
+  constexpr PairDesc d = pair_desc(P);
+  if constexpr (d.type == kPairLin) {
+    return kQ ? hmul2_bf16(s.w[d.a], 0x3E803E80u) : s.w[d.a];  // query side: x / 4
+  } else if constexpr (d.type == kPairConst) {
+    return s.one;
+  } else if constexpr (d.type == kPairEven) {
+    // row a even: x_a is the low half of word a/2; the diagonal pair of a
+    // query row scales x_a^2 by 1/32 and x_a x_a+1 by 1/16
+    uint32_t A;
+    if constexpr (!kQ) A = bf16_pair<0, 0>(s.w[d.a >> 1], s.w[d.a >> 1]);
+    else if constexpr (d.b == d.a / 2) A = bf16_pair<0, 0>(s.s32[d.a >> 1], s.s16[d.a >> 1]);
+    else A = bf16_pair<0, 0>(s.s16[d.a >> 1], s.s16[d.a >> 1]);
+    return hmul2_bf16(A, s.w[d.b]);
+  } else if constexpr (d.type == kPairOdd) {
+    const uint32_t x = kQ ? s.s16[d.a >> 1] : s.w[d.a >> 1];
+    return hmul2_bf16(bf16_pair<1, 1>(x, x), s.w[d.b]);
+  } else if constexpr (d.type == kPairDiag) {
+    const uint32_t X = bf16_pair<1, 1>(s.w[d.a >> 1], s.w[d.b >> 1]);
+    const uint32_t A = kQ ? bf16_pair<1, 1>(s.s32[d.a >> 1], s.s32[d.b >> 1]) : X;
+    return hmul2_bf16(A, X);
+  } else {
+    return 0u;
+  }
 }
 
-// Features 8J .. 8J+7 of token `row` -> 128B-swizzled smem, 64 features per
-// 16 KB block: the K-major A layout of phi(Q) and the MN-major B layout of
-// phi(K) are the same bytes.
-template <bool kQ, int J>
-__device__ __forceinline__ void store_phi_chunk(const FeatSrc &s, uint32_t base, int row) {
-  st_shared_v4(base + (J >> 3) * kPhiBlock + sw128_offset(row, J & 7),
-               feat_pair<kQ, 8 * J + 0>(s), feat_pair<kQ, 8 * J + 2>(s),
-               feat_pair<kQ, 8 * J + 4>(s), feat_pair<kQ, 8 * J + 6>(s));
+// Slots 8J .. 8J+7 (pairs 4J .. 4J+3, one 16-byte chunk) of token `row` ->
+// 128B-swizzled smem, 64 slots per 16 KB block: the MN-major B layout of
+// phi(K) for the update MMA.
+template <int J>
+__device__ __forceinline__ void store_phik_chunk(const FeatIn &s, uint32_t base, int row) {
+  st_shared_v4(base + (J >> 3) * kPhiBlock + sw128_offset(row, J & 7), pair_val<false, 4 * J + 0>(s),
+               pair_val<false, 4 * J + 1>(s), pair_val<false, 4 * J + 2>(s),
+               pair_val<false, 4 * J + 3>(s));
 }
-template <bool kQ, int... J>
-__device__ __forceinline__ void store_phi(const FeatSrc &s, uint32_t base, int row,
-                                          std::integer_sequence<int, J...>) {
-  (store_phi_chunk<kQ, J>(s, base, row), ...);
+template <int... J>
+__device__ __forceinline__ void store_phik(const FeatIn &s, uint32_t base, int row,
+                                           std::integer_sequence<int, J...>) {
+  (store_phik_chunk<J>(s, base, row), ...);
 }
 
-// phi(Q) columns [16G, 16G+16) (features 32G .. 32G+31) of TMEM lane `row`
+// phi(Q) TMEM columns [16G, 16G+16) = pairs 16G .. 16G+15 of TMEM lane `row`
 template <int G, int... I>
-__device__ __forceinline__ void store_phiq_group(const FeatSrc &s, uint32_t addr,
+__device__ __forceinline__ void store_phiq_group(const FeatIn &s, uint32_t addr,
                                                  std::integer_sequence<int, I...>) {
-  const uint32_t w[16] = {feat_pair<true, 32 * G + 2 * I>(s)...};
+  const uint32_t w[16] = {pair_val<true, 16 * G + I>(s)...};
   tmem_st16(addr, w);
 }
 template <int... G>
-__device__ __forceinline__ void store_phiq(const FeatSrc &s, uint32_t addr0,
+__device__ __forceinline__ void store_phiq(const FeatIn &s, uint32_t addr0,
                                            std::integer_sequence<int, G...>) {
   (store_phiq_group<G>(s, addr0 + 16 * G, std::make_integer_sequence<int, 16>{}), ...);
+}
+
+// Shared-memory address of the 16-byte chunk holding features f0 .. f0+7
+// (f0 a multiple of 8) of snapshot row e in buffer `buf`.
+__device__ __forceinline__ uint32_t snap_chunk_addr(uint32_t sb, int buf, int f0, int e) {
+  return sb + kOffSnap + buf * kSnapBytes + (f0 >> 6) * kSnapKBlock + sw128_offset(e, (f0 & 63) >> 3);
 }
 
 struct Params {
@@ -275,6 +311,15 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   const int64_t t_end = min64(p.n, t_begin + p.seg_len);
   const int n_chunks = (int)((t_end - t_begin + kT - 1) / kT);
 
+#ifdef LA_TRACE
+  if (threadIdx.x == 0 && !kStateOnly && blockIdx.y * gridDim.x + blockIdx.x < kTraceCtas) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    la_trace_cta[blockIdx.y * gridDim.x + blockIdx.x][0] = (long long)globaltimer();
+    la_trace_cta[blockIdx.y * gridDim.x + blockIdx.x][2] = smid;
+    la_trace_cta[blockIdx.y * gridDim.x + blockIdx.x][3] = clock64();
+  }
+#endif
   if (threadIdx.x == 0) {
     // every barrier: one arrival (a leader thread, a TMA expect-tx or a
     // tcgen05.commit), except: a Q/K stage is released by the features and
@@ -326,6 +371,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         const int round = c / stages;
         if (round > 0 && !mbar_wait(&bars[empty0 + st], (round - 1) & 1, abort_flag)) break;
         const int row = (int)(t_begin + (int64_t)c * kT);
+        LA_TRACE_AT(5, c, is_v ? 1 : 0);
         if (is_v) {
           mbar_arrive_expect_tx(&bars[full0 + st], kVBytes);
           tma_load_3d(smem + kOffV + st * kVBytes, &tm_v, &bars[full0 + st], 0, row, (int)bh);
@@ -359,6 +405,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       for (int c = 0; c < n_chunks; ++c) {
         const int b = c & 1;
         if (!mbar_wait(&bars[kVFull0 + b], (c >> 1) & 1, abort_flag)) break;
+        LA_TRACE_AT(0, c, 7);
         if (!mbar_wait(&bars[kPhiKReady0 + b], (c >> 1) & 1, abort_flag)) break;
         // S^T may change once the snapshot of S_c has been read out
         if ((c == 0 || !kStateOnly) && !mbar_wait(&bars[kSnapReady0 + b], (c >> 1) & 1, abort_flag))
@@ -398,8 +445,11 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           const int b = c & 1;
           // O = phi(Q) S_c   (K = 160 features in 10 steps; S_c is snapshot b)
           if (!mbar_wait(&bars[kPhiQReady], c & 1, abort_flag)) break;
+          LA_TRACE_AT(0, c, 4);
           if (!mbar_wait(&bars[kSnapReady0 + b], (c >> 1) & 1, abort_flag)) break;
+          LA_TRACE_AT(0, c, 5);
           if (c > 0 && !mbar_wait(&bars[kOFree], (c - 1) & 1, abort_flag)) break;
+          LA_TRACE_AT(0, c, 6);
           // let the update of tile c enter the pipe first: the next snapshot,
           // and so the next tile, waits on it
           if (!spin_until_at_least(up_issued, c + 1, abort_flag)) break;
@@ -465,14 +515,15 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       // phi(K) into buffer c&1 once the update of tile c-2 has read it
       if (c >= 2) mbar_wait(&bars[kUpDone0 + s], ((c >> 1) - 1) & 1, abort_flag);
       if (!wg_ok(1, abort_flag)) break;
+      LA_TRACE_AT(1, c, 3);
       {
-        FeatSrc fk;
+        FeatIn fk;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) fk.raw[i] = vrow ? kw[i] : 0u;
-        fk.one_valid = vrow ? 0x3F803F80u : 0u;  // padding tokens add nothing to the state
-        store_phi<false>(fk, sb + kOffPhiK + s * kPhiBytes, row,
-                         std::make_integer_sequence<int, kFPad / 8>{});
+        for (int i = 0; i < 8; ++i) fk.w[i] = vrow ? kw[i] : 0u;
+        fk.one = vrow ? 0x3F80u : 0u;  // padding tokens add nothing to the state
+        store_phik(fk, sb + kOffPhiK + s * kPhiBytes, row, std::make_integer_sequence<int, kFPad / 8>{});
       }
+      LA_TRACE_AT(1, c, 4);
       fence_proxy_async_smem();
       named_barrier_sync(1, 128);
       if (leader) {
@@ -487,17 +538,18 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
         if (!wg_ok(1, abort_flag)) break;
         tc_fence_after();
-        FeatSrc fs;
+        LA_TRACE_AT(1, c, 5);
+        FeatIn fs;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          fs.raw[i] = qw[i];
-          fs.s4[i] = hmul2_bf16(qw[i], 0x3E803E80u);   // x / 4   (exact)
+          fs.w[i] = qw[i];
           fs.s16[i] = hmul2_bf16(qw[i], 0x3D803D80u);  // x / 16  (exact)
           fs.s32[i] = hmul2_bf16(qw[i], 0x3D003D00u);  // x / 32  (exact)
         }
-        fs.one_valid = 0x3F803F80u;
+        fs.one = 0x3F80u;
         store_phiq(fs, taddr(tmem, wq * 32, kColPhiQ), std::make_integer_sequence<int, kFPad / 32>{});
         tmem_wait_st();
+        LA_TRACE_AT(1, c, 6);
         tc_fence_before();
         fence_proxy_async_smem();
         named_barrier_sync(1, 128);
@@ -564,7 +616,9 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           // which the other warp of this quarter may still be reading: store
           // only after both warps have loaded their groups (barrier below).
           if (G2 == 0) {
+            LA_TRACE_AT(2, c, 2);
             named_barrier_sync(5 + wq, 64);
+            LA_TRACE_AT(2, c, 3);
           }
           tmem_st16(taddr(tmem, wq * 32, kColSc + 16 * G), w);
         }
@@ -591,9 +645,9 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       uint32_t w[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const int f = f0 + i;
+        const int f = c_slot_map.f[f0 + i];
         float x = 0.f;
-        if (!kStateOnly && real && f < kF) {
+        if (!kStateOnly && real && f >= 0) {
           if (p.init_state) x = p.init_state[((uint64_t)bh * kF + f) * kSV + e];
           for (int gg = 0; gg < g; ++gg)
             x += p.seg_states[(((uint64_t)bh * p.segments + gg) * kF + f) * kSV + e];
@@ -605,14 +659,12 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
 #pragma unroll
         for (int buf = 0; buf < 2; ++buf) {
           if (buf == 1 && e <= kDv) continue;  // buffer 1: only the zero rows now
-          const uint32_t blk = sb + kOffSnap + buf * kSnapBytes + (f0 >> 6) * kSnapKBlock;
-          const int ch = (f0 & 63) >> 3;
-          st_shared_v4(blk + sw128_offset(e, ch),
+          st_shared_v4(snap_chunk_addr(sb, buf, f0, e),
                        pack_bf16(__uint_as_float(w[0]), __uint_as_float(w[1])),
                        pack_bf16(__uint_as_float(w[2]), __uint_as_float(w[3])),
                        pack_bf16(__uint_as_float(w[4]), __uint_as_float(w[5])),
                        pack_bf16(__uint_as_float(w[6]), __uint_as_float(w[7])));
-          st_shared_v4(blk + sw128_offset(e, ch + 1),
+          st_shared_v4(snap_chunk_addr(sb, buf, f0 + 8, e),
                        pack_bf16(__uint_as_float(w[8]), __uint_as_float(w[9])),
                        pack_bf16(__uint_as_float(w[10]), __uint_as_float(w[11])),
                        pack_bf16(__uint_as_float(w[12]), __uint_as_float(w[13])),
@@ -638,8 +690,8 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int f = col0 + 16 * grp + i;
-            if (real && f < kF) dst[(uint64_t)f * kSV + e] = __uint_as_float(r[i]);
+            const int f = c_slot_map.f[col0 + 16 * grp + i];
+            if (real && f >= 0) dst[(uint64_t)f * kSV + e] = __uint_as_float(r[i]);
           }
         }
       }
@@ -665,13 +717,16 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       auto put_final = [&](int f0, const uint32_t *r) {
         float *dst = p.final_state + (uint64_t)bh * kF * kSV;
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (real && f0 + i < kF) dst[(uint64_t)(f0 + i) * kSV + e] = __uint_as_float(r[i]);
+        for (int i = 0; i < 16; ++i) {
+          const int f = c_slot_map.f[f0 + i];
+          if (real && f >= 0) dst[(uint64_t)f * kSV + e] = __uint_as_float(r[i]);
+        }
       };
       for (int c = 0; c < n_chunks; ++c) {
         // S^T holds S_{c+1} once the update of tile c is done; its snapshot
         // goes to buffer (c+1)&1, last read by phi(Q) S of tile c-1
         mbar_wait(&bars[kSReady], c & 1, abort_flag);
+        LA_TRACE_AT(3, c, 2);
         if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
         if (!wg_ok(3, abort_flag, 256)) break;
         tc_fence_after();
@@ -763,6 +818,13 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     tmem_dealloc(tmem, kTmemCols);
   }
   if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, kErrTimeout);
+#ifdef LA_TRACE
+  if (threadIdx.x == 0 && !kStateOnly && blockIdx.y * gridDim.x + blockIdx.x < kTraceCtas)
+  {
+    la_trace_cta[blockIdx.y * gridDim.x + blockIdx.x][1] = (long long)globaltimer();
+    la_trace_cta[blockIdx.y * gridDim.x + blockIdx.x][4] = clock64();
+  }
+#endif
 }
 
 // ---------------------------------------------------------------- host side
@@ -825,9 +887,14 @@ int launch(const void *q, const void *k, const void *v, const Params &p, int64_t
 
 #ifdef LA_TRACE
 extern "C" int la_debug_read_trace(long long *dst, int count) {
-  const int n = 5 * kTraceChunks * kTraceEvents;
+  const int n = kTraceMaxCtas * 6 * kTraceChunks * kTraceEvents;
   if (count < n) return -1;
   return cudaMemcpyFromSymbol(dst, la_trace_buf, sizeof(long long) * n) == cudaSuccess ? n : -1;
+}
+extern "C" int la_debug_read_cta_trace(long long *dst, int count) {
+  const int n = kTraceCtas * 5;
+  if (count < n) return -1;
+  return cudaMemcpyFromSymbol(dst, la_trace_cta, sizeof(long long) * n) == cudaSuccess ? n : -1;
 }
 #endif
 

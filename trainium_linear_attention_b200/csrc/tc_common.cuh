@@ -62,20 +62,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_try_wait, but the thread may sleep in hardware until the phase
+// completes or about `suspend_ns` nanoseconds pass, instead of returning at
+// once: waiting warps then take no issue slots or shared-memory bandwidth.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity,
+                                                    uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return ok != 0;
+}
+constexpr uint32_t kSuspendNs = 200000;  // one sleep; the abort flag and the clock are checked after each
+
 // Waits for the phase with the given parity to complete.  Returns false if
 // the CTA is aborting (flag set by any thread) or the wait timed out, in
 // which case the CTA's abort flag is raised.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  uint32_t spins = 0;
-  while (!mbar_try_wait(bar, parity)) {
-    if ((++spins & 255u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer() - t0 > kWaitTimeoutNs) {
-        *abort_flag = 1;
-        return false;
-      }
+  while (!mbar_try_wait_sleep(bar, parity, kSuspendNs)) {
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      return false;
     }
   }
   return true;
@@ -89,6 +103,7 @@ __device__ __forceinline__ bool spin_until_at_least(volatile int *counter, int t
   const uint64_t t0 = globaltimer();
   uint32_t spins = 0;
   while (*counter < target) {
+    __nanosleep(20);
     if ((++spins & 255u) == 0) {
       if (*abort_flag) return false;
       if (globaltimer() - t0 > kWaitTimeoutNs) {
