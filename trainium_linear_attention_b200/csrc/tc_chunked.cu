@@ -727,11 +727,26 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         // goes to buffer (c+1)&1, last read by phi(Q) S of tile c-1
         mbar_wait(&bars[kSReady], c & 1, abort_flag);
         LA_TRACE_AT(3, c, 2);
+        if (c == n_chunks - 1) {
+          // the state after the last tile: no tile reads its snapshot; the
+          // last segment writes it out as the final state
+          if (!wg_ok(3, abort_flag, 256)) break;
+          tc_fence_after();
+          if (write_final && wq < 3) {
+#pragma unroll 1
+            for (int grp = 0; grp < 5; ++grp) {
+              uint32_t r[16];
+              tmem_ld16(taddr(tmem, wq * 32, kColS + col0 + 16 * grp), r);
+              tmem_wait_ld();
+              put_final(col0 + 16 * grp, r);
+            }
+          }
+          break;
+        }
         if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
         if (!wg_ok(3, abort_flag, 256)) break;
         tc_fence_after();
         LA_TRACE_AT(3, c, 0);
-        const bool last = write_final && c == n_chunks - 1;
         const uint32_t snap = sb + kOffSnap + ((c + 1) & 1) * kSnapBytes;
         if (wq < 3) {  // rows 96..127 carry nothing
           // five 16-column groups; each group's load overlaps the stores of
@@ -744,9 +759,9 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
             uint32_t *cur = (grp & 1) ? r1 : r0;
             uint32_t *nxt = (grp & 1) ? r0 : r1;
             tmem_wait_ld();
+            LA_TRACE_AT(3, c, 3 + grp);
             if (grp + 1 < 5) tmem_ld16(base + 16 * (grp + 1), nxt);
             put(snap, col0 + 16 * grp, cur);
-            if (last) put_final(col0 + 16 * grp, cur);
           }
         }
         fence_proxy_async_smem();
