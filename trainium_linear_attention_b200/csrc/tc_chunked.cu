@@ -31,16 +31,16 @@
 // c+1 while PV(c) and UP(c+1) run, and P of tile c+1 while UP(c+1) and
 // QS(c+1) run.
 //
-// Warp roles (896 threads, one CTA per SM):
-//   warp 0      TMA producer: Q/K tiles (3-stage ring)
-//   warp 3      TMA producer: V tiles (2-stage ring)
-//   warp 1      TMEM allocator + update MMA issuer (S^T += ...)
-//   warp 2      output MMA issuer (phi(Q) S, P [V 1], scores)
-//   warps 4-7   features: phi(K) -> smem (2 buffers), phi(Q) -> TMEM
-//   warps 8-15  polynomial: scores -> P (TMEM); two warps per TMEM lane quarter
-//   warps 16-23 state: S^T (TMEM, fp32) -> bf16 snapshot in smem (2 buffers);
-//               two warps per lane quarter, 80 feature columns each
-//   warps 24-27 epilogue: O (TMEM) -> normalised bf16 output rows
+// Warp roles (800 threads, one CTA per SM):
+//   warp 19     TMA producer: Q/K tiles (3-stage ring) and V tiles (2-stage ring)
+//   warp 23     TMEM allocator + update MMA issuer (S^T += ...)
+//   warp 24     output MMA issuer (phi(Q) S, P [V 1], scores)
+//   warps 0-3   features: phi(K) -> smem (2 buffers), phi(Q) -> TMEM
+//   warps 4-11  polynomial: scores -> P (TMEM); two warps per TMEM lane quarter
+//   warps 16-18, 20-22  state: S^T (TMEM, fp32) -> bf16 snapshot in smem (2
+//               buffers); lane quarters 0-2 (S^T rows >= 96 are always zero),
+//               two warps per quarter, 80 feature columns each
+//   warps 12-15 epilogue: O (TMEM) -> normalised bf16 output rows
 //
 // The state-only variant (kStateOnly) runs just the phi(K) / update path and
 // writes the segment's state; it seeds the later segments of a head.
@@ -62,9 +62,20 @@ constexpr int kFPad = 160;    // padded feature count (K of phi(Q) S, N of the u
 constexpr int kSV = kDv + 1;  // state columns in global memory: values + normaliser
 constexpr int kNO = 80;       // N of phi(Q) S: 64 values, normaliser, 15 zero rows
 
-constexpr int kWarpTma = 0, kWarpUpd = 1, kWarpOut = 2, kWarpTmaV = 3, kWarpFeat = 4, kWarpPoly = 8,
-              kWarpState = 16, kWarpEpi = 24;
-constexpr int kThreads = 28 * 32;
+// Warp roles.  A warp reaches the TMEM lanes of quarter warp % 4 only, so
+// the TMEM roles come in sets that cover the quarters they need; the three
+// single-thread roles fill the remaining slots.  25 warps leave 80 registers
+// per thread.
+constexpr int kWarpFeat = 0;     // 0..3    features
+constexpr int kWarpPoly = 4;     // 4..11   polynomial (two warps per quarter)
+constexpr int kWarpEpi = 12;     // 12..15  epilogue
+constexpr int kWarpState0 = 16;  // 16..18  state, columns 0..79 (quarters 0..2)
+constexpr int kWarpTma = 19;     //         TMA producer (Q/K and V rings)
+constexpr int kWarpState1 = 20;  // 20..22  state, columns 80..159 (quarters 0..2)
+constexpr int kWarpUpd = 23;     //         TMEM allocator + update MMA issuer
+constexpr int kWarpOut = 24;     //         output MMA issuer
+constexpr int kThreads = 25 * 32;
+constexpr int kStateThreads = 6 * 32;
 
 // TMEM columns (one CTA per SM owns all 512)
 constexpr uint32_t kColS = 0;       // S^T    128 lanes x 160 fp32
@@ -350,42 +361,54 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kWarpTma || warp == kWarpTmaV) {
-    // ------------------------------------------------------------ TMA producers
-    // warp 0 streams the Q/K tiles (3 stages), warp 3 the V tiles (2 stages);
-    // each ring is released by its own consumers, so K can run ahead of V.
+  if (warp == kWarpTma) {
+    // ------------------------------------------------------------ TMA producer
+    // One thread feeds both rings, each released by its own consumers: it
+    // issues whichever next copy has a free stage, so K can run ahead of V.
     if (lane == 0) {
-      const bool is_v = warp == kWarpTmaV;
-      const int stages = is_v ? kVStages : kQKStages;
-      const int full0 = is_v ? kVFull0 : kQKFull0;
-      const int empty0 = is_v ? kVEmpty0 : kQKEmpty0;
-      if (is_v) {
-        prefetch_tmap(&tm_v);
-      } else {
-        prefetch_tmap(&tm_k);
-        if (!kStateOnly) prefetch_tmap(&tm_q);
-      }
-      int issued = 0;
-      for (int c = 0; c < n_chunks; ++c) {
-        const int st = c % stages;
-        const int round = c / stages;
-        if (round > 0 && !mbar_wait(&bars[empty0 + st], (round - 1) & 1, abort_flag)) break;
-        const int row = (int)(t_begin + (int64_t)c * kT);
-        LA_TRACE_AT(5, c, is_v ? 1 : 0);
-        if (is_v) {
-          mbar_arrive_expect_tx(&bars[full0 + st], kVBytes);
-          tma_load_3d(smem + kOffV + st * kVBytes, &tm_v, &bars[full0 + st], 0, row, (int)bh);
-        } else {
-          mbar_arrive_expect_tx(&bars[full0 + st], kStateOnly ? kQBytes : 2 * kQBytes);
-          if (!kStateOnly)
-            tma_load_3d(smem + kOffQ + st * kQBytes, &tm_q, &bars[full0 + st], 0, row, (int)bh);
-          tma_load_3d(smem + kOffK + st * kQBytes, &tm_k, &bars[full0 + st], 0, row, (int)bh);
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
+      if (!kStateOnly) prefetch_tmap(&tm_q);
+      int cq = 0, cv = 0;  // next tiles to load
+      uint64_t t_idle = globaltimer();
+      while ((cq < n_chunks || cv < n_chunks) && !*abort_flag) {
+        bool progress = false;
+        if (cq < n_chunks) {
+          const int st = cq % kQKStages, round = cq / kQKStages;
+          if (round == 0 || mbar_try_wait(&bars[kQKEmpty0 + st], (round - 1) & 1)) {
+            const int row = (int)(t_begin + (int64_t)cq * kT);
+            LA_TRACE_AT(5, cq, 0);
+            mbar_arrive_expect_tx(&bars[kQKFull0 + st], kStateOnly ? kQBytes : 2 * kQBytes);
+            if (!kStateOnly)
+              tma_load_3d(smem + kOffQ + st * kQBytes, &tm_q, &bars[kQKFull0 + st], 0, row, (int)bh);
+            tma_load_3d(smem + kOffK + st * kQBytes, &tm_k, &bars[kQKFull0 + st], 0, row, (int)bh);
+            ++cq;
+            progress = true;
+          }
         }
-        issued = c + 1;
+        if (cv < n_chunks) {
+          const int st = cv % kVStages, round = cv / kVStages;
+          if (round == 0 || mbar_try_wait(&bars[kVEmpty0 + st], (round - 1) & 1)) {
+            const int row = (int)(t_begin + (int64_t)cv * kT);
+            LA_TRACE_AT(5, cv, 1);
+            mbar_arrive_expect_tx(&bars[kVFull0 + st], kVBytes);
+            tma_load_3d(smem + kOffV + st * kVBytes, &tm_v, &bars[kVFull0 + st], 0, row, (int)bh);
+            ++cv;
+            progress = true;
+          }
+        }
+        if (progress) {
+          t_idle = globaltimer();
+        } else {
+          __nanosleep(64);
+          if (globaltimer() - t_idle > kWaitTimeoutNs) *abort_flag = 1;
+        }
       }
       // every issued copy must land before the CTA can exit
-      for (int c = issued - stages < 0 ? 0 : issued - stages; c < issued; ++c)
-        wait_teardown(&bars[full0 + c % stages], (c / stages) & 1);
+      for (int c = cq - kQKStages < 0 ? 0 : cq - kQKStages; c < cq; ++c)
+        wait_teardown(&bars[kQKFull0 + c % kQKStages], (c / kQKStages) & 1);
+      for (int c = cv - kVStages < 0 ? 0 : cv - kVStages; c < cv; ++c)
+        wait_teardown(&bars[kVFull0 + c % kVStages], (c / kVStages) & 1);
     }
   } else if (warp == kWarpUpd || warp == kWarpOut) {
     // ------------------------------------------------------------ MMA issuers
@@ -560,7 +583,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         LA_TRACE_AT(1, c, 2);
       }
     }
-  } else if (warp < kWarpState) {
+  } else if (warp < kWarpEpi) {
     // ------------------------------------------------------------ polynomial
     if (!kStateOnly) {
       const int wq = warp & 3;              // TMEM lane quarter: query rows 32wq ..
@@ -572,7 +595,6 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       for (int c = 0; c < n_chunks; ++c) {
         const int64_t t0 = t_begin + (int64_t)c * kT;
         const int valid = (int)min64(kT, t_end - t0);
-        const bool full_tile = valid == kT;
         mbar_wait(&bars[kScReady], c & 1, abort_flag);
         if (!wg_ok(2, abort_flag, 256)) break;
         tc_fence_after();
@@ -589,23 +611,17 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
             tmem_ld16(taddr(tmem, wq * 32, kColSc + 32 * G), r);
             tmem_ld16(taddr(tmem, wq * 32, kColSc + 32 * G + 16), r + 16);
             tmem_wait_ld();
-            if (G < wq && full_tile) {
+            // keys 32G .. 32G + m of this group are visible to this row (one
+            // masked body for every group keeps the hot loop's code small)
+            const int m = min(row, valid - 1) - 32 * G;
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const uint64_t s2 = f2pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-                w[i] = pack_bf16x2(ffma2(s2, ffma2(s2, c32, c4), one2));
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const int j0 = 32 * G + 2 * i;
-                const uint64_t s2 = f2pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-                float p0, p1;
-                f2unpack(ffma2(s2, ffma2(s2, c32, c4), one2), p0, p1);
-                p0 = (j0 <= row && j0 < valid) ? p0 : 0.f;
-                p1 = (j0 + 1 <= row && j0 + 1 < valid) ? p1 : 0.f;
-                w[i] = pack_bf16(p0, p1);
-              }
+            for (int i = 0; i < 16; ++i) {
+              const uint64_t s2 = f2pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+              float p0, p1;
+              f2unpack(ffma2(s2, ffma2(s2, c32, c4), one2), p0, p1);
+              p0 = 2 * i <= m ? p0 : 0.f;
+              p1 = 2 * i + 1 <= m ? p1 : 0.f;
+              w[i] = pack_bf16(p0, p1);
             }
           } else {
 #pragma unroll
@@ -629,13 +645,13 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         LA_TRACE_AT(2, c, 1);
       }
     }
-  } else if (warp < kWarpEpi) {
+  } else if (warp >= kWarpState0) {
     // ------------------------------------------------------------ state
-    const int wq = warp & 3;
-    const int half = (warp - kWarpState) >> 2;
+    const int wq = warp & 3;       // quarters 0..2: S^T rows 0..95
+    const int half = warp >= kWarpState1 ? 1 : 0;
     const int e = wq * 32 + lane;  // row of S^T: value column e (< 64), normaliser (64)
     const int col0 = 80 * half;    // this warp's 80 feature columns
-    const bool leader = (warp == kWarpState && lane == 0);
+    const bool leader = (warp == kWarpState0 && lane == 0);
     const bool real = e < kSV;
     // S_0 = init_state + states of the earlier segments (fixed order).  Rows
     // 65..79 of both snapshot buffers are zero for good (S^T rows >= 65 never
@@ -675,13 +691,13 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     tmem_wait_st();
     fence_proxy_async_smem();
     tc_fence_before();
-    named_barrier_sync(3, 256);
+    named_barrier_sync(3, kStateThreads);
     if (leader) mbar_arrive(&bars[kSnapReady0]);
 
     if (kStateOnly) {
       // the segment's state, once every update has completed
       mbar_wait(&bars[kDone], 0, abort_flag);
-      if (wg_ok(3, abort_flag, 256)) {
+      if (wg_ok(3, abort_flag, kStateThreads)) {
         tc_fence_after();
         float *dst = p.seg_out + ((uint64_t)bh * p.segments + g) * kF * kSV;
         for (int grp = 0; grp < 5; ++grp) {
@@ -730,9 +746,9 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         if (c == n_chunks - 1) {
           // the state after the last tile: no tile reads its snapshot; the
           // last segment writes it out as the final state
-          if (!wg_ok(3, abort_flag, 256)) break;
+          if (!wg_ok(3, abort_flag, kStateThreads)) break;
           tc_fence_after();
-          if (write_final && wq < 3) {
+          if (write_final) {
 #pragma unroll 1
             for (int grp = 0; grp < 5; ++grp) {
               uint32_t r[16];
@@ -744,11 +760,11 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           break;
         }
         if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
-        if (!wg_ok(3, abort_flag, 256)) break;
+        if (!wg_ok(3, abort_flag, kStateThreads)) break;
         tc_fence_after();
         LA_TRACE_AT(3, c, 0);
         const uint32_t snap = sb + kOffSnap + ((c + 1) & 1) * kSnapBytes;
-        if (wq < 3) {  // rows 96..127 carry nothing
+        {
           // five 16-column groups; each group's load overlaps the stores of
           // the previous one
           uint32_t r0[16], r1[16];
@@ -766,7 +782,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         }
         fence_proxy_async_smem();
         tc_fence_before();
-        named_barrier_sync(3, 256);
+        named_barrier_sync(3, kStateThreads);
         if (leader) mbar_arrive(&bars[kSnapReady0 + ((c + 1) & 1)]);
         LA_TRACE_AT(3, c, 1);
       }
