@@ -245,16 +245,23 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
     return LA_ERR_INVALID_ARGUMENT;  // nothing to reuse without segments
   }
   const bool normalize = (flags & LA_CHUNKED_NORMALIZE) != 0;
+  // With two segments the state pass covers only the first: it runs as two
+  // half-length pieces so that it fills as many SMs as the output pass.
+  const int ratio =
+      (tc && g == 2 && !(flags & LA_CHUNKED_REUSE_SEGMENTS) && seg_len % (2 * kSegmentTile) == 0)
+          ? 2
+          : 1;
   if (g > 1 && !(flags & LA_CHUNKED_REUSE_SEGMENTS)) {
     // states of segments 0 .. g-2 seed the later segments
-    st = tc ? launch_chunked_state_tc(k, v, seg_states, bh, seq_len, g, g - 1, seg_len, info, s)
+    st = tc ? launch_chunked_state_tc(k, v, seg_states, bh, seq_len, g, (g - 1) * ratio,
+                                      seg_len / ratio, info, s)
             : launch_chunked_state_simt(k, v, seg_states, bh, seq_len, (int)d_qk, (int)d_v,
                                         dtype, g, seg_len, s);
     if (st != LA_OK) return st;
   }
   if (tc)
     return launch_chunked_output_tc(q, k, v, out, init_state, final_state, seg_states, bh,
-                                    seq_len, eps, normalize, g, seg_len, info, s);
+                                    seq_len, eps, normalize, g, ratio, seg_len, info, s);
   return launch_chunked_output_simt(q, k, v, out, init_state, final_state, seg_states, bh,
                                     seq_len, (int)d_qk, (int)d_v, dtype, eps, normalize, g,
                                     seg_len, s);

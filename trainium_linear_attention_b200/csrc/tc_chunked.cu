@@ -87,37 +87,47 @@ constexpr uint32_t kTmemCols = 512;
 // Shared memory (offsets from a 1024-byte aligned base)
 constexpr uint32_t kQBytes = kT * kDqk * 2;         // 4 KB, 32B-swizzled rows
 constexpr uint32_t kVBytes = kT * kDv * 2;          // 16 KB, 128B-swizzled rows
-constexpr int kQKStages = 3;                        // Q/K ring
-constexpr int kVStages = 2;                         // V ring
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kOffQ + kQKStages * kQBytes;
-constexpr uint32_t kOffV = kOffK + kQKStages * kQBytes;     // 24576
-constexpr uint32_t kOffOnes = kOffV + kVStages * kVBytes;   // 57344: 16 rows x 128 B
 constexpr uint32_t kPhiBlock = kT * 128;            // 64 features of 128 tokens
 constexpr uint32_t kPhiBytes = 3 * kPhiBlock;       // 160 features (3 blocks)
-constexpr uint32_t kOffPhiK = kOffOnes + 2048;      // 59392: 2 buffers
 // Snapshots of S: the K-major B operand of phi(Q) S, 80 rows x 160 features
 // in three 64-feature blocks of 80 x 128 B.  (Letting the two buffers share
 // their half-used third block was measured 19% slower: the state warps then
 // store into 128-byte rows the tensor core is reading.)
 constexpr uint32_t kSnapKBlock = kNO * 128;         // 10 KB per 64-feature block
 constexpr uint32_t kSnapBytes = 3 * kSnapKBlock;
-constexpr uint32_t kOffSnap = kOffPhiK + 2 * kPhiBytes;  // 157696: 2 x 30 KB
-constexpr uint32_t kOffBar = kOffSnap + 2 * kSnapBytes;  // 219136
-constexpr uint32_t kSmemBytes = kOffBar + 256;
-constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;       // alignment slack
+constexpr int kMaxStages = 6;
 
-static_assert(kOffV % 1024 == 0 && kOffOnes % 1024 == 0 && kOffPhiK % 1024 == 0 &&
-                  kPhiBytes % 1024 == 0 && kOffSnap % 1024 == 0 && kSnapKBlock % 1024 == 0,
-              "128B-swizzled regions need 1024-byte alignment");
-static_assert(kSmemAlloc <= 227 * 1024, "shared memory budget");
+// Shared-memory layout (offsets from a 1024-byte aligned base).  The full
+// kernel: Q/K ring (3 stages), V ring (2), ones block, phi(K) x 2, snapshots
+// x 2.  The state-only kernel needs no Q, phi(Q) or snapshots and spends the
+// room on deeper K and V rings, since nothing else hides its load latency.
+template <bool kStateOnly>
+struct Layout {
+  static constexpr int kQKStages = kStateOnly ? 6 : 3;
+  static constexpr int kVStages = kStateOnly ? 6 : 2;
+  static constexpr uint32_t kOffQ = 0;
+  static constexpr uint32_t kOffK = kOffQ + (kStateOnly ? 0 : kQKStages * kQBytes);
+  static constexpr uint32_t kOffV = kOffK + kQKStages * kQBytes;
+  static constexpr uint32_t kOffOnes = kOffV + kVStages * kVBytes;  // 16 rows x 128 B
+  static constexpr uint32_t kOffPhiK = kOffOnes + 2048;
+  static constexpr uint32_t kOffSnap = kOffPhiK + 2 * kPhiBytes;
+  static constexpr uint32_t kOffBar = kOffSnap + (kStateOnly ? 0 : 2 * kSnapBytes);
+  static constexpr uint32_t kSmemAlloc = kOffBar + 512 + 1024;  // barriers, alignment slack
+  static_assert(kQKStages <= kMaxStages && kVStages <= kMaxStages, "barrier slots");
+  static_assert(kOffV % 1024 == 0 && kOffOnes % 1024 == 0 && kOffPhiK % 1024 == 0 &&
+                    kPhiBytes % 1024 == 0 && kOffSnap % 1024 == 0 && kSnapKBlock % 1024 == 0,
+                "128B-swizzled regions need 1024-byte alignment");
+  static_assert(kSmemAlloc <= 227 * 1024, "shared memory budget");
+};
 
-// Barriers.  Per-buffer pairs (..0/..1) complete once per two tiles; a
-// producer that may run two tiles ahead of its consumer needs them.
-enum Bar { kQKFull0, kQKFull1, kQKFull2, kQKEmpty0, kQKEmpty1, kQKEmpty2, kVFull0, kVFull1,
-           kVEmpty0, kVEmpty1, kPhiKReady0, kPhiKReady1, kUpDone0, kUpDone1,
-           kQSDone0, kQSDone1, kSnapReady0, kSnapReady1, kPhiQReady, kScReady, kPReady, kOReady,
-           kOFree, kSReady, kDone, kNumBars };
+// Barriers.  Ring stages have their own full/empty pairs; per-buffer pairs
+// (..0/..1) complete once per two tiles (a producer that may run two tiles
+// ahead of its consumer needs them).
+enum Bar { kQKFull = 0, kQKEmpty = kQKFull + kMaxStages, kVFull = kQKEmpty + kMaxStages,
+           kVEmpty = kVFull + kMaxStages, kPhiKReady0 = kVEmpty + kMaxStages, kPhiKReady1,
+           kUpDone0, kUpDone1, kQSDone0, kQSDone1, kSnapReady0, kSnapReady1, kPhiQReady, kScReady,
+           kPReady, kOReady, kOFree, kSReady, kDone, kNumBars };
+static_assert(8 * kNumBars + 12 <= 512, "barrier area");
 
 // Optional per-role timeline of CTA (0, 0), compiled in with -DLA_TRACE only.
 #ifdef LA_TRACE
@@ -278,7 +288,8 @@ __device__ __forceinline__ void store_phiq(const FeatIn &s, uint32_t addr0,
 // Shared-memory address of the 16-byte chunk holding features f0 .. f0+7
 // (f0 a multiple of 8) of snapshot row e in buffer `buf`.
 __device__ __forceinline__ uint32_t snap_chunk_addr(uint32_t sb, int buf, int f0, int e) {
-  return sb + kOffSnap + buf * kSnapBytes + (f0 >> 6) * kSnapKBlock + sw128_offset(e, (f0 & 63) >> 3);
+  return sb + Layout<false>::kOffSnap + buf * kSnapBytes + (f0 >> 6) * kSnapKBlock +
+         sw128_offset(e, (f0 & 63) >> 3);
 }
 
 struct Params {
@@ -290,7 +301,8 @@ struct Params {
   int *err;                 // device error word
   int64_t n;
   int64_t seg_len;
-  int segments;
+  int segments;             // segment count (the per-head stride of seg_states)
+  int state_ratio;          // state entries per earlier segment in seg_states
   float eps;
   int normalize;
 };
@@ -306,6 +318,10 @@ template <bool kStateOnly>
 __global__ void __launch_bounds__(kThreads, 1)
 chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  using L = Layout<kStateOnly>;
+  constexpr int kQKStages = L::kQKStages, kVStages = L::kVStages;
+  constexpr uint32_t kOffQ = L::kOffQ, kOffK = L::kOffK, kOffV = L::kOffV, kOffOnes = L::kOffOnes,
+                     kOffPhiK = L::kOffPhiK, kOffSnap = L::kOffSnap, kOffBar = L::kOffBar;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t sb = smem_u32(smem);
@@ -338,8 +354,8 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     // P V, `done` by both MMA issuers
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t count = 1;
-      if (i >= kQKEmpty0 && i <= kQKEmpty2) count = kStateOnly ? 1 : 2;
-      if (i == kVEmpty0 || i == kVEmpty1) count = kStateOnly ? 1 : 2;
+      if (i >= kQKEmpty && i < kQKEmpty + kMaxStages) count = kStateOnly ? 1 : 2;
+      if (i >= kVEmpty && i < kVEmpty + kMaxStages) count = kStateOnly ? 1 : 2;
       if (i == kDone) count = 2;
       mbar_init(&bars[i], count);
     }
@@ -375,24 +391,24 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         bool progress = false;
         if (cq < n_chunks) {
           const int st = cq % kQKStages, round = cq / kQKStages;
-          if (round == 0 || mbar_try_wait(&bars[kQKEmpty0 + st], (round - 1) & 1)) {
+          if (round == 0 || mbar_try_wait(&bars[kQKEmpty + st], (round - 1) & 1)) {
             const int row = (int)(t_begin + (int64_t)cq * kT);
             LA_TRACE_AT(5, cq, 0);
-            mbar_arrive_expect_tx(&bars[kQKFull0 + st], kStateOnly ? kQBytes : 2 * kQBytes);
+            mbar_arrive_expect_tx(&bars[kQKFull + st], kStateOnly ? kQBytes : 2 * kQBytes);
             if (!kStateOnly)
-              tma_load_3d(smem + kOffQ + st * kQBytes, &tm_q, &bars[kQKFull0 + st], 0, row, (int)bh);
-            tma_load_3d(smem + kOffK + st * kQBytes, &tm_k, &bars[kQKFull0 + st], 0, row, (int)bh);
+              tma_load_3d(smem + kOffQ + st * kQBytes, &tm_q, &bars[kQKFull + st], 0, row, (int)bh);
+            tma_load_3d(smem + kOffK + st * kQBytes, &tm_k, &bars[kQKFull + st], 0, row, (int)bh);
             ++cq;
             progress = true;
           }
         }
         if (cv < n_chunks) {
           const int st = cv % kVStages, round = cv / kVStages;
-          if (round == 0 || mbar_try_wait(&bars[kVEmpty0 + st], (round - 1) & 1)) {
+          if (round == 0 || mbar_try_wait(&bars[kVEmpty + st], (round - 1) & 1)) {
             const int row = (int)(t_begin + (int64_t)cv * kT);
             LA_TRACE_AT(5, cv, 1);
-            mbar_arrive_expect_tx(&bars[kVFull0 + st], kVBytes);
-            tma_load_3d(smem + kOffV + st * kVBytes, &tm_v, &bars[kVFull0 + st], 0, row, (int)bh);
+            mbar_arrive_expect_tx(&bars[kVFull + st], kVBytes);
+            tma_load_3d(smem + kOffV + st * kVBytes, &tm_v, &bars[kVFull + st], 0, row, (int)bh);
             ++cv;
             progress = true;
           }
@@ -406,9 +422,9 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       }
       // every issued copy must land before the CTA can exit
       for (int c = cq - kQKStages < 0 ? 0 : cq - kQKStages; c < cq; ++c)
-        wait_teardown(&bars[kQKFull0 + c % kQKStages], (c / kQKStages) & 1);
+        wait_teardown(&bars[kQKFull + c % kQKStages], (c / kQKStages) & 1);
       for (int c = cv - kVStages < 0 ? 0 : cv - kVStages; c < cv; ++c)
-        wait_teardown(&bars[kVFull0 + c % kVStages], (c / kVStages) & 1);
+        wait_teardown(&bars[kVFull + c % kVStages], (c / kVStages) & 1);
     }
   } else if (warp == kWarpUpd || warp == kWarpOut) {
     // ------------------------------------------------------------ MMA issuers
@@ -426,8 +442,9 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     const uint32_t a_ones = sb + kOffOnes;
     if (lane == 0 && warp == kWarpUpd) {
       for (int c = 0; c < n_chunks; ++c) {
-        const int b = c & 1;
-        if (!mbar_wait(&bars[kVFull0 + b], (c >> 1) & 1, abort_flag)) break;
+        const int b = c & 1;          // phi(K) buffer
+        const int sv = c % kVStages;  // V stage
+        if (!mbar_wait(&bars[kVFull + sv], (c / kVStages) & 1, abort_flag)) break;
         LA_TRACE_AT(0, c, 7);
         if (!mbar_wait(&bars[kPhiKReady0 + b], (c >> 1) & 1, abort_flag)) break;
         // S^T may change once the snapshot of S_c has been read out
@@ -435,15 +452,15 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           break;
         tc_fence_after();
         LA_TRACE_AT(0, c, 0);
-        const uint32_t v_base = sb + kOffV + b * kVBytes;
+        const uint32_t v_base = sb + kOffV + sv * kVBytes;
         const uint64_t db0 = make_sdesc(sb + kOffPhiK + b * kPhiBytes, kPhiBlock, 1024, kSwizzle128B);
         const uint64_t da0 = make_sdesc(v_base, a_ones - v_base, 1024, kSwizzle128B);
 #pragma unroll
         for (int j = 0; j < kT / 16; ++j)
           umma_ss(tmem + kColS, da0 + kStep * j, db0 + (uint64_t)((j * 2048) >> 4), id_up, 1u);
-        umma_commit(&bars[kSReady]);
+        if (!kStateOnly) umma_commit(&bars[kSReady]);
         umma_commit(&bars[kUpDone0 + b]);
-        umma_commit(&bars[kVEmpty0 + b]);
+        umma_commit(&bars[kVEmpty + sv]);
         *up_issued = c + 1;  // the state update of tile c is in the pipe
       }
       umma_commit(&bars[kDone]);
@@ -457,9 +474,9 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           const uint64_t db = make_sdesc(sb + kOffK + s * kQBytes, 16, 256, kSwizzle32B);
           umma_ss(tmem + kColSc, da, db, id_sc, 0);
           umma_commit(&bars[kScReady]);
-          umma_commit(&bars[kQKEmpty0 + s]);
+          umma_commit(&bars[kQKEmpty + s]);
         };
-        bool ok = mbar_wait(&bars[kQKFull0], 0, abort_flag);
+        bool ok = mbar_wait(&bars[kQKFull], 0, abort_flag);
         if (ok) {
           tc_fence_after();
           issue_scores(0);
@@ -489,10 +506,11 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           // O += P [V 1]: B = V (64 columns) with the ones block as its second
           // 64-column block (LBO), so O[:, 64] also collects the row sum of P.
           if (!mbar_wait(&bars[kPReady], c & 1, abort_flag)) break;
-          if (!mbar_wait(&bars[kVFull0 + b], (c >> 1) & 1, abort_flag)) break;
+          const int sv = c % kVStages;
+          if (!mbar_wait(&bars[kVFull + sv], (c / kVStages) & 1, abort_flag)) break;
           tc_fence_after();
           LA_TRACE_AT(0, c, 2);
-          const uint32_t v_base = sb + kOffV + b * kVBytes;
+          const uint32_t v_base = sb + kOffV + sv * kVBytes;
           const uint64_t db0 = make_sdesc(v_base, a_ones - v_base, 1024, kSwizzle128B);
 #pragma unroll
           for (int j = 0; j < kT / 16; ++j)
@@ -501,11 +519,11 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           // the scores of tile c+1 overwrite P(c): wait for P V to finish;
           // that also ends this issuer's use of TMA stage b
           if (!mbar_wait(&bars[kOReady], c & 1, abort_flag)) break;
-          mbar_arrive(&bars[kVEmpty0 + b]);
+          mbar_arrive(&bars[kVEmpty + sv]);
           LA_TRACE_AT(0, c, 3);
           if (c + 1 < n_chunks) {
             const int c1 = c + 1;
-            if (!mbar_wait(&bars[kQKFull0 + c1 % kQKStages], (c1 / kQKStages) & 1, abort_flag)) break;
+            if (!mbar_wait(&bars[kQKFull + c1 % kQKStages], (c1 / kQKStages) & 1, abort_flag)) break;
             tc_fence_after();
             issue_scores(c + 1);
           }
@@ -521,7 +539,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     for (int c = 0; c < n_chunks; ++c) {
       const int s = c & 1;           // phi(K) buffer
       const int sq = c % kQKStages;  // Q/K stage
-      mbar_wait(&bars[kQKFull0 + sq], (c / kQKStages) & 1, abort_flag);
+      mbar_wait(&bars[kQKFull + sq], (c / kQKStages) & 1, abort_flag);
       if (!wg_ok(1, abort_flag)) break;
       LA_TRACE_AT(1, c, 0);
       const int valid = (int)min64(kT, t_end - (t_begin + (int64_t)c * kT));
@@ -553,7 +571,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         mbar_arrive(&bars[kPhiKReady0 + s]);
         // kw has been consumed (and, in the state pass, the stage is done):
         // the next TMA copy may overwrite it
-        if (kStateOnly) mbar_arrive(&bars[kQKEmpty0 + sq]);
+        if (kStateOnly) mbar_arrive(&bars[kQKEmpty + sq]);
       }
       LA_TRACE_AT(1, c, 1);
       if (!kStateOnly) {
@@ -578,7 +596,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         named_barrier_sync(1, 128);
         if (leader) {
           mbar_arrive(&bars[kPhiQReady]);
-          mbar_arrive(&bars[kQKEmpty0 + sq]);  // qw consumed too: release the stage
+          mbar_arrive(&bars[kQKEmpty + sq]);  // qw consumed too: release the stage
         }
         LA_TRACE_AT(1, c, 2);
       }
@@ -665,7 +683,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         float x = 0.f;
         if (!kStateOnly && real && f >= 0) {
           if (p.init_state) x = p.init_state[((uint64_t)bh * kF + f) * kSV + e];
-          for (int gg = 0; gg < g; ++gg)
+          for (int gg = 0; gg < g * p.state_ratio; ++gg)
             x += p.seg_states[(((uint64_t)bh * p.segments + gg) * kF + f) * kSV + e];
         }
         w[i] = __float_as_uint(x);
@@ -906,6 +924,7 @@ int launch(const void *q, const void *k, const void *v, const Params &p, int64_t
   } else if (!make_map(&mq, q, bh, p.n, kDqk, CU_TENSOR_MAP_SWIZZLE_32B)) {
     return LA_ERR_CUDA;
   }
+  constexpr uint32_t kSmemAlloc = Layout<kStateOnly>::kSmemAlloc;
   cudaError_t e = cudaFuncSetAttribute(chunked_tc_kernel<kStateOnly>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
   if (e != cudaSuccess) return LA_ERR_CUDA;
@@ -939,6 +958,7 @@ int launch_chunked_state_tc(const void *k, const void *v, float *seg_states, int
   p.n = n;
   p.seg_len = seg_len;
   p.segments = segments;
+  p.state_ratio = 1;
   if (!p.err) return LA_ERR_CUDA;
   return launch<true>(nullptr, k, v, p, bh, n_launch, s);
 }
@@ -946,7 +966,7 @@ int launch_chunked_state_tc(const void *k, const void *v, float *seg_states, int
 int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *out,
                              const float *init_state, float *final_state,
                              const float *seg_states, int64_t bh, int64_t n, float eps,
-                             bool normalize, int segments, int64_t seg_len,
+                             bool normalize, int segments, int state_ratio, int64_t seg_len,
                              const DeviceInfo &info, cudaStream_t s) {
   (void)info;
   Params p{};
@@ -958,6 +978,7 @@ int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *
   p.n = n;
   p.seg_len = seg_len;
   p.segments = segments;
+  p.state_ratio = state_ratio;
   p.eps = eps;
   p.normalize = normalize ? 1 : 0;
   if (!p.err) return LA_ERR_CUDA;

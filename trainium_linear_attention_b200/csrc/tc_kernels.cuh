@@ -21,14 +21,18 @@ int launch_parallel_tc(const void *q, const void *k, const void *v, void *out, i
                        int64_t n, float eps, const DeviceInfo &info, cudaStream_t s);
 
 // State pass over segments [0, n_launch) of every head (n_launch <= segments).
+// States of the n_launch leading pieces of length seg_len of every head into
+// seg_states[bh][0 .. n_launch) (per-head stride `segments` entries).
 int launch_chunked_state_tc(const void *k, const void *v, float *seg_states, int64_t bh,
                             int64_t n, int segments, int n_launch, int64_t seg_len,
                             const DeviceInfo &info, cudaStream_t s);
 
+// Output of `segments` segments of length seg_len; segment g is seeded with
+// init_state + seg_states[bh][0 .. g * state_ratio).
 int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *out,
                              const float *init_state, float *final_state,
                              const float *seg_states, int64_t bh, int64_t n, float eps,
-                             bool normalize, int segments, int64_t seg_len,
+                             bool normalize, int segments, int state_ratio, int64_t seg_len,
                              const DeviceInfo &info, cudaStream_t s);
 
 int launch_sliding_tc(const void *q, const void *k, const void *v, void *out, int64_t bh,
