@@ -64,8 +64,9 @@ constexpr int kNO = 80;       // N of phi(Q) S: 64 values, normaliser, 15 zero r
 
 // Warp roles.  A warp reaches the TMEM lanes of quarter warp % 4 only, so
 // the TMEM roles come in sets that cover the quarters they need; the three
-// single-thread roles fill the remaining slots.  25 warps leave 80 registers
-// per thread.
+// single-thread roles fill the remaining slots.  (The register file is split
+// between the four schedulers; 25 warps put 7 on one of them, which leaves 72
+// registers per thread.)
 constexpr int kWarpFeat = 0;     // 0..3    features
 constexpr int kWarpPoly = 4;     // 4..11   polynomial (two warps per quarter)
 constexpr int kWarpEpi = 12;     // 12..15  epilogue
@@ -125,7 +126,7 @@ struct Layout {
 // ahead of its consumer needs them).
 enum Bar { kQKFull = 0, kQKEmpty = kQKFull + kMaxStages, kVFull = kQKEmpty + kMaxStages,
            kVEmpty = kVFull + kMaxStages, kPhiKReady0 = kVEmpty + kMaxStages, kPhiKReady1,
-           kUpDone0, kUpDone1, kQSDone0, kQSDone1, kSnapReady0, kSnapReady1, kPhiQReady, kScReady,
+           kUpDone0, kUpDone1, kQSDone0, kQSDone1, kSnapReady0, kSnapReady1, kSRead, kPhiQReady, kScReady,
            kPReady, kOReady, kOFree, kSReady, kDone, kNumBars };
 static_assert(8 * kNumBars + 12 <= 512, "barrier area");
 
@@ -447,9 +448,8 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         if (!mbar_wait(&bars[kVFull + sv], (c / kVStages) & 1, abort_flag)) break;
         LA_TRACE_AT(0, c, 7);
         if (!mbar_wait(&bars[kPhiKReady0 + b], (c >> 1) & 1, abort_flag)) break;
-        // S^T may change once the snapshot of S_c has been read out
-        if ((c == 0 || !kStateOnly) && !mbar_wait(&bars[kSnapReady0 + b], (c >> 1) & 1, abort_flag))
-          break;
+        // S^T may change once the state warps have read S_c out of it
+        if ((c == 0 || !kStateOnly) && !mbar_wait(&bars[kSRead], c & 1, abort_flag)) break;
         tc_fence_after();
         LA_TRACE_AT(0, c, 0);
         const uint32_t v_base = sb + kOffV + sv * kVBytes;
@@ -710,7 +710,10 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     fence_proxy_async_smem();
     tc_fence_before();
     named_barrier_sync(3, kStateThreads);
-    if (leader) mbar_arrive(&bars[kSnapReady0]);
+    if (leader) {
+      mbar_arrive(&bars[kSRead]);  // S_0 is in TMEM
+      mbar_arrive(&bars[kSnapReady0]);
+    }
 
     if (kStateOnly) {
       // the segment's state, once every update has completed
@@ -777,27 +780,35 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           }
           break;
         }
-        if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
         if (!wg_ok(3, abort_flag, kStateThreads)) break;
         tc_fence_after();
         LA_TRACE_AT(3, c, 0);
-        const uint32_t snap = sb + kOffSnap + ((c + 1) & 1) * kSnapBytes;
+        // S_{c+1} -> bf16 snapshot buffer (c+1)&1, last read by phi(Q) S of
+        // tile c-1.  S^T is released to the next update as soon as the last
+        // TMEM load has landed, before the last group is stored.
+        if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
         {
-          // five 16-column groups; each group's load overlaps the stores of
-          // the previous one
-          uint32_t r0[16], r1[16];
+          const uint32_t snap = sb + kOffSnap + ((c + 1) & 1) * kSnapBytes;
           const uint32_t base = taddr(tmem, wq * 32, kColS + col0);
+          uint32_t r0[16], r1[16];
           tmem_ld16(base, r0);
 #pragma unroll
           for (int grp = 0; grp < 5; ++grp) {
             uint32_t *cur = (grp & 1) ? r1 : r0;
             uint32_t *nxt = (grp & 1) ? r0 : r1;
             tmem_wait_ld();
-            LA_TRACE_AT(3, c, 3 + grp);
-            if (grp + 1 < 5) tmem_ld16(base + 16 * (grp + 1), nxt);
+            if (grp + 1 < 5) {
+              tmem_ld16(base + 16 * (grp + 1), nxt);
+            } else {
+              tc_fence_before();
+              named_barrier_sync(3, kStateThreads);
+              if (leader) mbar_arrive(&bars[kSRead]);
+              LA_TRACE_AT(3, c, 6);
+            }
             put(snap, col0 + 16 * grp, cur);
           }
         }
+        LA_TRACE_AT(3, c, 7);
         fence_proxy_async_smem();
         tc_fence_before();
         named_barrier_sync(3, kStateThreads);
@@ -818,40 +829,47 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         if (!wg_ok(4, abort_flag)) break;
         tc_fence_after();
         LA_TRACE_AT(4, c, 0);
-        // O leaves TMEM in two round trips: (denominator, values 0..31), then
-        // values 32..63
-        uint32_t o[32];
+        // O leaves TMEM in two round trips, (denominator, values 0..31) then
+        // values 32..63, each normalised and packed to bf16 on arrival; TMEM
+        // O is released before any global store is issued
+        uint32_t w[32];
         const uint32_t obase = taddr(tmem, wq * 32, kColO);
-        const uint32_t dbits = tmem_ld1(obase + kDv);
-        tmem_ld16(obase, o);
-        tmem_ld16(obase + 16, o + 16);
-        tmem_wait_ld();
-        // O[:, 64] = phi(q).z + rowsum(P): the full denominator before eps
-        const float den = __uint_as_float(dbits) + p.eps;
-        const float inv = p.normalize ? 1.f / den : 1.f;
-        const uint64_t inv2 = f2pack(inv, inv);
-        __nv_bfloat16 *orow = p.out + ((uint64_t)bh * p.n + t0 + row) * kDv;
-        auto store32 = [&](int col) {
+        {
+          uint32_t o[32];
+          const uint32_t dbits = tmem_ld1(obase + kDv);
+          tmem_ld16(obase, o);
+          tmem_ld16(obase + 16, o + 16);
+          tmem_wait_ld();
+          // O[:, 64] = phi(q).z + rowsum(P): the full denominator before eps
+          const float den = __uint_as_float(dbits) + p.eps;
+          const float inv = p.normalize ? 1.f / den : 1.f;
+          const uint64_t inv2 = f2pack(inv, inv);
 #pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4) {
-            uint32_t w[4];
+          for (int i = 0; i < 16; ++i)
+            w[i] = pack_bf16x2(fmul2(f2pack(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), inv2));
+          tmem_ld16(obase + 32, o);
+          tmem_ld16(obase + 48, o + 16);
+          tmem_wait_ld();
+          tc_fence_before();
+          named_barrier_sync(4, 128);
+          if (leader) mbar_arrive(&bars[kOFree]);  // O is in registers: TMEM O reusable
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int k = 8 * v4 + 2 * i;
-              w[i] = pack_bf16x2(fmul2(f2pack(__uint_as_float(o[k]), __uint_as_float(o[k + 1])), inv2));
-            }
-            if (row < valid) *(uint4 *)(orow + col + 8 * v4) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-        };
-        store32(0);
-        tmem_ld16(obase + 32, o);
-        tmem_ld16(obase + 48, o + 16);
-        tmem_wait_ld();
-        tc_fence_before();
-        named_barrier_sync(4, 128);
-        if (leader) mbar_arrive(&bars[kOFree]);  // O is in registers: TMEM O reusable
+          for (int i = 0; i < 16; ++i)
+            w[16 + i] =
+                pack_bf16x2(fmul2(f2pack(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), inv2));
+        }
         LA_TRACE_AT(4, c, 1);
-        store32(32);
+        // one 128-byte row per thread as four 32-byte stores: full sectors, so
+        // L2 never merges partial writes (measured 6% faster than 16-byte stores)
+        if (row < valid) {
+          uint4 *orow = (uint4 *)(p.out + ((uint64_t)bh * p.n + t0 + row) * kDv);
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8)
+            asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(orow + 2 * v8),
+                         "r"(w[8 * v8]), "r"(w[8 * v8 + 1]), "r"(w[8 * v8 + 2]), "r"(w[8 * v8 + 3]),
+                         "r"(w[8 * v8 + 4]), "r"(w[8 * v8 + 5]), "r"(w[8 * v8 + 6]), "r"(w[8 * v8 + 7])
+                         : "memory");
+        }
         LA_TRACE_AT(4, c, 2);
       }
     }
