@@ -22,17 +22,17 @@
 // registers and stored to TMEM, its phi(K) to shared memory, by the thread
 // that owns the token.
 //
-// Every M=128, K=16 tcgen05.mma costs about 100 cycles whatever its N up to
-// 160, so a tile is ~27 MMAs (~2,800 cycles) of tensor-pipe time.  The issue
-// issue cost of one MMA (~70 cycles) and of a tcgen05.commit (~140) is paid by
-// the issuing thread, so two threads issue: one the state updates UP(c), the
-// other QS(c), PV(c) and the scores of tile c+1.  The state snapshot and
-// phi(K) of tile c+1 are produced while QS(c) and PV(c) run, phi(Q) of tile
-// c+1 while PV(c) and UP(c+1) run, and P of tile c+1 while UP(c+1) and
-// QS(c+1) run.
+// A thread pays ~100 cycles to issue one M=128, K=16 tcgen05.mma (measured:
+// one thread issues no faster than one per ~100-150 cycles, longer than an
+// N <= 160 MMA runs), and ~90 per tcgen05.commit, so two threads issue: one
+// the state updates UP(c), the other QS(c), PV(c) and the scores of tile
+// c+1.  (Giving QS, PV and the scores a thread each, with P in its own TMEM
+// columns, was measured 9% slower.)  The state snapshot and phi(K) of tile
+// c+1 are produced while QS(c) and PV(c) run, phi(Q) of tile c+1 while PV(c)
+// and UP(c+1) run, and P of tile c+1 while UP(c+1) and QS(c+1) run.
 //
 // Warp roles (800 threads, one CTA per SM):
-//   warp 19     TMA producer: Q/K tiles (3-stage ring) and V tiles (2-stage ring)
+//   warp 19     TMA producer: Q/K tiles (2-stage ring) and V tiles (3-stage ring)
 //   warp 23     TMEM allocator + update MMA issuer (S^T += ...)
 //   warp 24     output MMA issuer (phi(Q) S, P [V 1], scores)
 //   warps 0-3   features: phi(K) -> smem (2 buffers), phi(Q) -> TMEM
@@ -99,13 +99,15 @@ constexpr uint32_t kSnapBytes = 3 * kSnapKBlock;
 constexpr int kMaxStages = 6;
 
 // Shared-memory layout (offsets from a 1024-byte aligned base).  The full
-// kernel: Q/K ring (3 stages), V ring (2), ones block, phi(K) x 2, snapshots
+// kernel: Q/K ring (2 stages), V ring (3), ones block, phi(K) x 2, snapshots
 // x 2.  The state-only kernel needs no Q, phi(Q) or snapshots and spends the
 // room on deeper K and V rings, since nothing else hides its load latency.
 template <bool kStateOnly>
 struct Layout {
-  static constexpr int kQKStages = kStateOnly ? 6 : 3;
-  static constexpr int kVStages = kStateOnly ? 6 : 2;
+  // (full kernel: V is released only after P V, late in the tile, so its
+  // ring is the deeper one: measured 3% faster than 3 Q/K and 2 V stages)
+  static constexpr int kQKStages = kStateOnly ? 6 : 2;
+  static constexpr int kVStages = kStateOnly ? 6 : 3;
   static constexpr uint32_t kOffQ = 0;
   static constexpr uint32_t kOffK = kOffQ + (kStateOnly ? 0 : kQKStages * kQBytes);
   static constexpr uint32_t kOffV = kOffK + kQKStages * kQBytes;
@@ -540,7 +542,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       const int s = c & 1;           // phi(K) buffer
       const int sq = c % kQKStages;  // Q/K stage
       mbar_wait(&bars[kQKFull + sq], (c / kQKStages) & 1, abort_flag);
-      if (!wg_ok(1, abort_flag)) break;
+      named_barrier_sync(1, 128);
       LA_TRACE_AT(1, c, 0);
       const int valid = (int)min64(kT, t_end - (t_begin + (int64_t)c * kT));
       const bool vrow = row < valid;
@@ -555,7 +557,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       }
       // phi(K) into buffer c&1 once the update of tile c-2 has read it
       if (c >= 2) mbar_wait(&bars[kUpDone0 + s], ((c >> 1) - 1) & 1, abort_flag);
-      if (!wg_ok(1, abort_flag)) break;
+      named_barrier_sync(1, 128);
       LA_TRACE_AT(1, c, 3);
       {
         FeatIn fk;
@@ -577,7 +579,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       if (!kStateOnly) {
         // phi(Q) -> TMEM once phi(Q) S of the previous tile has read it
         if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
-        if (!wg_ok(1, abort_flag)) break;
+        named_barrier_sync(1, 128);
         tc_fence_after();
         LA_TRACE_AT(1, c, 5);
         FeatIn fs;
@@ -614,7 +616,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         const int64_t t0 = t_begin + (int64_t)c * kT;
         const int valid = (int)min64(kT, t_end - t0);
         mbar_wait(&bars[kScReady], c & 1, abort_flag);
-        if (!wg_ok(2, abort_flag, 256)) break;
+        named_barrier_sync(2, 256);
         tc_fence_after();
         LA_TRACE_AT(2, c, 0);
         // P = tril(1 + s/4 + s^2/32) for raw scores s = q.k (d = 16).  Key group
@@ -718,7 +720,8 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     if (kStateOnly) {
       // the segment's state, once every update has completed
       mbar_wait(&bars[kDone], 0, abort_flag);
-      if (wg_ok(3, abort_flag, kStateThreads)) {
+      named_barrier_sync(3, kStateThreads);
+      {
         tc_fence_after();
         float *dst = p.seg_out + ((uint64_t)bh * p.segments + g) * kF * kSV;
         for (int grp = 0; grp < 5; ++grp) {
@@ -767,7 +770,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         if (c == n_chunks - 1) {
           // the state after the last tile: no tile reads its snapshot; the
           // last segment writes it out as the final state
-          if (!wg_ok(3, abort_flag, kStateThreads)) break;
+          named_barrier_sync(3, kStateThreads);
           tc_fence_after();
           if (write_final) {
 #pragma unroll 1
@@ -780,7 +783,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           }
           break;
         }
-        if (!wg_ok(3, abort_flag, kStateThreads)) break;
+        named_barrier_sync(3, kStateThreads);
         tc_fence_after();
         LA_TRACE_AT(3, c, 0);
         // S_{c+1} -> bf16 snapshot buffer (c+1)&1, last read by phi(Q) S of
@@ -819,14 +822,13 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   } else {
     // ------------------------------------------------------------ epilogue
     if (!kStateOnly) {
-      const int wq = warp & 3;
-      const int row = wq * 32 + lane;
+      const int wq = warp & 3;  // rows 32wq .. 32wq+31 of the tile, one per lane
       const bool leader = (warp == kWarpEpi && lane == 0);
       for (int c = 0; c < n_chunks; ++c) {
         const int64_t t0 = t_begin + (int64_t)c * kT;
         const int valid = (int)min64(kT, t_end - t0);
         mbar_wait(&bars[kOReady], c & 1, abort_flag);
-        if (!wg_ok(4, abort_flag)) break;
+        named_barrier_sync(4, 128);
         tc_fence_after();
         LA_TRACE_AT(4, c, 0);
         // O leaves TMEM in two round trips, (denominator, values 0..31) then
@@ -859,16 +861,39 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
                 pack_bf16x2(fmul2(f2pack(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), inv2));
         }
         LA_TRACE_AT(4, c, 1);
-        // one 128-byte row per thread as four 32-byte stores: full sectors, so
-        // L2 never merges partial writes (measured 6% faster than 16-byte stores)
-        if (row < valid) {
-          uint4 *orow = (uint4 *)(p.out + ((uint64_t)bh * p.n + t0 + row) * kDv);
+        // 4x4 transpose of 32-byte pieces inside each group of four lanes
+        // (two butterfly stages): afterwards lane 4g+i holds piece i of rows
+        // 4g..4g+3, and each store instruction writes eight whole rows
+        {
+          const int gi = lane & 3;
 #pragma unroll
-          for (int v8 = 0; v8 < 4; ++v8)
-            asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(orow + 2 * v8),
-                         "r"(w[8 * v8]), "r"(w[8 * v8 + 1]), "r"(w[8 * v8 + 2]), "r"(w[8 * v8 + 3]),
-                         "r"(w[8 * v8 + 4]), "r"(w[8 * v8 + 5]), "r"(w[8 * v8 + 6]), "r"(w[8 * v8 + 7])
-                         : "memory");
+          for (int m = 2; m >= 1; m >>= 1) {
+            const bool hi = (gi & m) != 0;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              // the two slots this lane exchanges: bit m of the slot differs from bit m of gi
+              const int s0 = m == 2 ? k : (k << 1);      // slot with bit m clear
+              const int s1 = s0 | m;                     // slot with bit m set
+#pragma unroll
+              for (int r = 0; r < 8; ++r) {
+                const uint32_t send = hi ? w[8 * s0 + r] : w[8 * s1 + r];
+                const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, m);
+                if (hi) w[8 * s0 + r] = recv;
+                else w[8 * s1 + r] = recv;
+              }
+            }
+          }
+          const int64_t row0 = t0 + wq * 32 + (lane & ~3);  // first row of this lane's group
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (wq * 32 + (lane & ~3) + j < valid) {
+              uint4 *dst = (uint4 *)(p.out + ((uint64_t)bh * p.n + row0 + j) * kDv) + 2 * gi;
+              asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst),
+                           "r"(w[8 * j]), "r"(w[8 * j + 1]), "r"(w[8 * j + 2]), "r"(w[8 * j + 3]),
+                           "r"(w[8 * j + 4]), "r"(w[8 * j + 5]), "r"(w[8 * j + 6]), "r"(w[8 * j + 7])
+                           : "memory");
+            }
+          }
         }
         LA_TRACE_AT(4, c, 2);
       }

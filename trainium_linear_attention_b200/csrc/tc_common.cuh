@@ -84,6 +84,7 @@ constexpr uint32_t kSuspendNs = 200000;  // one sleep; the abort flag and the cl
 // which case the CTA's abort flag is raised.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
+  if (*abort_flag) return false;
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait_sleep(bar, parity, kSuspendNs)) {
     if (*abort_flag) return false;
@@ -128,14 +129,6 @@ __device__ __forceinline__ void tc_fence_after() {
 __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
-// Warpgroup-uniform continuation check after a wait: every thread of the
-// group reaches the barrier, then all see the same abort flag, so no thread
-// is left waiting at a later barrier for peers that already gave up.
-__device__ __forceinline__ bool wg_ok(int id, volatile int *abort_flag, int nthreads = 128) {
-  named_barrier_sync(id, nthreads);
-  return *abort_flag == 0;
-}
-
 // ---------------------------------------------------------------------- TMA ---
 __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map, uint64_t *bar,
                                             int x, int y, int z) {
