@@ -2,7 +2,7 @@
 """Benchmark of the chunked BASED hot path, one JSON line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--mode heads|sp] [--workload c4|c2|c3|c5]
+                    [--mode heads|sp] [--seq-len N] [--segments G]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
 Default workload: chunked BASED, B=8, H=16, N=32768,
@@ -20,6 +20,8 @@ convention) / that time.  ``e2e`` repeats the measurement through the public
 API with pinned host inputs copied in and the output copied back every step.
 ``--impl reference`` times the CPU port of the reference's chunked algorithm
 (oracle/, numpy, all host threads) on a bounded sample of the same workload.
+The other configurations (C2, C3 sliding window, the C5 parallel/chunked
+crossover sweep) are measured by ``python -m trainium_linear_attention_b200.sweep``.
 """
 
 from __future__ import annotations
@@ -40,9 +42,6 @@ sys.path.insert(0, str(ROOT))
 WORKLOADS = {
     # name: (batch, heads, seq_len, d_qk, d_v, kind)
     "c4": (8, 16, 32768, 16, 64, "chunked"),
-    "c2": (4, 16, 2048, 16, 64, "chunked"),
-    "c3": (4, 16, 4096, 64, 64, "sliding"),
-    "c5": (None, 16, None, 16, 64, "crossover"),
 }
 METRIC = "BASED chunked attn tokens/s @N=32K,H=16 on 1/2/4/8 B200; % of roofline"
 L2_FLUSH_BYTES = 256 << 20
@@ -55,8 +54,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--mode", choices=["heads", "sp"], default="heads")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c4")
-    ap.add_argument("--seq-len", type=int, default=None, help="override N (c5 sweep point)")
+    ap.add_argument("--seq-len", type=int, default=None, help="override N (not a bench line)")
     ap.add_argument("--segments", type=int, default=0, help="0 = library's choice")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

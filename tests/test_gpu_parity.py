@@ -236,12 +236,30 @@ def test_sliding_config3():
     assert O.rel_l2(np64(y), want) <= TOL_BF16
 
 
-@pytest.mark.parametrize("t,w", [(1, 64), (65, 64), (200, 1), (300, 128), (129, 500), (1000, 65)])
+@pytest.mark.parametrize("t,w", [(1, 64), (65, 64), (200, 1), (300, 128), (129, 500), (1000, 65),
+                                 (513, 129), (700, 130), (333, 66), (4097, 64), (130, 2)])
 def test_sliding_edges_bf16(t, w):
     q, k, v = inputs((1, 2, t, 64), 64, seed=t + w, scale=1.0)
     y = T.nki_sliding_window_attn(*cuda(q, k, v), window_size=w)
     want = O.sliding_window_attn(np64(q), np64(k), np64(v), w)
     assert O.rel_l2(np64(y), want) <= TOL_BF16
+
+
+def test_sliding_tensor_core_matches_cuda_core_path():
+    """The tcgen05 kernel (aligned tensors) and the CUDA-core kernel
+    (unaligned copies of the same values) agree."""
+    q, k, v = cuda(*inputs((2, 3, 1500, 64), 64, seed=31, scale=1.0))
+
+    def shifted(x):
+        buf = torch.empty(x.numel() + 1, dtype=x.dtype, device=DEV)
+        y = buf[1:].view(x.shape)
+        y.copy_(x)
+        return y
+
+    for w in (64, 100):
+        y_tc = T.nki_sliding_window_attn(q, k, v, window_size=w)
+        y_simt = T.nki_sliding_window_attn(shifted(q), shifted(k), shifted(v), window_size=w)
+        assert O.rel_l2(np64(y_tc), np64(y_simt)) <= 1e-2
 
 
 # -------------------------------------------------------------- dispatch ---

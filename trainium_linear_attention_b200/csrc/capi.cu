@@ -111,8 +111,10 @@ bool use_tensor_cores(int dtype, int64_t dqk, int64_t dv) {
   return dtype == LA_DTYPE_BFLOAT16 && dqk == 16 && dv == 64;
 }
 
-// TMA needs 16-byte aligned tensors; other pointers take the SIMT kernels
+// TMA needs 16-byte aligned inputs and the tensor-core epilogues store the
+// output in 32-byte pieces; other pointers take the SIMT kernels
 bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+bool aligned32(const void *p) { return ((uintptr_t)p & 31u) == 0; }
 
 size_t state_floats(int64_t bh, int64_t dqk, int64_t dv) {
   return (size_t)bh * (size_t)feature_dim(dqk) * (size_t)(dv + 1);
@@ -219,7 +221,7 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
   if ((st = require_sm100(&info)) != LA_OK) return st;
   cudaStream_t s = (cudaStream_t)stream;
   const bool tc = use_tensor_cores(dtype, d_qk, d_v) && tc_chunked_enabled() && aligned16(q) &&
-                  aligned16(k) && aligned16(v) && aligned16(out);
+                  aligned16(k) && aligned16(v) && aligned32(out);
   if (!tc && !chunked_simt_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
   if (seq_len == 0) {
     // no tokens: the final state is the initial state (or zero)
@@ -312,7 +314,9 @@ int la_sliding_window_fwd(const void *q, const void *k, const void *v, void *out
   DeviceInfo info;
   if ((st = require_sm100(&info)) != LA_OK) return st;
   cudaStream_t s = (cudaStream_t)stream;
-  if (dtype == LA_DTYPE_BFLOAT16 && head_dim == 64 && tc_sliding_enabled())
+  if (dtype == LA_DTYPE_BFLOAT16 && head_dim == 64 && tc_sliding_enabled() &&
+      sliding_tc_supported(window) && aligned16(q) && aligned16(k) && aligned16(v) &&
+      aligned32(out))
     return launch_sliding_tc(q, k, v, out, batch * heads, seq_len, window, info, s);
   return launch_sliding_simt(q, k, v, out, batch * heads, seq_len, (int)head_dim, dtype, window,
                              s);

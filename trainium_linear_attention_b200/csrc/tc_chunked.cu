@@ -49,6 +49,7 @@
 
 #include "tc_common.cuh"
 #include "tc_kernels.cuh"
+#include "tma_host.cuh"
 
 namespace la {
 namespace {
@@ -920,38 +921,10 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
 }
 
 // ---------------------------------------------------------------- host side
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = (EncodeTiledFn)ptr;
-    cudaGetLastError();
-  });
-  return fn;
-}
-
 // 3-D map over (bh, n, d) bf16 with a (1, 128, d) box; rows past n read as zero.
 bool make_map(CUtensorMap *map, const void *base, int64_t bh, int64_t n, int d,
               CUtensorMapSwizzle swz) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn || ((uintptr_t)base & 15)) return false;
-  cuuint64_t gdim[3] = {(cuuint64_t)d, (cuuint64_t)n, (cuuint64_t)bh};
-  cuuint64_t gstride[2] = {(cuuint64_t)d * 2, (cuuint64_t)n * d * 2};
-  cuuint32_t box[3] = {(cuuint32_t)d, (cuuint32_t)kT, 1};
-  cuuint32_t estride[3] = {1, 1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), gdim, gstride,
-            box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return make_tmap_3d(map, base, bh, n, d, kT, swz);
 }
 
 template <bool kStateOnly>

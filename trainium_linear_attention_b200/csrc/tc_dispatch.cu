@@ -4,9 +4,7 @@
 namespace la {
 bool tc_chunked_enabled() { return true; }
 bool tc_parallel_enabled() { return false; }
-bool tc_sliding_enabled() { return false; }
+bool tc_sliding_enabled() { return true; }
 int launch_parallel_tc(const void *, const void *, const void *, void *, int64_t, int64_t, float,
                        const DeviceInfo &, cudaStream_t) { return LA_ERR_UNSUPPORTED; }
-int launch_sliding_tc(const void *, const void *, const void *, void *, int64_t, int64_t, int64_t,
-                      const DeviceInfo &, cudaStream_t) { return LA_ERR_UNSUPPORTED; }
 }  // namespace la

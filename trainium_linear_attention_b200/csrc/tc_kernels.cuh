@@ -35,6 +35,8 @@ int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *
                              bool normalize, int segments, int state_ratio, int64_t seg_len,
                              const DeviceInfo &info, cudaStream_t s);
 
+// Windows the tensor-core sliding kernel handles (W <= 129 at head_dim 64).
+bool sliding_tc_supported(int64_t window);
 int launch_sliding_tc(const void *q, const void *k, const void *v, void *out, int64_t bh,
                       int64_t n, int64_t window, const DeviceInfo &info, cudaStream_t s);
 

@@ -26,11 +26,16 @@ from .. import ops
 
 _native_available = None
 
-#: sequence length up to which ``solution`` uses the parallel kernel (bf16
-#: tensor-core path); longer sequences use the chunked kernel.
+#: sequence length up to which ``solution`` uses the parallel kernel for bf16
+#: inputs whose chunked form has no tensor-core kernel (both on CUDA cores);
+#: longer sequences use the chunked kernel.
 CROSSOVER_SEQ_LEN_BF16 = 1024
-#: the same for fp32 inputs (both SIMT kernels)
+#: the same for fp32 inputs (both kernels on CUDA cores)
 CROSSOVER_SEQ_LEN_FP32 = 2048
+#: bf16 with d_qk = 16, d_v = 64 (the tcgen05 chunked kernel): the chunked
+#: form is faster at every measured length (B*N = 262144, H = 16: 33x at
+#: N = 512, 600x at N = 8192), so it is used from the first token
+CROSSOVER_SEQ_LEN_BF16_TC = 0
 
 
 def _check_nki() -> bool:
@@ -76,7 +81,12 @@ def solution(q, k, v, eps=1e-6):
     """BASED causal attention on B200: parallel kernel for short sequences,
     chunked recurrent kernel for long ones.  Raises on any failure."""
     t = q.shape[-2]
-    limit = CROSSOVER_SEQ_LEN_FP32 if q.dtype == torch.float32 else CROSSOVER_SEQ_LEN_BF16
+    if q.dtype == torch.float32:
+        limit = CROSSOVER_SEQ_LEN_FP32
+    elif q.shape[-1] == 16 and v.shape[-1] == 64:
+        limit = CROSSOVER_SEQ_LEN_BF16_TC
+    else:
+        limit = CROSSOVER_SEQ_LEN_BF16
     if t <= limit:
         return ops.based_parallel(q, k, v, eps=eps)
     return ops.based_chunked(q, k, v, eps=eps)
