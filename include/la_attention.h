@@ -75,8 +75,9 @@ int64_t la_based_feature_dim(int64_t d_qk);
  * Replaces solution_nki (kernels/pytorch_attention.py:44-78) together with the
  * kernel it builds, get_based_attn_kernel / _kernel (kernels/nki_attention.py:
  * 25-115): one call computes the normalised output; no padding copies and no
- * host-side num/den division.  Computes in fp32 on CUDA cores for fp32 and
- * bf16 inputs.
+ * host-side num/den division.  bf16 inputs with d_qk = 16, d_v = 64 (and
+ * q/k/v 16-byte, out 32-byte aligned) use the tcgen05 tensor-core kernel;
+ * everything else computes in fp32 on CUDA cores.
  * ------------------------------------------------------------------------- */
 int la_based_parallel_fwd(const void *q, const void *k, const void *v, void *out,
                           int64_t batch, int64_t heads, int64_t seq_len,

@@ -61,6 +61,34 @@ def test_parallel_bf16(shape, dv):
     assert O.rel_l2(np64(y), want) <= TOL_BF16
 
 
+@pytest.mark.parametrize("t", [1, 127, 128, 129, 256, 700])
+def test_parallel_tensor_core_lengths(t):
+    """The tcgen05 parallel kernel (bf16, d_qk 16, d_v 64) on ragged and
+    tile-multiple lengths, against the oracle and against the chunked kernel."""
+    q, k, v = inputs((2, 3, t, 16), 64, seed=100 + t)
+    qc, kc, vc = cuda(q, k, v)
+    y = ops.based_parallel(qc, kc, vc)
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+    assert O.rel_l2(np64(y), np64(ops.based_chunked(qc, kc, vc))) <= 1e-2
+
+
+def test_parallel_tensor_core_matches_cuda_core_path():
+    """Aligned tensors take the tcgen05 kernel, unaligned copies of the same
+    values the CUDA-core kernel; both agree."""
+    q, k, v = cuda(*inputs((1, 4, 900, 16), 64, seed=41))
+
+    def shifted(x):
+        buf = torch.empty(x.numel() + 1, dtype=x.dtype, device=DEV)
+        y = buf[1:].view(x.shape)
+        y.copy_(x)
+        return y
+
+    y_tc = ops.based_parallel(q, k, v)
+    y_simt = ops.based_parallel(shifted(q), shifted(k), shifted(v))
+    assert O.rel_l2(np64(y_tc), np64(y_simt)) <= 1e-2
+
+
 # ----------------------------------------------------------------- chunked ---
 
 def test_chunked_fp32_golden(golden):

@@ -171,7 +171,8 @@ int la_based_parallel_fwd(const void *q, const void *k, const void *v, void *out
   DeviceInfo info;
   if ((st = require_sm100(&info)) != LA_OK) return st;
   cudaStream_t s = (cudaStream_t)stream;
-  if (use_tensor_cores(dtype, d_qk, d_v) && tc_parallel_enabled())
+  if (use_tensor_cores(dtype, d_qk, d_v) && tc_parallel_enabled() && aligned16(q) &&
+      aligned16(k) && aligned16(v) && aligned32(out))
     return launch_parallel_tc(q, k, v, out, batch * heads, seq_len, eps, info, s);
   return launch_parallel_simt(q, k, v, out, batch * heads, seq_len, (int)d_qk, (int)d_v, dtype,
                               eps, s);

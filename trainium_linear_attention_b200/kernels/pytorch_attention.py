@@ -32,10 +32,10 @@ _native_available = None
 CROSSOVER_SEQ_LEN_BF16 = 1024
 #: the same for fp32 inputs (both kernels on CUDA cores)
 CROSSOVER_SEQ_LEN_FP32 = 2048
-#: bf16 with d_qk = 16, d_v = 64 (the tcgen05 chunked kernel): the chunked
-#: form is faster at every measured length (B*N = 262144, H = 16: 33x at
-#: N = 512, 600x at N = 8192), so it is used from the first token
-CROSSOVER_SEQ_LEN_BF16_TC = 0
+#: bf16 with d_qk = 16, d_v = 64 (both forms on tcgen05 kernels): measured at
+#: B*N = 262144, H = 16 on B200, parallel 0.71 ms vs chunked 0.94 ms at
+#: N = 512, but 1.04 vs 0.68 ms at N = 1024 and 3.05 vs 0.49 at N = 4096
+CROSSOVER_SEQ_LEN_BF16_TC = 512
 
 
 def _check_nki() -> bool:
