@@ -359,7 +359,8 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t count = 1;
       if (i >= kQKEmpty && i < kQKEmpty + kMaxStages) count = kStateOnly ? 1 : 2;
-      if (i >= kVEmpty && i < kVEmpty + kMaxStages) count = kStateOnly ? 1 : 2;
+      if (i >= kVEmpty && i < kVEmpty + kMaxStages) count = 2;
+      if ((i == kUpDone0 || i == kUpDone1) && kStateOnly) count = 2;
       if (i == kDone) count = 2;
       mbar_init(&bars[i], count);
     }
@@ -444,7 +445,11 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     // a K-step of 16 tokens: start address +2048 B, LBO (distance to the ones block) -2048 B
     constexpr uint64_t kStep = (uint64_t)(2048 >> 4) - ((uint64_t)(2048 >> 4) << 16);
     const uint32_t a_ones = sb + kOffOnes;
-    if (lane == 0 && warp == kWarpUpd) {
+    // The state-only kernel has no other MMAs, so its updates are split over
+    // both issuing threads: tokens 0..63 of each tile into S^T, tokens
+    // 64..127 into a second accumulator (the full kernel's O columns) that
+    // starts at zero; the two are summed when the state is written out.
+    auto update_loop = [&](int j0, int j1, uint32_t dcol, bool second) {
       for (int c = 0; c < n_chunks; ++c) {
         const int b = c & 1;          // phi(K) buffer
         const int sv = c % kVStages;  // V stage
@@ -452,21 +457,28 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         LA_TRACE_AT(0, c, 7);
         if (!mbar_wait(&bars[kPhiKReady0 + b], (c >> 1) & 1, abort_flag)) break;
         // S^T may change once the state warps have read S_c out of it
-        if ((c == 0 || !kStateOnly) && !mbar_wait(&bars[kSRead], c & 1, abort_flag)) break;
+        if (!second && (c == 0 || !kStateOnly) && !mbar_wait(&bars[kSRead], c & 1, abort_flag))
+          break;
         tc_fence_after();
         LA_TRACE_AT(0, c, 0);
         const uint32_t v_base = sb + kOffV + sv * kVBytes;
         const uint64_t db0 = make_sdesc(sb + kOffPhiK + b * kPhiBytes, kPhiBlock, 1024, kSwizzle128B);
         const uint64_t da0 = make_sdesc(v_base, a_ones - v_base, 1024, kSwizzle128B);
 #pragma unroll
-        for (int j = 0; j < kT / 16; ++j)
-          umma_ss(tmem + kColS, da0 + kStep * j, db0 + (uint64_t)((j * 2048) >> 4), id_up, 1u);
+        for (int j = j0; j < j1; ++j)
+          umma_ss(tmem + dcol, da0 + kStep * j, db0 + (uint64_t)((j * 2048) >> 4), id_up,
+                  (second && c == 0 && j == j0) ? 0u : 1u);
         if (!kStateOnly) umma_commit(&bars[kSReady]);
         umma_commit(&bars[kUpDone0 + b]);
         umma_commit(&bars[kVEmpty + sv]);
-        *up_issued = c + 1;  // the state update of tile c is in the pipe
+        if (!second) *up_issued = c + 1;  // the state update of tile c is in the pipe
       }
       umma_commit(&bars[kDone]);
+    };
+    if (lane == 0 && warp == kWarpUpd) {
+      update_loop(0, kStateOnly ? kT / 32 : kT / 16, kColS, false);
+    } else if (lane == 0 && kStateOnly) {
+      update_loop(kT / 32, kT / 16, kColO, true);
     } else if (lane == 0) {
       if (!kStateOnly) {
         const uint64_t qs_b_desc0 = make_sdesc(sb + kOffSnap, 16, 1024, kSwizzle128B);
@@ -726,13 +738,15 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         tc_fence_after();
         float *dst = p.seg_out + ((uint64_t)bh * p.segments + g) * kF * kSV;
         for (int grp = 0; grp < 5; ++grp) {
-          uint32_t r[16];
+          uint32_t r[16], r2[16];
           tmem_ld16(taddr(tmem, wq * 32, kColS + col0 + 16 * grp), r);
+          tmem_ld16(taddr(tmem, wq * 32, kColO + col0 + 16 * grp), r2);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int f = c_slot_map.f[col0 + 16 * grp + i];
-            if (real && f >= 0) dst[(uint64_t)f * kSV + e] = __uint_as_float(r[i]);
+            if (real && f >= 0)
+              dst[(uint64_t)f * kSV + e] = __uint_as_float(r[i]) + __uint_as_float(r2[i]);
           }
         }
       }
