@@ -286,8 +286,8 @@ def run_ours(args):
 
     if args.mode == "heads":
         def step():
-            return ops.based_chunked(q, k, v, chunk_size=64, segments=g, workspace=workspace)
-        launches_per_step = 2 if g > 1 else 1
+            return ops.based_chunked(q, k, v, chunk_size=64, segments=seg, workspace=workspace)
+        launches_per_step = 2 if g > 1 else 1  # state pass (segments or lead/main split), output
     else:
         def step():
             return D.sequence_parallel_forward(q, k, v, chunk_size=64)

@@ -48,7 +48,7 @@ extern "C" {
 /* ---- flags for the chunked entry points ------------------------------------*/
 #define LA_CHUNKED_NORMALIZE        1u  /* divide by the normaliser (+eps)        */
 #define LA_CHUNKED_REUSE_SEGMENTS   2u  /* workspace already holds the segment
-                                           states written by la_based_chunked_state */
+                                           seeds written by la_based_chunked_state */
 
 /* Human-readable name of a status code (static storage, never NULL). */
 const char *la_status_string(int status);
@@ -106,6 +106,12 @@ int la_based_parallel_fwd(const void *q, const void *k, const void *v, void *out
  * segments processed by different CTAs (0 = let the library choose).  A
  * segmented run needs a workspace of la_based_chunked_workspace_size() bytes
  * (256-byte aligned); an unsegmented run needs none (workspace may be NULL).
+ * With segments = 0 the library may also split each head unequally, into a
+ * short lead and a long main piece, when between half and all of the SMs
+ * hold one head each (the leads run on the SMs the heads leave free); it
+ * needs one state per head of workspace.  la_based_chunked_plan with
+ * segments_requested = 0 reports the segment count the library picks (2 for
+ * that split) and a workspace that covers it and that many equal segments.
  * chunk_size: the reference's chunk length.  The result does not depend on it
  * beyond floating-point rounding (any positive value is accepted); the
  * kernels tile the sequence at their own fixed length.
@@ -147,9 +153,10 @@ int la_based_chunked_fwd_noalloc(const void *q, const void *k, const void *v, vo
 /* Total state sum_j phi_k(k_j) [v_j, 1]^T of every head over all seq_len
  * tokens, written to state_out (fp32, (batch*heads, F, d_v + 1)).  This is the
  * per-rank contribution exchanged by the sequence-parallel mode.  With a
- * workspace and segments > 1 the per-segment states are left in the workspace
- * so that a following la_based_chunked_fwd with LA_CHUNKED_REUSE_SEGMENTS
- * (same shapes and segments) skips its own state pass.  The reference has no
+ * workspace and segments > 1 the running sums of the per-segment states (the
+ * seed of each later segment) are left in the workspace so that a following
+ * la_based_chunked_fwd with LA_CHUNKED_REUSE_SEGMENTS (same shapes and
+ * segments) skips its own state pass.  The reference has no
  * counterpart (it has no multi-device mode). */
 int la_based_chunked_state(const void *k, const void *v, float *state_out,
                            int64_t batch, int64_t heads, int64_t seq_len,

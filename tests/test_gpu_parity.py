@@ -157,6 +157,30 @@ def test_chunked_segments_agree(segments):
     assert O.rel_l2(np64(yg), np64(y1)) <= 1e-2
 
 
+@pytest.mark.parametrize("t", [8000, 8192])
+def test_chunked_lead_main_split(t):
+    """96 heads on a 148-SM B200: segments=0 splits every head into a short
+    lead and a long main piece.  Output, final state (from an initial state)
+    and the oracle agree with the unsplit run."""
+    b, h = 6, 16
+    q, k, v = inputs((b, h, t, 16), 64, seed=t)
+    qd, kd, vd = cuda(q, k, v)
+    g, ws = ops.chunked_plan(b * h, t, 16, 64, torch.bfloat16)
+    if torch.cuda.get_device_properties(0).multi_processor_count == 148:
+        assert g == 2 and ws > 0  # the split is in use
+    F = ops.feature_dim(16)
+    s0 = torch.randn(b * h, F, 65, generator=torch.Generator().manual_seed(3)).abs().to(DEV)
+    y, st = ops.based_chunked(qd, kd, vd, init_state=s0, return_state=True)
+    y1, st1 = ops.based_chunked(qd, kd, vd, init_state=s0, return_state=True, segments=1)
+    assert O.rel_l2(np64(y), np64(y1)) <= 1e-2
+    assert O.rel_l2(st.double().cpu().numpy(), st1.double().cpu().numpy()) <= 1e-5
+    yn = ops.based_chunked(qd, kd, vd)
+    for bh in (0, b * h - 1):
+        bb, hh = divmod(bh, h)
+        want = O.based_chunked(np64(q[bb, hh]), np64(k[bb, hh]), np64(v[bb, hh]))
+        assert O.rel_l2(np64(yn[bb, hh]), want) <= TOL_BF16
+
+
 def test_chunked_state_roundtrip():
     """Seeding the second half with the first half's final state reproduces
     the whole sequence; the states match the oracle's."""

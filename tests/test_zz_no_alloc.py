@@ -76,3 +76,14 @@ def test_noalloc_rejects_requests_beyond_its_scratch():
                                               N.LA_DTYPE_BFLOAT16, 64, 1e-6, flags, None, None, 8,
                                               None)
     assert st == N.LA_ERR_INVALID_ARGUMENT
+
+
+def test_noalloc_lead_main_split():
+    """segments=0 at 96 heads: the library's lead/main split, one seed state
+    per head in the scratch."""
+    q, k, v = _inputs(6, 16, 4096, seed=22)
+    want = ops.based_chunked(q, k, v)
+    out = torch.empty_like(v)
+    assert _noalloc(q, k, v, out, 0) == N.LA_OK
+    torch.cuda.synchronize()
+    assert O.rel_l2(out.float().cpu().numpy(), want.float().cpu().numpy()) <= 1e-6

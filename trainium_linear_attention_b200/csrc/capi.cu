@@ -107,6 +107,33 @@ int auto_segments(int64_t bh, int64_t n, int sm_count) {
   return effective_segments(n, (int)g);
 }
 
+// Lead/main split of the tensor-core chunked forward, for SMs / 2 < bh < SMs
+// (where equal segments leave SMs - bh SMs idle): each head's main CTA covers
+// [lead, n) and is seeded by a state pass over [0, lead); the bh short lead
+// CTAs run in waves on the SMs - bh free SMs while the main CTAs run.  The lead
+// length balances the two: (tiles - a) = waves * (a + kLeadStartTiles), in
+// 128-token tiles, where kLeadStartTiles is a CTA's start-up and drain in tile
+// times.  The split pays when the tiles taken off the main CTAs outweigh the
+// state pass over the leads (~0.35 of a full tile each, plus its launch).
+// Measured on a B200 at N = 32768: 80 and 96 heads 12% faster (two waves of
+// leads), 112 heads 1% (four waves), 128 heads 4% slower (seven waves: the
+// main CTAs next to SMs that keep starting lead CTAs run slower), hence at
+// most kMaxLeadWaves waves.
+constexpr int64_t kLeadStartTiles = 2;
+constexpr int64_t kMinLeadTiles = 8;
+constexpr int64_t kMaxLeadWaves = 3;
+
+int64_t lead_tokens(int64_t bh, int64_t n, int sm_count) {
+  if (bh <= 0 || 2 * bh <= sm_count || bh >= sm_count) return 0;
+  const int64_t free_sms = sm_count - bh;
+  const int64_t waves = (bh + free_sms - 1) / free_sms;
+  if (waves > kMaxLeadWaves) return 0;
+  const int64_t tiles = n / kSegmentTile;
+  const int64_t a = (tiles - waves * kLeadStartTiles) / (waves + 1);
+  if (a < kMinLeadTiles) return 0;
+  return a * kSegmentTile;
+}
+
 bool use_tensor_cores(int dtype, int64_t dqk, int64_t dv) {
   return dtype == LA_DTYPE_BFLOAT16 && dqk == 16 && dv == 64;
 }
@@ -121,6 +148,20 @@ size_t state_floats(int64_t bh, int64_t dqk, int64_t dv) {
 }
 
 }  // namespace
+
+size_t chunked_fwd_scratch_bytes(int64_t bh, int64_t n, int64_t d_qk, int64_t d_v, int dtype,
+                                 int segments, unsigned flags) {
+  if (segments == 0 && !(flags & LA_CHUNKED_REUSE_SEGMENTS) &&
+      use_tensor_cores(dtype, d_qk, d_v) && tc_chunked_enabled()) {
+    DeviceInfo info;
+    if (require_sm100(&info) == LA_OK && lead_tokens(bh, n, info.sm_count) > 0)
+      return (state_floats(bh, d_qk, d_v) * sizeof(float) + 255) / 256 * 256;
+  }
+  int g = 0;
+  size_t need = 0;
+  if (la_based_chunked_plan(bh, n, d_qk, d_v, dtype, segments, &g, &need) != LA_OK) return 0;
+  return need;
+}
 }  // namespace la
 
 using namespace la;
@@ -189,7 +230,15 @@ int la_based_chunked_plan(int64_t batch_heads, int64_t seq_len, int64_t d_qk, in
     DeviceInfo info;
     int st = require_sm100(&info);
     if (st != LA_OK) return st;
-    g = auto_segments(batch_heads, seq_len, info.sm_count);
+    if (use_tensor_cores(dtype, d_qk, d_v) && tc_chunked_enabled() &&
+        lead_tokens(batch_heads, seq_len, info.sm_count) > 0) {
+      // the forward's lead/main split: two pieces per head.  The workspace
+      // also covers two equal segments, for callers that pass segments_out
+      // on explicitly (the split itself needs one state per head).
+      g = 2;
+    } else {
+      g = auto_segments(batch_heads, seq_len, info.sm_count);
+    }
   }
   g = effective_segments(seq_len, g);
   if (segments_out) *segments_out = g;
@@ -235,6 +284,20 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
     }
     return LA_OK;
   }
+  const int64_t lead = (segments == 0 && tc && !(flags & LA_CHUNKED_REUSE_SEGMENTS))
+                           ? lead_tokens(bh, seq_len, info.sm_count)
+                           : 0;
+  if (lead > 0) {
+    const size_t need = (state_floats(bh, d_qk, d_v) * sizeof(float) + 255) / 256 * 256;
+    if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u))
+      return LA_ERR_WORKSPACE;
+    float *lead_states = (float *)workspace;
+    st = launch_chunked_state_tc(k, v, lead_states, bh, seq_len, 1, 1, lead, info, s);
+    if (st != LA_OK) return st;
+    return launch_chunked_output_tc(q, k, v, out, init_state, final_state, lead_states, bh,
+                                    seq_len, eps, (flags & LA_CHUNKED_NORMALIZE) != 0, 1,
+                                    seq_len, lead, info, s);
+  }
   const int g = segments == 0 ? auto_segments(bh, seq_len, info.sm_count)
                               : effective_segments(seq_len, segments);
   const int64_t seg_len = g > 1 ? segment_len(seq_len, g) : seq_len;
@@ -255,16 +318,21 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
           ? 2
           : 1;
   if (g > 1 && !(flags & LA_CHUNKED_REUSE_SEGMENTS)) {
-    // states of segments 0 .. g-2 seed the later segments
+    // states of segments 0 .. g-2 (ratio slots each), then their prefix sums:
+    // slot g - 1 seeds segment g
     st = tc ? launch_chunked_state_tc(k, v, seg_states, bh, seq_len, g, (g - 1) * ratio,
                                       seg_len / ratio, info, s)
             : launch_chunked_state_simt(k, v, seg_states, bh, seq_len, (int)d_qk, (int)d_v,
                                         dtype, g, seg_len, s);
     if (st != LA_OK) return st;
+    if ((g - 1) * ratio > 1 &&
+        (st = launch_prefix_segments(seg_states, nullptr, bh, g, g - 1, ratio,
+                                     (int64_t)feature_dim(d_qk) * (d_v + 1), s)) != LA_OK)
+      return st;
   }
   if (tc)
     return launch_chunked_output_tc(q, k, v, out, init_state, final_state, seg_states, bh,
-                                    seq_len, eps, normalize, g, ratio, seg_len, info, s);
+                                    seq_len, eps, normalize, g, seg_len, 0, info, s);
   return launch_chunked_output_simt(q, k, v, out, init_state, final_state, seg_states, bh,
                                     seq_len, (int)d_qk, (int)d_v, dtype, eps, normalize, g,
                                     seg_len, s);
@@ -302,7 +370,10 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
           : launch_chunked_state_simt(k, v, dst, bh, seq_len, (int)d_qk, (int)d_v, dtype, g,
                                       seg_len, s);
   if (st != LA_OK || g == 1) return st;
-  return launch_sum_segments(dst, state_out, bh, g, (int64_t)feature_dim(d_qk) * (d_v + 1), s);
+  // the total, and in the workspace the prefix slots a forward with
+  // LA_CHUNKED_REUSE_SEGMENTS seeds its segments from
+  return launch_prefix_segments(dst, state_out, bh, g, g, 1,
+                                (int64_t)feature_dim(d_qk) * (d_v + 1), s);
 }
 
 int la_sliding_window_fwd(const void *q, const void *k, const void *v, void *out, int64_t batch,

@@ -71,14 +71,15 @@ extern "C" int la_based_chunked_fwd_noalloc(const void *q, const void *k, const 
   if (batch < 0 || heads < 0 || seq_len < 0 || d_qk < 1 || d_v < 1 || segments < 0)
     return LA_ERR_INVALID_ARGUMENT;
   int g = segments;
-  size_t need = 0;
   const int st = la_based_chunked_plan(batch * heads, seq_len, d_qk, d_v, dtype, segments, &g,
-                                       &need);
+                                       nullptr);
   if (st != LA_OK) return st;
+  const size_t need =
+      la::chunked_fwd_scratch_bytes(batch * heads, seq_len, d_qk, d_v, dtype, segments, flags);
   if (need > la::kNoAllocScratchBytes) return LA_ERR_WORKSPACE;
   void *scratch = la::noalloc_scratch_ptr();
   if (!scratch) return LA_ERR_CUDA;
   return la_based_chunked_fwd(q, k, v, out, batch, heads, seq_len, d_qk, d_v, dtype, chunk_size,
                               eps, flags, init_state, final_state, scratch,
-                              la::kNoAllocScratchBytes, g, stream);
+                              la::kNoAllocScratchBytes, segments, stream);
 }

@@ -75,4 +75,9 @@ int launch_chunked_output_simt(const void *q, const void *k, const void *v, void
 // Largest (d_qk, d_v) the SIMT chunked kernels hold on chip.
 bool chunked_simt_supported(int64_t dqk, int64_t dv);
 
+// Workspace bytes la_based_chunked_fwd needs for these arguments (the exact
+// need; la_based_chunked_plan may report more).
+size_t chunked_fwd_scratch_bytes(int64_t bh, int64_t n, int64_t d_qk, int64_t d_v, int dtype,
+                                 int segments, unsigned flags);
+
 }  // namespace la

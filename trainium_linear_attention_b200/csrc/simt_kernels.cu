@@ -304,10 +304,11 @@ chunked_output_simt_kernel(const T *__restrict__ q, const T *__restrict__ k,
   const T *kh = k + bh * n * dqk;
   const T *vh = v + bh * n * dv;
 
-  // prefix state: init + sum of earlier segments, summed in segment order
+  // prefix state: init + the sum of the earlier segments' states (slot g - 1
+  // of seg_states after launch_prefix_segments)
   for (int i = threadIdx.x; i < F * ldv; i += blockDim.x) {
     float s = init_state ? init_state[bh * (int64_t)F * ldv + i] : 0.f;
-    for (int gg = 0; gg < g; ++gg) s += seg_states[(bh * segments + gg) * (int64_t)F * ldv + i];
+    if (g > 0) s += seg_states[(bh * segments + g - 1) * (int64_t)F * ldv + i];
     c.S[i] = s;
   }
 
@@ -499,22 +500,27 @@ int launch_chunked_output_simt(const void *q, const void *k, const void *v, void
 
 namespace la {
 namespace {
-__global__ void sum_segments_kernel(const float *__restrict__ seg, float *__restrict__ out,
-                                    int segments, int64_t per_head) {
+__global__ void prefix_segments_kernel(float *__restrict__ seg, float *__restrict__ total,
+                                       int stride, int groups, int ratio, int64_t per_head) {
   const int64_t bh = blockIdx.y;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per_head;
        i += (int64_t)gridDim.x * blockDim.x) {
-    float acc = 0.f;
-    for (int g = 0; g < segments; ++g) acc += seg[(bh * segments + g) * per_head + i];
-    out[bh * per_head + i] = acc;
+    float *base = seg + bh * stride * per_head + i;
+    float run = 0.f;
+    for (int gr = 0; gr < groups; ++gr) {
+      // read this group's slots [gr*ratio, (gr+1)*ratio) before writing slot gr <= gr*ratio
+      for (int r = 0; r < ratio; ++r) run += base[(int64_t)(gr * ratio + r) * per_head];
+      base[(int64_t)gr * per_head] = run;
+    }
+    if (total) total[bh * per_head + i] = run;
   }
 }
 }  // namespace
 
-int launch_sum_segments(const float *seg, float *out, int64_t bh, int segments, int64_t per_head,
-                        cudaStream_t s) {
+int launch_prefix_segments(float *seg, float *total, int64_t bh, int stride, int groups,
+                           int ratio, int64_t per_head, cudaStream_t s) {
   dim3 grid((unsigned)((per_head + 255) / 256), (unsigned)bh);
-  sum_segments_kernel<<<grid, 256, 0, s>>>(seg, out, segments, per_head);
+  prefix_segments_kernel<<<grid, 256, 0, s>>>(seg, total, stride, groups, ratio, per_head);
   return check_launch();
 }
 }  // namespace la

@@ -305,8 +305,8 @@ struct Params {
   int *err;                 // device error word
   int64_t n;
   int64_t seg_len;
+  int64_t lead_len;         // > 0: lead/main split (output pass: grid (bh, 2))
   int segments;             // segment count (the per-head stride of seg_states)
-  int state_ratio;          // state entries per earlier segment in seg_states
   float eps;
   int normalize;
 };
@@ -336,10 +336,15 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int g = blockIdx.x;
-  const int64_t bh = blockIdx.y;
-  const int64_t t_begin = (int64_t)g * p.seg_len;
-  const int64_t t_end = min64(p.n, t_begin + p.seg_len);
+  // Equal segments: grid (segments, bh), segment g covers [g seg_len, (g+1) seg_len).
+  // Lead/main split: grid (bh, 2); y = 0 is the main piece [lead_len, n) (g = 1,
+  // dispatched first), y = 1 the lead piece [0, lead_len) (g = 0).
+  const bool split = p.lead_len > 0;
+  const int g = split ? (blockIdx.y == 0 ? 1 : 0) : (int)blockIdx.x;
+  const int64_t bh = split ? blockIdx.x : blockIdx.y;
+  const int64_t t_begin = split ? (g ? p.lead_len : 0) : (int64_t)g * p.seg_len;
+  const int64_t t_end = split ? (g ? p.n : p.lead_len) : min64(p.n, t_begin + p.seg_len);
+  const int last_g = split ? 1 : p.segments - 1;
   const int n_chunks = (int)((t_end - t_begin + kT - 1) / kT);
 
 #ifdef LA_TRACE
@@ -689,20 +694,27 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     // S_0 = init_state + states of the earlier segments (fixed order).  Rows
     // 65..79 of both snapshot buffers are zero for good (S^T rows >= 65 never
     // change: their rows of [V 1 0]^T are zero).
+    // The seed is init_state + the prefix slot g - 1; the 32 loads of a
+    // group of 16 columns are independent and issued together.
+    const float *seed_a =
+        (!kStateOnly && real && p.init_state) ? p.init_state + (uint64_t)bh * kF * kSV + e
+                                              : nullptr;
+    const float *seed_b =
+        (!kStateOnly && real && g > 0)
+            ? p.seg_states + ((uint64_t)bh * p.segments + (g - 1)) * kF * kSV + e
+            : nullptr;
     for (int grp = 0; grp < 5; ++grp) {
       const int f0 = col0 + 16 * grp;
       uint32_t w[16];
+      float xa[16], xb[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int f = c_slot_map.f[f0 + i];
-        float x = 0.f;
-        if (!kStateOnly && real && f >= 0) {
-          if (p.init_state) x = p.init_state[((uint64_t)bh * kF + f) * kSV + e];
-          for (int gg = 0; gg < g * p.state_ratio; ++gg)
-            x += p.seg_states[(((uint64_t)bh * p.segments + gg) * kF + f) * kSV + e];
-        }
-        w[i] = __float_as_uint(x);
+        xa[i] = (seed_a && f >= 0) ? __ldg(seed_a + f * kSV) : 0.f;
+        xb[i] = (seed_b && f >= 0) ? __ldg(seed_b + f * kSV) : 0.f;
       }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(xa[i] + xb[i]);
       tmem_st16(taddr(tmem, wq * 32, kColS + f0), w);
       if (!kStateOnly && e < kNO) {
 #pragma unroll
@@ -751,7 +763,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         }
       }
     } else {
-      const bool write_final = p.final_state != nullptr && g == p.segments - 1;
+      const bool write_final = p.final_state != nullptr && g == last_g;
       // snapshot a group of 16 columns of row e (rows <= 64 carry data)
       auto put = [&](uint32_t snap, int f0, const uint32_t *r) {
         if (e <= kDv) {
@@ -958,7 +970,8 @@ int launch(const void *q, const void *k, const void *v, const Params &p, int64_t
   cudaError_t e = cudaFuncSetAttribute(chunked_tc_kernel<kStateOnly>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
   if (e != cudaSuccess) return LA_ERR_CUDA;
-  dim3 grid((unsigned)n_launch, (unsigned)bh);
+  const dim3 grid = (!kStateOnly && p.lead_len > 0) ? dim3((unsigned)bh, 2u)
+                                                   : dim3((unsigned)n_launch, (unsigned)bh);
   chunked_tc_kernel<kStateOnly><<<grid, kThreads, kSmemAlloc, s>>>(mq, mk, mv, p);
   return check_launch();
 }
@@ -988,7 +1001,6 @@ int launch_chunked_state_tc(const void *k, const void *v, float *seg_states, int
   p.n = n;
   p.seg_len = seg_len;
   p.segments = segments;
-  p.state_ratio = 1;
   if (!p.err) return LA_ERR_CUDA;
   return launch<true>(nullptr, k, v, p, bh, n_launch, s);
 }
@@ -996,7 +1008,7 @@ int launch_chunked_state_tc(const void *k, const void *v, float *seg_states, int
 int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *out,
                              const float *init_state, float *final_state,
                              const float *seg_states, int64_t bh, int64_t n, float eps,
-                             bool normalize, int segments, int state_ratio, int64_t seg_len,
+                             bool normalize, int segments, int64_t seg_len, int64_t lead_len,
                              const DeviceInfo &info, cudaStream_t s) {
   (void)info;
   Params p{};
@@ -1007,8 +1019,8 @@ int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *
   p.err = device_error_word();
   p.n = n;
   p.seg_len = seg_len;
+  p.lead_len = lead_len;
   p.segments = segments;
-  p.state_ratio = state_ratio;
   p.eps = eps;
   p.normalize = normalize ? 1 : 0;
   if (!p.err) return LA_ERR_CUDA;

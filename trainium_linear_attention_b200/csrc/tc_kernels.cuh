@@ -27,12 +27,16 @@ int launch_chunked_state_tc(const void *k, const void *v, float *seg_states, int
                             int64_t n, int segments, int n_launch, int64_t seg_len,
                             const DeviceInfo &info, cudaStream_t s);
 
-// Output of `segments` segments of length seg_len; segment g is seeded with
-// init_state + seg_states[bh][0 .. g * state_ratio).
+// Output of `segments` segments of length seg_len; segment g > 0 is seeded
+// with init_state + seg_states[bh][g - 1] (the prefix slots written by
+// launch_prefix_segments; per-head stride `segments`).  lead_len > 0 selects
+// the lead/main split instead: per head a main CTA over [lead_len, n) seeded
+// with init_state + seg_states[bh] (segments = 1) and a lead CTA over
+// [0, lead_len); all main CTAs are dispatched before the leads.
 int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *out,
                              const float *init_state, float *final_state,
                              const float *seg_states, int64_t bh, int64_t n, float eps,
-                             bool normalize, int segments, int state_ratio, int64_t seg_len,
+                             bool normalize, int segments, int64_t seg_len, int64_t lead_len,
                              const DeviceInfo &info, cudaStream_t s);
 
 // Windows the tensor-core sliding kernel handles (W <= 129 at head_dim 64).
@@ -40,8 +44,12 @@ bool sliding_tc_supported(int64_t window);
 int launch_sliding_tc(const void *q, const void *k, const void *v, void *out, int64_t bh,
                       int64_t n, int64_t window, const DeviceInfo &info, cudaStream_t s);
 
-// out[bh][i] = sum_g seg[bh][g][i]  (fixed order, deterministic)
-int launch_sum_segments(const float *seg, float *out, int64_t bh, int segments, int64_t per_head,
-                        cudaStream_t s);
+// In place, per head (seg[bh][0 .. stride) holding states): slot gr becomes
+// the sum of slots [0, (gr + 1) * ratio) for gr < groups, i.e. the seed of
+// segment gr + 1 when each segment's state occupies `ratio` slots; total (if
+// not null) receives the sum of all groups * ratio slots.  Fixed order,
+// deterministic.
+int launch_prefix_segments(float *seg, float *total, int64_t bh, int stride, int groups,
+                           int ratio, int64_t per_head, cudaStream_t s);
 
 }  // namespace la

@@ -114,7 +114,7 @@ def based_chunked(q, k, v, chunk_size: int = 64, eps: float = 1e-6, normalize: b
     out = torch.empty((b, h, t, dv), dtype=q.dtype, device=q.device)
     final = torch.empty((b * h, F, dv + 1), dtype=torch.float32, device=q.device) if return_state else None
     with torch.cuda.device(q.device):
-        g, ws_bytes = chunked_plan(b * h, t, d, dv, q.dtype, segments)
+        _, ws_bytes = chunked_plan(b * h, t, d, dv, q.dtype, segments)
         if workspace is None:
             workspace = _workspace(ws_bytes, q.device)
         elif workspace.numel() * workspace.element_size() < ws_bytes:
@@ -124,8 +124,8 @@ def based_chunked(q, k, v, chunk_size: int = 64, eps: float = 1e-6, normalize: b
         st = N.lib().la_based_chunked_fwd(
             _ptr(q), _ptr(k), _ptr(v), _ptr(out), b, h, t, d, dv, code, int(chunk_size),
             float(eps), flags, _ptr(init_state), _ptr(final), _ptr(workspace),
-            0 if workspace is None else workspace.numel() * workspace.element_size(), g,
-            _stream_ptr(q.device))
+            0 if workspace is None else workspace.numel() * workspace.element_size(),
+            int(segments), _stream_ptr(q.device))
     N.check(st, "la_based_chunked_fwd")
     if return_state:
         return out, final
@@ -140,13 +140,13 @@ def based_chunked_state(k, v, segments: int = 0, workspace: torch.Tensor | None 
     dv = v.shape[-1]
     state = torch.empty((b * h, feature_dim(d), dv + 1), dtype=torch.float32, device=k.device)
     with torch.cuda.device(k.device):
-        g, ws_bytes = chunked_plan(b * h, t, d, dv, k.dtype, segments)
+        _, ws_bytes = chunked_plan(b * h, t, d, dv, k.dtype, segments)
         if workspace is None:
             workspace = _workspace(ws_bytes, k.device)
         st = N.lib().la_based_chunked_state(
             _ptr(k), _ptr(v), _ptr(state), b, h, t, d, dv, code, _ptr(workspace),
-            0 if workspace is None else workspace.numel() * workspace.element_size(), g,
-            _stream_ptr(k.device))
+            0 if workspace is None else workspace.numel() * workspace.element_size(),
+            int(segments), _stream_ptr(k.device))
     N.check(st, "la_based_chunked_state")
     return state
 
