@@ -116,7 +116,8 @@ struct Layout {
   static constexpr uint32_t kOffPhiK = kOffOnes + 2048;
   static constexpr uint32_t kOffSnap = kOffPhiK + 2 * kPhiBytes;
   static constexpr uint32_t kOffBar = kOffSnap + (kStateOnly ? 0 : 2 * kSnapBytes);
-  static constexpr uint32_t kSmemAlloc = kOffBar + 512 + 1024;  // barriers, alignment slack
+  static constexpr uint32_t kOffSlot = kOffBar + 512;            // slot map (kFPad shorts)
+  static constexpr uint32_t kSmemAlloc = kOffSlot + 512 + 1024;  // + alignment slack
   static_assert(kQKStages <= kMaxStages && kVStages <= kMaxStages, "barrier slots");
   static_assert(kOffV % 1024 == 0 && kOffOnes % 1024 == 0 && kOffPhiK % 1024 == 0 &&
                     kPhiBytes % 1024 == 0 && kOffSnap % 1024 == 0 && kSnapKBlock % 1024 == 0,
@@ -205,9 +206,10 @@ __host__ __device__ constexpr int slot_feature(int s) {
     default: return -1;
   }
 }
-struct SlotMap {
+struct alignas(16) SlotMap {
   short f[kFPad];
 };
+static_assert(sizeof(SlotMap) <= 512 && kFPad % 2 == 0, "slot map area");
 __host__ __device__ constexpr SlotMap make_slot_map() {
   SlotMap m{};
   for (int s = 0; s < kFPad; ++s) m.f[s] = (short)slot_feature(s);
@@ -226,7 +228,10 @@ __host__ __device__ constexpr bool slot_map_is_bijection() {
          pair_desc(77).type == kPairPad;
 }
 static_assert(slot_map_is_bijection(), "every feature has exactly one slot");
-__constant__ SlotMap c_slot_map = make_slot_map();
+// In global memory: each CTA copies it to shared memory at start (a uniform
+// read of constant memory per slot costs a constant-cache miss per line and
+// serialises; the copy is one coalesced load).
+__device__ const SlotMap g_slot_map = make_slot_map();
 
 // A token's inputs as bf16x2 words (x_2i lo, x_2i+1 hi): raw, and (query side)
 // divided by 16 and by 32.  `one` is {1, 0}, or 0 for a padding key.
@@ -325,7 +330,8 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   using L = Layout<kStateOnly>;
   constexpr int kQKStages = L::kQKStages, kVStages = L::kVStages;
   constexpr uint32_t kOffQ = L::kOffQ, kOffK = L::kOffK, kOffV = L::kOffV, kOffOnes = L::kOffOnes,
-                     kOffPhiK = L::kOffPhiK, kOffSnap = L::kOffSnap, kOffBar = L::kOffBar;
+                     kOffPhiK = L::kOffPhiK, kOffSnap = L::kOffSnap, kOffBar = L::kOffBar,
+                     kOffSlot = L::kOffSlot;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t sb = smem_u32(smem);
@@ -333,6 +339,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   uint32_t *tmem_slot = (uint32_t *)(smem + kOffBar + 8 * kNumBars);
   volatile int *abort_flag = (volatile int *)(smem + kOffBar + 8 * kNumBars + 4);
   volatile int *up_issued = (volatile int *)(smem + kOffBar + 8 * kNumBars + 8);
+  const short *slot_map = (const short *)(smem + kOffSlot);  // slot -> feature (or -1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -373,6 +380,8 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     *up_issued = 0;
     fence_barrier_init();
   }
+  if (threadIdx.x < kFPad / 2)
+    ((uint32_t *)(smem + kOffSlot))[threadIdx.x] = ((const uint32_t *)g_slot_map.f)[threadIdx.x];
   // constant "ones" block: A-operand rows 64..127 of [V 1 0]^T for 16 tokens;
   // row 64 (element 0 of each token row, 128B-swizzled) is 1, the rest 0.
   for (int i = threadIdx.x; i < 2048 / 4; i += kThreads) {
@@ -392,6 +401,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     // One thread feeds both rings, each released by its own consumers: it
     // issues whichever next copy has a free stage, so K can run ahead of V.
     if (lane == 0) {
+      LA_TRACE_AT(5, 0, 2);
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_v);
       if (!kStateOnly) prefetch_tmap(&tm_q);
@@ -696,25 +706,43 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     // change: their rows of [V 1 0]^T are zero).
     // The seed is init_state + the prefix slot g - 1; the 32 loads of a
     // group of 16 columns are independent and issued together.
-    const float *seed_a =
-        (!kStateOnly && real && p.init_state) ? p.init_state + (uint64_t)bh * kF * kSV + e
-                                              : nullptr;
-    const float *seed_b =
-        (!kStateOnly && real && g > 0)
-            ? p.seg_states + ((uint64_t)bh * p.segments + (g - 1)) * kF * kSV + e
-            : nullptr;
+    LA_TRACE_AT(3, 0, 3);
+    const float *head_a = !kStateOnly && p.init_state ? p.init_state + (uint64_t)bh * kF * kSV
+                                                      : nullptr;
+    const float *head_b =
+        !kStateOnly && g > 0 ? p.seg_states + ((uint64_t)bh * p.segments + (g - 1)) * kF * kSV
+                             : nullptr;
+    if (leader) {  // the seeds, into L2 while the first group's loads are in flight
+      if (head_a) prefetch_l2(head_a, sizeof(float) * kF * kSV);
+      if (head_b) prefetch_l2(head_b, sizeof(float) * kF * kSV);
+    }
+    // Loads are unconditional (padding slots read feature 0 and are zeroed
+    // after), so that all 32 of a group are in flight together.
+    const bool seeded = real && (head_a || head_b);
+    const float *seed_a = seeded ? (head_a ? head_a : head_b) + e : nullptr;
+    const float *seed_b = seeded ? (head_b ? head_b : head_a) + e : nullptr;
     for (int grp = 0; grp < 5; ++grp) {
       const int f0 = col0 + 16 * grp;
       uint32_t w[16];
-      float xa[16], xb[16];
+      if (seeded) {
+        float xa[16], xb[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int f = c_slot_map.f[f0 + i];
-        xa[i] = (seed_a && f >= 0) ? __ldg(seed_a + f * kSV) : 0.f;
-        xb[i] = (seed_b && f >= 0) ? __ldg(seed_b + f * kSV) : 0.f;
+        for (int i = 0; i < 16; ++i) {
+          const int f = slot_map[f0 + i];
+          const int fi = f >= 0 ? f : 0;
+          xa[i] = __ldg(seed_a + fi * kSV);
+          xb[i] = __ldg(seed_b + fi * kSV);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int f = slot_map[f0 + i];
+          const float x = (head_a ? xa[i] : 0.f) + (head_b ? xb[i] : 0.f);
+          w[i] = __float_as_uint(f >= 0 ? x : 0.f);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = 0u;
       }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(xa[i] + xb[i]);
       tmem_st16(taddr(tmem, wq * 32, kColS + f0), w);
       if (!kStateOnly && e < kNO) {
 #pragma unroll
@@ -733,10 +761,12 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         }
       }
     }
+    LA_TRACE_AT(3, 0, 4);
     tmem_wait_st();
     fence_proxy_async_smem();
     tc_fence_before();
     named_barrier_sync(3, kStateThreads);
+    LA_TRACE_AT(3, 0, 5);
     if (leader) {
       mbar_arrive(&bars[kSRead]);  // S_0 is in TMEM
       mbar_arrive(&bars[kSnapReady0]);
@@ -756,7 +786,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int f = c_slot_map.f[col0 + 16 * grp + i];
+            const int f = slot_map[col0 + 16 * grp + i];
             if (real && f >= 0)
               dst[(uint64_t)f * kSV + e] = __uint_as_float(r[i]) + __uint_as_float(r2[i]);
           }
@@ -785,7 +815,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         float *dst = p.final_state + (uint64_t)bh * kF * kSV;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int f = c_slot_map.f[f0 + i];
+          const int f = slot_map[f0 + i];
           if (real && f >= 0) dst[(uint64_t)f * kSV + e] = __uint_as_float(r[i]);
         }
       };

@@ -143,6 +143,16 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
+// Bring the 16-byte-aligned part of [p, p + bytes) into L2 (a hint: nothing
+// is read into the SM; the edges that are not 16-byte aligned are skipped).
+__device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes) {
+  const uintptr_t lo = ((uintptr_t)p + 15) & ~(uintptr_t)15;
+  const uintptr_t hi = ((uintptr_t)p + bytes) & ~(uintptr_t)15;
+  if (hi > lo)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"((uint32_t)(hi - lo))
+                 : "memory");
+}
+
 // --------------------------------------------------------------------- TMEM ---
 // Executed by one whole warp.
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
