@@ -502,15 +502,31 @@ namespace la {
 namespace {
 __global__ void prefix_segments_kernel(float *__restrict__ seg, float *__restrict__ total,
                                        int stride, int groups, int ratio, int64_t per_head) {
+  constexpr int kMaxSlots = 16;
   const int64_t bh = blockIdx.y;
+  const int slots = groups * ratio;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per_head;
        i += (int64_t)gridDim.x * blockDim.x) {
     float *base = seg + bh * stride * per_head + i;
     float run = 0.f;
-    for (int gr = 0; gr < groups; ++gr) {
-      // read this group's slots [gr*ratio, (gr+1)*ratio) before writing slot gr <= gr*ratio
-      for (int r = 0; r < ratio; ++r) run += base[(int64_t)(gr * ratio + r) * per_head];
-      base[(int64_t)gr * per_head] = run;
+    if (slots <= kMaxSlots) {
+      // every slot is read before any is written: the loads are all in flight
+      float x[kMaxSlots];
+#pragma unroll
+      for (int j = 0; j < kMaxSlots; ++j) x[j] = j < slots ? base[(int64_t)j * per_head] : 0.f;
+#pragma unroll
+      for (int j = 0; j < kMaxSlots; ++j) {
+        if (j < slots) {
+          run += x[j];
+          if (j % ratio == ratio - 1) base[(int64_t)(j / ratio) * per_head] = run;
+        }
+      }
+    } else {
+      for (int gr = 0; gr < groups; ++gr) {
+        // read this group's slots [gr*ratio, (gr+1)*ratio) before writing slot gr <= gr*ratio
+        for (int r = 0; r < ratio; ++r) run += base[(int64_t)(gr * ratio + r) * per_head];
+        base[(int64_t)gr * per_head] = run;
+      }
     }
     if (total) total[bh * per_head + i] = run;
   }
