@@ -881,9 +881,14 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     if (!kStateOnly) {
       const int wq = warp & 3;  // rows 32wq .. 32wq+31 of the tile, one per lane
       const bool leader = (warp == kWarpEpi && lane == 0);
-      for (int c = 0; c < n_chunks; ++c) {
-        const int64_t t0 = t_begin + (int64_t)c * kT;
-        const int valid = (int)min64(kT, t_end - t0);
+      // this lane's store target after the transpose: piece (lane & 3) of row
+      // (lane & ~3) of its quarter, advanced one tile per iteration; rows_left
+      // counts the rows of the segment from that row on
+      const int gi = lane & 3;
+      uint4 *dst_row = (uint4 *)(p.out + ((uint64_t)bh * p.n + t_begin + wq * 32 + (lane & ~3)) * kDv) +
+                       2 * gi;
+      int64_t rows_left = t_end - (t_begin + wq * 32 + (lane & ~3));
+      for (int c = 0; c < n_chunks; ++c, dst_row += kT * kDv / 8, rows_left -= kT) {
         mbar_wait(&bars[kOReady], c & 1, abort_flag);
         named_barrier_sync(4, 128);
         tc_fence_after();
@@ -922,7 +927,6 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         // (two butterfly stages): afterwards lane 4g+i holds piece i of rows
         // 4g..4g+3, and each store instruction writes eight whole rows
         {
-          const int gi = lane & 3;
 #pragma unroll
           for (int m = 2; m >= 1; m >>= 1) {
             const bool hi = (gi & m) != 0;
@@ -940,11 +944,10 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
               }
             }
           }
-          const int64_t row0 = t0 + wq * 32 + (lane & ~3);  // first row of this lane's group
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            if (wq * 32 + (lane & ~3) + j < valid) {
-              uint4 *dst = (uint4 *)(p.out + ((uint64_t)bh * p.n + row0 + j) * kDv) + 2 * gi;
+            if (j < rows_left) {
+              uint4 *dst = dst_row + j * (kDv / 8);
               asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst),
                            "r"(w[8 * j]), "r"(w[8 * j + 1]), "r"(w[8 * j + 2]), "r"(w[8 * j + 3]),
                            "r"(w[8 * j + 4]), "r"(w[8 * j + 5]), "r"(w[8 * j + 6]), "r"(w[8 * j + 7])
