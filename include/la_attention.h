@@ -64,6 +64,10 @@ int la_abi_version(void);
  * The reference has no counterpart (its dispatcher hides all failures). */
 int la_take_device_error(void *stream);
 
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads), for callers that account for launches; diagnostics only. */
+uint64_t la_launch_count(void);
+
 /* Width F of the Taylor feature basis for key width d_qk: 1 + d + d(d+1)/2
  * (153 at d_qk = 16).  Replaces the width computed by the reference's
  * taylor_feature_map (benchmarks/chunked_attention_benchmark.py:34-53). */

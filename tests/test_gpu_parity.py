@@ -181,6 +181,18 @@ def test_chunked_lead_main_split(t):
         assert O.rel_l2(np64(yn[bb, hh]), want) <= TOL_BF16
 
 
+def test_launch_counter_counts_each_kernel():
+    """la_launch_count: one output kernel unsegmented; state pass, running
+    sums and output with three segments."""
+    from trainium_linear_attention_b200 import _native as N
+    q, k, v = cuda(*inputs((1, 2, 3000, 16), 64, seed=9))
+    for segments, launches in ((1, 1), (3, 3)):
+        before = N.lib().la_launch_count()
+        ops.based_chunked(q, k, v, segments=segments)
+        torch.cuda.synchronize()
+        assert N.lib().la_launch_count() - before == launches
+
+
 def test_chunked_state_roundtrip():
     """Seeding the second half with the first half's final state reproduces
     the whole sequence; the states match the oracle's."""

@@ -33,6 +33,7 @@ EXPORTED_SYMBOLS = (
     "la_status_string",
     "la_abi_version",
     "la_take_device_error",
+    "la_launch_count",
     "la_based_feature_dim",
     "la_based_parallel_fwd",
     "la_based_chunked_plan",
@@ -68,6 +69,8 @@ def _declare(lib) -> None:
     lib.la_abi_version.restype = _int
     lib.la_take_device_error.argtypes = [_p]
     lib.la_take_device_error.restype = _int
+    lib.la_launch_count.argtypes = []
+    lib.la_launch_count.restype = ctypes.c_uint64
     lib.la_based_feature_dim.argtypes = [_i64]
     lib.la_based_feature_dim.restype = _i64
     lib.la_based_parallel_fwd.argtypes = [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _f, _p]

@@ -2,6 +2,7 @@
 // and dispatch between the tcgen05 tensor-core kernels (bf16, d_qk = 16,
 // d_v = 64 on sm_100) and the SIMT kernels (fp32 and every other shape).
 #include <math.h>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -31,6 +32,12 @@ int *device_error_word() {
   }
   return cache[dev];
 }
+
+namespace {
+std::atomic<uint64_t> g_launches{0};
+}  // namespace
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int current_device_info(DeviceInfo *info) {
   static std::mutex mu;
@@ -182,6 +189,8 @@ const char *la_status_string(int status) {
 }
 
 int la_abi_version(void) { return 1; }
+
+uint64_t la_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int la_take_device_error(void *stream) {
   DeviceInfo info;

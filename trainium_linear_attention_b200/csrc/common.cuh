@@ -47,8 +47,13 @@ int current_device_info(DeviceInfo *info);
 
 inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? LA_OK : LA_ERR_CUDA; }
 
-// Returns LA_ERR_CUDA if the most recent launch failed.
+// Counts one kernel launch (la_launch_count).
+void note_launch();
+
+// Called after every kernel launch: counts it and returns LA_ERR_CUDA if it
+// failed.
 inline int check_launch() {
+  note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LA_OK : LA_ERR_CUDA;
 }

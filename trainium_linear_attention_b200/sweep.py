@@ -4,8 +4,9 @@
 
 c2   chunked BASED, B=4, H=16, N=2048, d_qk=16, d_v=64
 c3   sliding-window softmax attention, B=4, H=16, N=4096, d=64, W=64 (config 3)
-c5   parallel and chunked BASED at B*N = 262144, H=16, N = 512 .. 65536: the
-     crossover that ``solution()`` dispatches on (config 5)
+c5   parallel and chunked BASED at B*N = 262144, H=16, N = 512 .. 65536 (by
+     default; --c5-min-n / --c5-max-n): the crossover that ``solution()``
+     dispatches on (config 5)
 
 All inputs are bf16, iid N(0,1) * scale (0.5 for BASED, 1 for sliding),
 generated on the device from a fixed seed.  Each point: warm-up calls, then
@@ -87,6 +88,7 @@ def main():
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--what", default="c2,c3,c5")
     ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--c5-min-n", type=int, default=512)
     ap.add_argument("--c5-max-n", type=int, default=65536)
     args = ap.parse_args()
     what = set(args.what.split(","))
@@ -104,7 +106,7 @@ def main():
         line("c3", "sliding", b, h, n, d, d, ms, st, h * (3 * d * 2 + d * 2), h * w * 4 * d,
              {"window": w})
     if "c5" in what:
-        n = 512
+        n = args.c5_min_n
         while n <= args.c5_max_n:
             b = 262144 // n
             q, k, v = inputs(b, h, n, dqk, dv, 0.5)
