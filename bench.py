@@ -1,11 +1,11 @@
 #!/usr/bin/env python
-"""Benchmark of the chunked BASED hot path, one JSON line.
+"""Benchmark of the chunked BASED hot path (benchmark configuration 4), one JSON line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--mode heads|sp] [--seq-len N] [--segments G]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-Default workload: chunked BASED, B=8, H=16, N=32768,
+Default workload (benchmark configuration 4): chunked BASED, B=8, H=16, N=32768,
 d_qk=16, d_v=64, bf16 inputs iid N(0,1)*0.5 (seeded per head), sharded by
 batch x head over the ranks (no collective on the data path).  A step is one
 pass of the chunked kernel over the rank's heads.  ``--mode sp`` runs the

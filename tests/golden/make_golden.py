@@ -60,7 +60,7 @@ def main(ref_root: str) -> None:
         out[f"{name}.q"], out[f"{name}.k"], out[f"{name}.v"] = q.numpy(), k.numpy(), v.numpy()
         out[f"{name}.out"] = ref_reduced(q, k, v, eps=eps).numpy()
 
-    # BASELINE config 1 exactly: B=1, H=4, N=256, d_qk=16, d_v=64, fp32, N(0,1)*0.5.
+    # benchmark configuration 1 exactly: B=1, H=4, N=256, d_qk=16, d_v=64, fp32, N(0,1)*0.5.
     based_case("c1", (1, 4, 256, 16), 64, seed=0)
     # ragged / odd lengths, d_v != d_qk, several heads
     based_case("par_odd", (2, 2, 65, 16), 32, seed=1)

@@ -1,7 +1,7 @@
 """GPU parity: the CUDA kernels (through the C ABI) against the CPU oracle and
 the reference's golden vectors.
 
-Tolerances (rel-L2 over the whole output, the north-star's metric):
+Tolerances (rel-L2 over the whole output, the parity metric):
   * fp32 inputs:  <= 1e-4 against the fp32 reference;
   * bf16 inputs:  <= 2e-2 against the fp32/fp64 reference evaluated on the
     same bf16-rounded inputs.
@@ -100,7 +100,7 @@ def test_chunked_fp32_golden(golden):
 
 
 def test_chunked_config2():
-    """B=4, H=16, N=2048, d_qk=16, d_v=64, bf16, chunk 64."""
+    """Configuration 2: B=4, H=16, N=2048, d_qk=16, d_v=64, bf16, chunk 64."""
     q, k, v = inputs((4, 16, 2048, 16), 64, seed=2)
     y = T.based_chunked(*cuda(q, k, v), chunk_size=64)
     want = O.based_attn_reduced(np64(q), np64(k), np64(v))
@@ -238,7 +238,7 @@ def test_chunked_sequence_parallel_emulated():
 
 
 def test_chunked_full_size_properties():
-    """BASELINE config 4 sizes (B=8, H=16, N=32768): two heads against the
+    """Configuration 4 sizes (B=8, H=16, N=32768): two heads against the
     oracle, every head through size-independent properties -- the output is a
     convex combination of the values (weights 1+s+s^2/2 > 0), and the
     segmented and unsegmented runs agree."""
@@ -293,7 +293,7 @@ def test_sliding_fp32_golden(golden, case):
 
 
 def test_sliding_config3():
-    """W=64, B=4, H=16, N=4096, d=64, bf16, N(0,1) inputs."""
+    """Configuration 3: W=64, B=4, H=16, N=4096, d=64, bf16, N(0,1) inputs."""
     q, k, v = inputs((4, 16, 4096, 64), 64, seed=3, scale=1.0)
     y = T.nki_sliding_window_attn(*cuda(q, k, v), window_size=64)
     want = O.sliding_window_attn(np64(q), np64(k), np64(v), 64)

@@ -2,7 +2,7 @@
 
     python -m trainium_linear_attention_b200.sweep [--what c2,c3,c5] [--steps 20]
 
-c2   chunked BASED, B=4, H=16, N=2048, d_qk=16, d_v=64
+c2   chunked BASED, B=4, H=16, N=2048, d_qk=16, d_v=64 (configuration 2)
 c3   sliding-window softmax attention, B=4, H=16, N=4096, d=64, W=64 (config 3)
 c5   parallel and chunked BASED at B*N = 262144, H=16, N = 512 .. 65536 (by
      default; --c5-min-n / --c5-max-n): the crossover that ``solution()``
