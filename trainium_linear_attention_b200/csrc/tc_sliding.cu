@@ -235,30 +235,35 @@ sliding_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       __syncwarp();
       tc_fence_after();
       const uint32_t srow = taddr(tmem, wq * 32, b * L::kBufCols);
+      // band of this row relative to the warp's first column; empty for rows
+      // past n, so that no per-element test of the row is needed
+      const int rel_lo = row_ok ? c_lo - w_lo : 1 << 20;
+      const int rel_hi = row_ok ? c_hi - w_lo : -(1 << 20);
       float m = -INFINITY;
       for (int ch = 0; ch < nchunk; ++ch) {
         uint32_t x[16];
         tmem_ld16(srow + w_lo + 16 * ch, x);
+        const int lo = rel_lo - 16 * ch, hi = rel_hi - 16 * ch;  // in-band: lo <= i <= hi
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int col = w_lo + 16 * ch + i;
-          if (col >= c_lo && col <= c_hi) m = fmaxf(m, __uint_as_float(x[i]));
-        }
+        for (int i = 0; i < 16; ++i)
+          m = fmaxf(m, (i >= lo && i <= hi) ? __uint_as_float(x[i]) : -INFINITY);
       }
-      const float mb = row_ok ? m * p.scale_log2 : 0.f;
+      const float mb = m * p.scale_log2;  // -inf for rows past n: every value masked below
+      const uint64_t sc2 = f2pack(p.scale_log2, p.scale_log2), nmb2 = f2pack(-mb, -mb);
       float l = 0.f;
       for (int ch = 0; ch < nchunk; ++ch) {
         uint32_t x[16], pk[8];
         tmem_ld16(srow + w_lo + 16 * ch, x);
+        const int lo = rel_lo - 16 * ch, hi = rel_hi - 16 * ch;
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int col = w_lo + 16 * ch + 2 * i;
-          float e0 = ex2_approx(fmaf(__uint_as_float(x[2 * i]), p.scale_log2, -mb));
-          float e1 = ex2_approx(fmaf(__uint_as_float(x[2 * i + 1]), p.scale_log2, -mb));
-          e0 = (row_ok && col >= c_lo && col <= c_hi) ? e0 : 0.f;
-          e1 = (row_ok && col + 1 >= c_lo && col + 1 <= c_hi) ? e1 : 0.f;
+          float a0, a1;
+          f2unpack(ffma2(f2pack(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1])), sc2, nmb2),
+                   a0, a1);
+          const float e0 = (2 * i >= lo && 2 * i <= hi) ? ex2_approx(a0) : 0.f;
+          const float e1 = (2 * i + 1 >= lo && 2 * i + 1 <= hi) ? ex2_approx(a1) : 0.f;
           l += e0 + e1;
           pk[i] = pack_bf16(e0, e1);
         }
