@@ -73,6 +73,21 @@ def test_parallel_tensor_core_lengths(t):
     assert O.rel_l2(np64(y), np64(ops.based_chunked(qc, kc, vc))) <= 1e-2
 
 
+@pytest.mark.parametrize("t", [384, 512, 513])
+def test_parallel_tensor_core_many_items(t):
+    """80 heads: the persistent kernel (N <= 512) runs several work items
+    per CTA, both TMEM buffers and O accumulators in turn; N = 513 takes the
+    one-CTA-per-tile kernel.  First, middle and last heads against the oracle."""
+    b, h = 2, 40
+    q, k, v = inputs((b, h, t, 16), 64, seed=t + 1)
+    y = ops.based_parallel(*cuda(q, k, v))
+    for bh in (0, 41, b * h - 1):
+        bb, hh = divmod(bh, h)
+        want = O.based_attn_reduced(np64(q[bb, hh]), np64(k[bb, hh]), np64(v[bb, hh]))
+        assert O.rel_l2(np64(y[bb, hh]), want) <= TOL_BF16
+    assert bool(torch.isfinite(y.float()).all())
+
+
 def test_parallel_tensor_core_matches_cuda_core_path():
     """Aligned tensors take the tcgen05 kernel, unaligned copies of the same
     values the CUDA-core kernel; both agree."""
