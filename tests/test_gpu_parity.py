@@ -73,13 +73,14 @@ def test_parallel_tensor_core_lengths(t):
     assert O.rel_l2(np64(y), np64(ops.based_chunked(qc, kc, vc))) <= 1e-2
 
 
-@pytest.mark.parametrize("t", [384, 512, 513])
-def test_parallel_tensor_core_many_items(t):
-    """80 heads: the persistent kernel (N <= 512) runs several work items
-    per CTA, both TMEM buffers and O accumulators in turn; N = 513 takes the
-    one-CTA-per-tile kernel.  First, middle and last heads against the oracle."""
-    b, h = 2, 40
-    q, k, v = inputs((b, h, t, 16), 64, seed=t + 1)
+@pytest.mark.parametrize("b,h,t", [(2, 40, 384), (2, 40, 512), (2, 40, 513), (8, 80, 256),
+                                   (8, 80, 300)])
+def test_parallel_tensor_core_many_items(b, h, t):
+    """The persistent kernel (N <= 512) runs several work items per CTA,
+    both TMEM buffers and O accumulators in turn: single items at 80 heads,
+    whole heads per CTA at 640; N = 513 takes the one-CTA-per-tile kernel.
+    First, middle and last heads against the oracle."""
+    q, k, v = inputs((b, h, t, 16), 64, seed=t + b)
     y = ops.based_parallel(*cuda(q, k, v))
     for bh in (0, 41, b * h - 1):
         bb, hh = divmod(bh, h)

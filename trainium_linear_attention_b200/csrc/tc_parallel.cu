@@ -284,6 +284,7 @@ struct ParallelParams {
   int64_t items;  // bh * tiles
   int64_t bh;
   int tiles;      // query tiles per head
+  int head_major; // a CTA takes whole heads (else single items, longest first)
   float eps;
 };
 
@@ -304,14 +305,24 @@ enum PBar {
 };
 static_assert(8 * kNumPBars + 8 <= 256, "barrier area");
 
-// The work item of a CTA's j-th turn: query tile qt of head h.
+// The work item of a CTA's j-th turn: query tile qt of head h.  Head-major
+// (many heads per SM): the CTA takes heads b, b + grid, ..., each with its
+// query tiles from the last down, so a head's K/V tiles are read again while
+// they are still in L2.  Otherwise single items round-robin, longest first.
 struct Item {
   int64_t h;
   int qt;
 };
 __device__ __forceinline__ Item item_of(const ParallelParams &p, int j) {
+  if (p.head_major)
+    return {blockIdx.x + (int64_t)(j / p.tiles) * gridDim.x, p.tiles - 1 - j % p.tiles};
   const int64_t idx = blockIdx.x + (int64_t)j * gridDim.x;
   return {idx % p.bh, p.tiles - 1 - (int)(idx / p.bh)};
+}
+__device__ __forceinline__ int item_count(const ParallelParams &p) {
+  if (p.head_major)
+    return (int64_t)blockIdx.x < p.bh ? (int)((p.bh - 1 - blockIdx.x) / gridDim.x + 1) * p.tiles : 0;
+  return (int64_t)blockIdx.x < p.items ? (int)((p.items - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
 }
 
 __device__ __forceinline__ bool wait_teardown(uint64_t *bar, uint32_t parity) {
@@ -332,8 +343,7 @@ parallel_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
   volatile int *abort_flag = (volatile int *)(smem + kOffBar + 8 * kNumPBars + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int count =
-      (int64_t)blockIdx.x < p.items ? (int)((p.items - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
+  const int count = item_count(p);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumPBars; ++i) mbar_init(&bars[i], 1);
@@ -612,6 +622,9 @@ int launch_parallel_tc(const void *q, const void *k, const void *v, void *out, i
                            persistent::kSmemAlloc) != cudaSuccess)
     return LA_ERR_CUDA;
   const int sms = info.sm_count > 0 ? info.sm_count : 1;
+  // whole heads per CTA once every SM has at least four (at most one head
+  // of imbalance in four)
+  p.head_major = bh >= 4 * (int64_t)sms ? 1 : 0;
   const int64_t grid = p.items < sms ? p.items : sms;
   persistent::parallel_tc_kernel<<<(unsigned)grid, persistent::kThreadsPar, persistent::kSmemAlloc,
                                    s>>>(mq, mk, mv, p);
