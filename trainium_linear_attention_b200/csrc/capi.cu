@@ -320,12 +320,16 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
     return LA_ERR_INVALID_ARGUMENT;  // nothing to reuse without segments
   }
   const bool normalize = (flags & LA_CHUNKED_NORMALIZE) != 0;
-  // With two segments the state pass covers only the first: it runs as two
-  // half-length pieces so that it fills as many SMs as the output pass.
-  const int ratio =
-      (tc && g == 2 && !(flags & LA_CHUNKED_REUSE_SEGMENTS) && seg_len % (2 * kSegmentTile) == 0)
-          ? 2
-          : 1;
+  // With two segments the state pass covers only the first: a long one runs
+  // as two half-length pieces so that it fills as many SMs as the output
+  // pass.  The two half states then need the running-sum launch; below
+  // kMinSplitStateTokens per segment that launch costs more than the halving
+  // saves (measured at B=4, H=16, N=2048: 0.044 ms unsplit vs 0.050 ms).
+  constexpr int64_t kMinSplitStateTokens = 32 * kSegmentTile;
+  const int ratio = (tc && g == 2 && !(flags & LA_CHUNKED_REUSE_SEGMENTS) &&
+                     seg_len % (2 * kSegmentTile) == 0 && seg_len >= kMinSplitStateTokens)
+                        ? 2
+                        : 1;
   if (g > 1 && !(flags & LA_CHUNKED_REUSE_SEGMENTS)) {
     // states of segments 0 .. g-2 (ratio slots each), then their prefix sums:
     // slot g - 1 seeds segment g
