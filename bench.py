@@ -17,7 +17,12 @@ events on the launching stream; L2 is flushed (256 MB write) before every
 timed step, outside the events; the per-rank sum is max-reduced over ranks
 after a barrier.  ``value`` = B*N tokens (heads not counted, the reference's
 convention) / that time.  ``e2e`` repeats the measurement through the public
-API with pinned host inputs copied in and the output copied back every step.
+API with pinned host inputs copied in and the output copied back every step
+(heads mode: ``based_chunked_host``, which copies one group of heads while
+the kernels of the previous group run and the group before is copied back;
+sequence-parallel mode: serial copies around the sequence-parallel forward).
+``sp_phases_ms`` (sequence-parallel mode) splits a step into the state pass,
+the NCCL all-gather with the prefix sum, and the seeded forward.
 ``--impl reference`` times the CPU port of the reference's chunked algorithm
 (oracle/, numpy, all host threads) on a bounded sample of the same workload.
 The other configurations (C2, C3 sliding window, the C5 parallel/chunked
@@ -58,6 +63,8 @@ def parse_args():
     ap.add_argument("--seq-len", type=int, default=None, help="override N (not a bench line)")
     ap.add_argument("--segments", type=int, default=0, help="0 = library's choice")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-groups", type=int, default=8,
+                    help="head groups of the end-to-end leg (copies overlap the kernels)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -239,7 +246,7 @@ def config_dict(args, b, h, n, dqk, dv):
             "batch": b, "heads": h, "seq_len": n, "d_qk": dqk, "d_v": dv, "chunk_size": 64,
             "global_batch": b, "parallelism": (f"heads{args.gpus}" if args.mode == "heads"
                                                else f"sp{args.gpus}"),
-            "inputs": "iid N(0,1)*0.5, seeded per head, bf16",
+            "inputs": "iid N(0,1)*0.5, seeded, bf16 (the reference arm: fp32 numpy sample)",
             "l2": "flushed (256 MB write) before every timed step"}
 
 
@@ -289,8 +296,15 @@ def run_ours(args):
         def step():
             return ops.based_chunked(q, k, v, chunk_size=64, segments=seg, workspace=workspace)
     else:
+        sp_timings = D.SPTimings()
+        sp_sums = {"state_ms": 0.0, "exchange_ms": 0.0, "forward_ms": 0.0, "steps": 0}
+
         def step():
-            return D.sequence_parallel_forward(q, k, v, chunk_size=64)
+            y = D.sequence_parallel_forward(q, k, v, chunk_size=64, timings=sp_timings)
+            for key in ("state_ms", "exchange_ms", "forward_ms"):
+                sp_sums[key] += getattr(sp_timings, key)
+            sp_sums["steps"] += 1
+            return y
 
     def barrier():
         if world > 1:
@@ -312,6 +326,9 @@ def run_ours(args):
     torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if args.mode == "sp":
+        for key in sp_sums:
+            sp_sums[key] = 0.0 if key != "steps" else 0
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             flush.zero_()
@@ -326,22 +343,32 @@ def run_ours(args):
     tokens = b * n  # B*N, the reference's tokens convention (heads not counted)
     value = tokens * args.steps / (total_ms / 1e3)
     ms_per_step = total_ms / args.steps
+    sp_split = None
+    if args.mode == "sp":
+        # per-step device time of each phase, max over ranks (state pass,
+        # NCCL all-gather + prefix sum, seeded forward)
+        n_sp = max(1, sp_sums["steps"])
+        sp_split = {key: max_over_ranks(sp_sums[key] / n_sp)
+                    for key in ("state_ms", "exchange_ms", "forward_ms")}
 
     # ---- end to end through the public API (pinned host in, host out)
     e2e = None
     if not args.no_e2e:
         out_host = torch.empty((1, local_heads, t_local, dv), dtype=torch.bfloat16).pin_memory()
-        from trainium_linear_attention_b200 import based_chunked as api_based_chunked
+        from trainium_linear_attention_b200 import based_chunked_host as api_based_chunked_host
 
-        def e2e_step():
-            qd = qh.to(dev, non_blocking=True)
-            kd = kh.to(dev, non_blocking=True)
-            vd = vh.to(dev, non_blocking=True)
-            if args.mode == "heads":
-                y = api_based_chunked(qd, kd, vd, chunk_size=64)
-            else:
+        if args.mode == "heads":
+            def e2e_step():
+                # copies of one group of heads overlap the kernels of the previous one
+                api_based_chunked_host(qh, kh, vh, chunk_size=64, out=out_host,
+                                       head_groups=args.e2e_groups)
+        else:
+            def e2e_step():
+                qd = qh.to(dev, non_blocking=True)
+                kd = kh.to(dev, non_blocking=True)
+                vd = vh.to(dev, non_blocking=True)
                 y = D.sequence_parallel_forward(qd, kd, vd, chunk_size=64)
-            out_host.copy_(y, non_blocking=True)
+                out_host.copy_(y, non_blocking=True)
 
         for _ in range(args.warmup):
             e2e_step()
@@ -360,7 +387,9 @@ def run_ours(args):
         d2h = out_host.numel() * out_host.element_size()
         e2e = {"value": tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "ms_per_step": e2e_ms / args.steps}
+               "ms_per_step": e2e_ms / args.steps,
+               "pipelining": (f"{args.e2e_groups} head groups, copies on two side streams"
+                              if args.mode == "heads" else "serial copies")}
 
     # ---- roofline of the step on this rank (the chunked kernel dominates it)
     hbm_gbs, tflops, peak_kind = measured_peaks()
@@ -393,10 +422,14 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
-            "config": dict(config_dict(args, b, h, n, dqk, dv), segments=g),
+            "config": config_dict(args, b, h, n, dqk, dv),
+            "plan": {"segments_per_head": g, "local_heads": local_heads,
+                     "local_tokens": t_local},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "clocks": clk.summary(), "gpu_launches": launches_per_step * args.steps,
         }
+        if sp_split is not None:
+            line["sp_phases_ms"] = sp_split
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

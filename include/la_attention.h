@@ -4,9 +4,12 @@
  *
  * Every entry point takes plain device pointers, sizes and a cudaStream_t
  * passed as void*, enqueues its kernels on that stream and returns an int
- * status (LA_OK == 0).  No entry point synchronises the stream, allocates
- * device memory or keeps state between calls; all are safe to call from
- * several host threads at once.
+ * status (LA_OK == 0).  No entry point synchronises the stream (except
+ * la_take_device_error, which says so) or allocates device memory.  All
+ * except la_based_chunked_fwd_noalloc keep no state between calls and are
+ * safe to call from several host threads at once; that one shares a scratch
+ * array compiled into the library between all its calls on a device (see
+ * its comment).
  *
  * Tensor layout: every q/k/v/out is a contiguous (batch, heads, seq_len, d)
  * row-major array in the element type given by `dtype`.  q and k have width
@@ -49,6 +52,11 @@ extern "C" {
 #define LA_CHUNKED_NORMALIZE        1u  /* divide by the normaliser (+eps)        */
 #define LA_CHUNKED_REUSE_SEGMENTS   2u  /* workspace already holds the segment
                                            seeds written by la_based_chunked_state */
+#define LA_CHUNKED_IDENTITY         4u  /* identity feature map phi(x) = x instead
+                                           of the Taylor map: the reference's
+                                           ref_identity_numerator (benchmarks/
+                                           chunked_attention_benchmark.py:81-93);
+                                           numerator only (not with NORMALIZE)   */
 
 /* Human-readable name of a status code (static storage, never NULL). */
 const char *la_status_string(int status);
@@ -98,6 +106,10 @@ int la_based_parallel_fwd(const void *q, const void *k, const void *v, void *out
  * LA_CHUNKED_NORMALIZE the normaliser is carried too (the reference returns
  * the numerator only).
  *
+ * With LA_CHUNKED_IDENTITY the feature map is the identity (the reference's
+ * ref_identity_numerator): phi_k(k) = k, phi_q(q) = q / sqrt(d_qk), F = d_qk,
+ * and only the numerator is returned (NORMALIZE is rejected).
+ *
  * State layout (init_state / final_state / la_based_chunked_state): fp32
  * (batch*heads, F, d_v + 1) in the key-side feature basis
  *     phi_k(k) = [1, k_0 .. k_{d-1}, k_i * k_j for i <= j in row-major order]
@@ -145,7 +157,8 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
  * needing more scratch returns LA_ERR_WORKSPACE; LA_CHUNKED_REUSE_SEGMENTS is
  * rejected (LA_ERR_INVALID_ARGUMENT).  All calls on a device share the array
  * and leave its contents behind: calls whose kernels overlap on the GPU race
- * on it.  The first call on a device resolves the array's address; make it
+ * on it.  The array's address belongs to the CUDA context: the first call in
+ * each context resolves it (and caches it for that context); make that call
  * before any stream capture.  The reference has no counterpart. */
 int la_based_chunked_fwd_noalloc(const void *q, const void *k, const void *v, void *out,
                                  int64_t batch, int64_t heads, int64_t seq_len,

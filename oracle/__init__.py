@@ -22,6 +22,8 @@ from .based_oracle import (  # noqa: F401
     kernel_feature_map_k,
     kernel_feature_map_q,
     sliding_window_attn,
+    identity_numerator,
+    identity_chunked,
     feature_dim,
     rel_l2,
 )

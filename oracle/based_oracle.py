@@ -239,6 +239,55 @@ def based_chunked(q, k, v, chunk: int = 64, eps: float = 1e-6, normalize: bool =
     return out
 
 
+def identity_numerator(q, k, v, dtype=np.float64):
+    """Dense identity-feature-map numerator, tril((q / sqrt(d)) k^T) v.
+
+    Follows benchmarks/chunked_attention_benchmark.py:81-93
+    (``ref_identity_numerator``: scale, mask, multiply by v; no feature map).
+    """
+    q = np.asarray(q, dtype=dtype)
+    k = np.asarray(k, dtype=dtype)
+    v = np.asarray(v, dtype=dtype)
+    d = q.shape[-1]
+    t = q.shape[-2]
+    s = np.matmul(q / math.sqrt(d), np.swapaxes(k, -1, -2))
+    s = s * np.tril(np.ones((t, t), dtype=dtype))
+    return np.matmul(s, v)
+
+
+def identity_chunked(q, k, v, chunk: int = 64, init_state=None, return_state: bool = False,
+                     dtype=np.float64):
+    """Chunked identity-feature-map numerator.
+
+    The recurrence of old/identity_linear_attn_nki_CHUNKED.py:38-59 (the
+    reference's chunked identity kernel: acc = Q_c S; acc += tril(Q_c K_c^T) V_c;
+    S += K_c^T V_c) with Q pre-scaled by 1/sqrt(d) as its caller does.  The
+    state is ``(..., d_qk, d_v + 1)`` with sum k as the last column, the
+    layout of the kernels' identity state.
+    """
+    q = np.asarray(q, dtype=dtype) / math.sqrt(q.shape[-1])
+    k = np.asarray(k, dtype=dtype)
+    v = np.asarray(v, dtype=dtype)
+    lead = q.shape[:-2]
+    t = q.shape[-2]
+    d, dv = k.shape[-1], v.shape[-1]
+    S = (np.zeros(lead + (d, dv + 1), dtype=dtype) if init_state is None
+         else np.array(init_state, dtype=dtype, copy=True))
+    v_aug = np.concatenate([v, np.ones(v.shape[:-1] + (1,), dtype=dtype)], axis=-1)
+    out = np.empty(lead + (t, dv), dtype=dtype)
+    for c0 in range(0, t, chunk):
+        c1 = min(t, c0 + chunk)
+        qc, kc, va = q[..., c0:c1, :], k[..., c0:c1, :], v_aug[..., c0:c1, :]
+        n = c1 - c0
+        acc = np.matmul(qc, S) + np.matmul(
+            np.matmul(qc, np.swapaxes(kc, -1, -2)) * np.tril(np.ones((n, n), dtype=dtype)), va)
+        S = S + np.matmul(np.swapaxes(kc, -1, -2), va)
+        out[..., c0:c1, :] = acc[..., :dv]
+    if return_state:
+        return out, S
+    return out
+
+
 # ---------------------------------------------------------------------------
 # Sliding-window softmax
 # ---------------------------------------------------------------------------

@@ -17,6 +17,7 @@ Functions called (reference file:line):
   benchmarks/chunked_attention_benchmark.py:34      taylor_feature_map
   benchmarks/chunked_attention_benchmark.py:55      ref_based_attn (dense Taylor features)
   benchmarks/chunked_attention_benchmark.py:68      ref_based_numerator
+  benchmarks/chunked_attention_benchmark.py:81      ref_identity_numerator
   benchmarks/sliding_attention_benchmark.py:32      ref_sliding_window_attn
 """
 
@@ -82,6 +83,19 @@ def main(ref_root: str) -> None:
     out["dense.q"], out["dense.k"], out["dense.v"] = q.numpy(), k.numpy(), v.numpy()
     out["dense.out"] = cab.ref_based_attn(q, k, v, eps=1e-6).numpy()
     out["dense.num"] = cab.ref_based_numerator(q, k, v).numpy()
+
+    # identity feature map, numerator only (fp32 inputs)
+    def identity_case(name, shape_qk, dv, seed):
+        gen = torch.Generator().manual_seed(seed)
+        b, h, t, d = shape_qk
+        q = _randn(gen, (b, h, t, d), 0.5)
+        k = _randn(gen, (b, h, t, d), 0.5)
+        v = _randn(gen, (b, h, t, dv), 0.5)
+        out[f"{name}.q"], out[f"{name}.k"], out[f"{name}.v"] = q.numpy(), k.numpy(), v.numpy()
+        out[f"{name}.num"] = cab.ref_identity_numerator(q, k, v).numpy()
+
+    identity_case("ident", (1, 2, 192, 16), 64, seed=40)
+    identity_case("ident_odd", (2, 2, 77, 16), 32, seed=41)
 
     # sliding window softmax
     def slide_case(name, shape, window, seed):

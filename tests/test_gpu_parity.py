@@ -254,22 +254,102 @@ def test_chunked_sequence_parallel_emulated():
 
 
 def test_chunked_full_size_properties():
-    """Configuration 4 sizes (B=8, H=16, N=32768): two heads against the
-    oracle, every head through size-independent properties -- the output is a
-    convex combination of the values (weights 1+s+s^2/2 > 0), and the
-    segmented and unsegmented runs agree."""
+    """Configuration 4 sizes (B=8, H=16, N=32768): eight heads spread over the
+    batch (the last included) against the fp64 oracle, every head through
+    size-independent properties -- the output is a convex combination of the
+    values (weights 1+s+s^2/2 > 0), and the segmented and unsegmented runs
+    agree."""
     q, k, v = inputs((8, 16, 32768, 16), 64, seed=4)
     qd, kd, vd = cuda(q, k, v)
     y = T.based_chunked(qd, kd, vd)
-    for bh in (0, 127):
+    for bh in (0, 17, 38, 55, 72, 93, 110, 127):
         b, h = divmod(bh, 16)
-        want = O.based_chunked(np64(q[b, h]), np64(k[b, h]), np64(v[b, h]))
+        want = O.based_chunked(np64(q[b, h]), np64(k[b, h]), np64(v[b, h]), chunk=1024)
         assert O.rel_l2(np64(y[b, h]), want) <= TOL_BF16
     vmax = vd.float().abs().amax(dim=2, keepdim=True)
     assert bool((y.float().abs() <= vmax * 1.01 + 1e-3).all())
     assert bool(torch.isfinite(y.float()).all())
     yg = ops.based_chunked(qd, kd, vd, segments=4)
     assert O.rel_l2(np64(yg), np64(y)) <= 1e-2
+
+
+def test_sequence_parallel_full_length_emulated():
+    """Configuration 4's sequence-parallel variant at full length (B=1, H=16,
+    N=262144) with 8 ranks emulated on one GPU through the same calls a rank
+    makes: its state pass with per-segment running sums left in its
+    workspace, the exclusive prefix of the earlier ranks' states, and the
+    seeded forward that reuses those segment sums.  Heads 0, 7 and 15 against
+    the fp64 chunked oracle over all 262144 tokens; every head finite and a
+    convex combination of the values."""
+    world, n = 8, 262144
+    q, k, v = inputs((1, 16, n, 16), 64, seed=262)
+    qd, kd, vd = cuda(q, k, v)
+    per = n // world
+    states, outs = [], []
+    holders = []
+    for r in range(world):
+        sl = slice(r * per, (r + 1) * per)
+        kr, vr = kd[:, :, sl], vd[:, :, sl]
+        g, ws_bytes = ops.chunked_plan(16, per, 16, 64, torch.bfloat16)
+        ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=DEV)
+        states.append(ops.based_chunked_state(kr, vr, segments=g, workspace=ws))
+        holders.append((g, ws))
+    for r in range(world):
+        sl = slice(r * per, (r + 1) * per)
+        prefix = torch.zeros_like(states[0])
+        for j in range(r):
+            prefix += states[j]
+        g, ws = holders[r]
+        outs.append(ops.based_chunked(qd[:, :, sl], kd[:, :, sl], vd[:, :, sl], init_state=prefix,
+                                      segments=g, workspace=ws, reuse_segments=g > 1))
+    y = torch.cat(outs, 2)
+    for h in (0, 7, 15):
+        want = O.based_chunked(np64(q[0, h]), np64(k[0, h]), np64(v[0, h]), chunk=1024)
+        assert O.rel_l2(np64(y[0, h]), want) <= TOL_BF16
+    assert bool(torch.isfinite(y.float()).all())
+    vmax = vd.float().abs().amax(dim=2, keepdim=True)
+    assert bool((y.float().abs() <= vmax * 1.01 + 1e-3).all())
+
+
+@pytest.mark.parametrize("n", [2048, 8192, 65536])
+def test_parallel_long_sequences_config5(n):
+    """Configuration 5's parallel kernel at B*N = 262144, H = 16: at N = 65536
+    each query tile walks up to 512 key tiles.  Two heads against the fp64
+    chunked oracle, every head against the chunked kernel."""
+    b = 262144 // n
+    q, k, v = inputs((b, 16, n, 16), 64, seed=500 + n)
+    qd, kd, vd = cuda(q, k, v)
+    y = ops.based_parallel(qd, kd, vd)
+    for bh in (0, b * 16 - 1):
+        bb, hh = divmod(bh, 16)
+        want = O.based_chunked(np64(q[bb, hh]), np64(k[bb, hh]), np64(v[bb, hh]), chunk=1024)
+        assert O.rel_l2(np64(y[bb, hh]), want) <= TOL_BF16
+    yc = ops.based_chunked(qd, kd, vd)
+    err = (y.float() - yc.float()).reshape(b * 16, -1).norm(dim=1) / \
+        yc.float().reshape(b * 16, -1).norm(dim=1)
+    assert float(err.max()) <= 1e-2
+
+
+def test_host_buffer_api_matches_device_call():
+    """based_chunked_host (pinned host tensors, copies overlapped with the
+    kernels per head group) gives the device call's result bit for bit, for
+    head counts that do and do not divide into the groups."""
+    for b, h, groups in ((2, 8, 8), (1, 5, 3), (1, 2, 8)):
+        q, k, v = inputs((b, h, 1500, 16), 64, seed=40 + h)
+        qp, kp, vp = (x.pin_memory() for x in (q, k, v))
+        y = T.based_chunked_host(qp, kp, vp, head_groups=groups)
+        torch.cuda.current_stream().synchronize()
+        assert y.device.type == "cpu"
+        # the same kernels on the same groups of heads (the segmentation, and
+        # so the rounding, depends on a call's head count)
+        qd, kd, vd = (x.reshape(1, b * h, 1500, -1) for x in cuda(q, k, v))
+        step = -(-(b * h) // min(groups, b * h))
+        want = torch.cat([ops.based_chunked(qd[:, lo:lo + step], kd[:, lo:lo + step],
+                                            vd[:, lo:lo + step])
+                          for lo in range(0, b * h, step)], 1).reshape(b, h, 1500, 64)
+        assert torch.equal(y, want.cpu())
+        oracle = O.based_attn_reduced(np64(q), np64(k), np64(v))
+        assert O.rel_l2(np64(y), oracle) <= TOL_BF16
 
 
 def test_deterministic():
@@ -349,8 +429,63 @@ def test_solution_dispatch_and_errors():
     y = T.solution(q, k, v)
     want = O.based_attn_reduced(np64(q), np64(k), np64(v))
     assert O.rel_l2(np64(y), want) <= TOL_BF16
+    assert torch.equal(y, ops.based_chunked(q, k, v))  # long: the chunked kernel
     with pytest.raises(TypeError):
         T.solution(q.half(), k.half(), v.half())
     with pytest.raises(RuntimeError):  # d_qk beyond the kernels: raises, no fallback
         qq = torch.zeros(1, 1, 8, 256, device=DEV, dtype=torch.bfloat16)
         T.solution_nki(qq, qq, qq)
+
+
+def test_solution_short_sequence_takes_parallel_kernel():
+    """N = 256 is below the measured crossover: solution() runs the parallel
+    kernel (one launch, bit-identical to solution_nki, different from the
+    chunked kernel's rounding) and matches the oracle."""
+    from trainium_linear_attention_b200 import _native as N
+    q, k, v = inputs((4, 16, 256, 16), 64, seed=256)
+    qd, kd, vd = cuda(q, k, v)
+    torch.cuda.synchronize()
+    before = N.lib().la_launch_count()
+    y = T.solution(qd, kd, vd)
+    torch.cuda.synchronize()
+    assert N.lib().la_launch_count() - before == 1
+    assert torch.equal(y, T.solution_nki(qd, kd, vd))
+    assert not torch.equal(y, ops.based_chunked(qd, kd, vd))
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+
+
+# --------------------------------------------------------- identity map ---
+
+@pytest.mark.parametrize("case", ["ident", "ident_odd"])
+def test_identity_fp32_golden(golden, case):
+    """chunked_identity_numerator (fp32) against the reference's own
+    ref_identity_numerator outputs."""
+    q, k, v = (torch.from_numpy(golden[f"{case}.{n}"]).to(DEV) for n in "qkv")
+    y = T.chunked_identity_numerator(q, k, v)
+    assert y.dtype == torch.float32
+    assert O.rel_l2(y.cpu().numpy(), golden[f"{case}.num"]) <= TOL_FP32
+
+
+@pytest.mark.parametrize("t,segments", [(1, 0), (65, 0), (1000, 0), (3000, 3), (4096, 0)])
+def test_identity_bf16(t, segments):
+    q, k, v = inputs((2, 4, t, 16), 64, seed=900 + t)
+    qd, kd, vd = cuda(q, k, v)
+    y = ops.based_chunked(qd, kd, vd, normalize=False, feature_map="identity", segments=segments)
+    want = O.identity_numerator(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+
+
+def test_identity_state_roundtrip():
+    q, k, v = cuda(*inputs((1, 2, 900, 16), 64, seed=77, dtype=torch.float32))
+    y, s = ops.based_chunked(q, k, v, normalize=False, feature_map="identity", return_state=True)
+    want, s_want = O.identity_chunked(np64(q), np64(k), np64(v), return_state=True)
+    assert O.rel_l2(np64(y), want) <= TOL_FP32
+    assert O.rel_l2(s.double().cpu().numpy(), s_want.reshape(2, 16, 65)) <= TOL_FP32
+    a, sa = ops.based_chunked(q[:, :, :400], k[:, :, :400], v[:, :, :400], normalize=False,
+                              feature_map="identity", return_state=True)
+    b = ops.based_chunked(q[:, :, 400:], k[:, :, 400:], v[:, :, 400:], normalize=False,
+                          feature_map="identity", init_state=sa)
+    assert O.rel_l2(np64(torch.cat([a, b], 2)), want) <= TOL_FP32
+    with pytest.raises(ValueError):
+        ops.based_chunked(q, k, v, feature_map="identity")  # normalised identity: rejected

@@ -110,3 +110,12 @@ def test_no_device_is_reported_not_faked():
     p = ctypes.c_void_p(16)
     st = N.lib().la_based_parallel_fwd(p, p, p, p, 1, 1, 8, 16, 64, 1, 1e-6, None)
     assert st == N.LA_ERR_NO_DEVICE
+
+
+def test_identity_flag_is_numerator_only():
+    """LA_CHUNKED_IDENTITY with LA_CHUNKED_NORMALIZE is rejected before any
+    device work (the identity map has no normalised form in the reference)."""
+    p = ctypes.c_void_p(256)
+    flags = N.LA_CHUNKED_IDENTITY | N.LA_CHUNKED_NORMALIZE
+    assert N.lib().la_based_chunked_fwd(p, p, p, p, 1, 1, 8, 16, 64, 1, 64, 1e-6, flags, None,
+                                        None, None, 0, 0, None) == N.LA_ERR_INVALID_ARGUMENT

@@ -103,3 +103,28 @@ def test_planted_error_is_caught(golden):
     q, k, v = golden["c1.q"], golden["c1.k"], golden["c1.v"].copy()
     v[0, 1, 100, 3] += 1.0
     assert O.rel_l2(O.based_attn_reduced(q, k, v), golden["c1.out"]) > 1e-3
+
+
+@pytest.mark.parametrize("case", ["ident", "ident_odd"])
+def test_identity_numerator_matches_reference(golden, case):
+    """oracle.identity_numerator / identity_chunked vs
+    benchmarks/chunked_attention_benchmark.py:81 ref_identity_numerator, at
+    several chunk sizes (the recurrence is exact algebra)."""
+    q, k, v = golden[f"{case}.q"], golden[f"{case}.k"], golden[f"{case}.v"]
+    want = golden[f"{case}.num"]
+    assert O.rel_l2(O.identity_numerator(q, k, v), want) < 1e-6
+    for chunk in (1, 13, 64, 1000):
+        assert O.rel_l2(O.identity_chunked(q, k, v, chunk=chunk), want) < 1e-6
+
+
+def test_identity_chunked_state_is_additive():
+    """Seeding the second half with the first half's identity state gives the
+    whole sequence (the sequence-split property the segmented kernels use)."""
+    rng = np.random.default_rng(5)
+    q, k = rng.standard_normal((2, 1, 2, 300, 16)) * 0.5
+    v = rng.standard_normal((1, 2, 300, 24)) * 0.5
+    whole = O.identity_chunked(q, k, v)
+    a, s = O.identity_chunked(q[..., :128, :], k[..., :128, :], v[..., :128, :], return_state=True)
+    b = O.identity_chunked(q[..., 128:, :], k[..., 128:, :], v[..., 128:, :], init_state=s)
+    assert s.shape == (1, 2, 16, 25)
+    assert O.rel_l2(np.concatenate([a, b], -2), whole) < 1e-12

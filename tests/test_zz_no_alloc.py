@@ -46,23 +46,28 @@ def _inputs(b, h, t, seed):
 
 
 def test_noalloc_matches_regular_entry_point_twice():
-    q, k, v = _inputs(1, 8, 4096, seed=21)
+    """Two calls in a row with different inputs of the same shape and segment
+    count: each must equal the regular entry point bit for bit (both run the
+    same kernels), so a call that read the previous call's segment states
+    from the shared scratch would fail here."""
     segments = 4
     g, ws = ops.chunked_plan(8, 4096, 16, 64, torch.bfloat16, segments)
     assert g == segments and 0 < ws <= SCRATCH_BYTES  # the scratch is really used
-    want = ops.based_chunked(q, k, v, segments=segments)  # caller-allocated workspace
-    oracle = O.based_attn_reduced(*(x.float().cpu().numpy().astype(np.float64) for x in (q, k, v)))
-    for _ in range(2):  # two calls in a row share the scratch
+    for seed in (21, 22):
+        q, k, v = _inputs(1, 8, 4096, seed=seed)
+        want = ops.based_chunked(q, k, v, segments=segments)  # caller-allocated workspace
         out = torch.empty_like(v)
         assert _noalloc(q, k, v, out, segments) == N.LA_OK
         torch.cuda.synchronize()
-        assert O.rel_l2(out.float().cpu().numpy(), want.float().cpu().numpy()) <= TOL_BF16
+        assert torch.equal(out, want)
+        oracle = O.based_attn_reduced(*(x.float().cpu().numpy().astype(np.float64)
+                                        for x in (q, k, v)))
         assert O.rel_l2(out.float().cpu().numpy(), oracle) <= TOL_BF16
     num = torch.empty_like(v)
     assert _noalloc(q, k, v, num, segments, normalize=False) == N.LA_OK
     want_num = ops.based_chunked(q, k, v, segments=segments, normalize=False)
     torch.cuda.synchronize()
-    assert O.rel_l2(num.float().cpu().numpy(), want_num.float().cpu().numpy()) <= TOL_BF16
+    assert torch.equal(num, want_num)
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch():
@@ -81,9 +86,9 @@ def test_noalloc_rejects_requests_beyond_its_scratch():
 def test_noalloc_lead_main_split():
     """segments=0 at 96 heads: the library's lead/main split, one seed state
     per head in the scratch."""
-    q, k, v = _inputs(6, 16, 4096, seed=22)
+    q, k, v = _inputs(6, 16, 4096, seed=23)
     want = ops.based_chunked(q, k, v)
     out = torch.empty_like(v)
     assert _noalloc(q, k, v, out, 0) == N.LA_OK
     torch.cuda.synchronize()
-    assert O.rel_l2(out.float().cpu().numpy(), want.float().cpu().numpy()) <= 1e-6
+    assert torch.equal(out, want)

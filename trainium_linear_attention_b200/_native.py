@@ -27,6 +27,7 @@ LA_DTYPE_BFLOAT16 = 1
 
 LA_CHUNKED_NORMALIZE = 1
 LA_CHUNKED_REUSE_SEGMENTS = 2
+LA_CHUNKED_IDENTITY = 4
 
 #: every symbol declared in include/la_attention.h
 EXPORTED_SYMBOLS = (

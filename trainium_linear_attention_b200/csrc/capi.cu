@@ -1,6 +1,7 @@
 // C ABI entry points (include/la_attention.h): argument validation, planning
 // and dispatch between the tcgen05 tensor-core kernels (bf16, d_qk = 16,
 // d_v = 64 on sm_100) and the SIMT kernels (fp32 and every other shape).
+#include <cuda.h>
 #include <math.h>
 #include <atomic>
 #include <mutex>
@@ -10,28 +11,73 @@
 
 namespace la {
 
-// The library's device error word (one per device that loads the library).
+// The library's device error word (one per context that loads the library).
 __device__ int la_device_error_word;
 
-int *device_error_word() {
+namespace {
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext *);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long *);
+
+void *driver_entry(const char *name) {
+  void *ptr = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    ptr = nullptr;
+  cudaGetLastError();
+  return ptr;
+}
+
+// Unique id (cuCtxGetId) of the context current on this thread; false if no
+// context is current or the driver cannot tell.
+bool current_context_id(unsigned long long *id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    get_current = (CtxGetCurrentFn)driver_entry("cuCtxGetCurrent");
+    get_id = (CtxGetIdFn)driver_entry("cuCtxGetId");
+  });
+  CUcontext ctx = nullptr;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx) return false;
+  return get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+void *context_symbol_address(const void *symbol) {
+  struct Entry {
+    unsigned long long ctx;
+    const void *symbol;
+    void *addr;
+  };
   static std::mutex mu;
-  static int *cache[64] = {};
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+  static Entry cache[256];
+  static int used = 0;
+  unsigned long long ctx = 0;
+  bool known = current_context_id(&ctx);
+  if (known) {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i)
+      if (cache[i].ctx == ctx && cache[i].symbol == symbol) return cache[i].addr;
+  }
+  // Resolve in the current context (the runtime creates the device's primary
+  // context here if no context was current yet).
+  void *addr = nullptr;
+  if (cudaGetSymbolAddress(&addr, symbol) != cudaSuccess) {
     cudaGetLastError();
     return nullptr;
   }
-  std::lock_guard<std::mutex> lock(mu);
-  if (!cache[dev]) {
-    int *ptr = nullptr;
-    if (cudaGetSymbolAddress((void **)&ptr, la_device_error_word) != cudaSuccess) {
-      cudaGetLastError();
-      return nullptr;
-    }
-    cache[dev] = ptr;
+  if (!known) known = current_context_id(&ctx);
+  if (known) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (used < 256) cache[used++] = Entry{ctx, symbol, addr};
   }
-  return cache[dev];
+  return addr;
 }
+
+int *device_error_word() { return (int *)context_symbol_address(&la_device_error_word); }
 
 namespace {
 std::atomic<uint64_t> g_launches{0};
@@ -156,18 +202,43 @@ size_t state_floats(int64_t bh, int64_t dqk, int64_t dv) {
 
 }  // namespace
 
-size_t chunked_fwd_scratch_bytes(int64_t bh, int64_t n, int64_t d_qk, int64_t d_v, int dtype,
-                                 int segments, unsigned flags) {
-  if (segments == 0 && !(flags & LA_CHUNKED_REUSE_SEGMENTS) &&
-      use_tensor_cores(dtype, d_qk, d_v) && tc_chunked_enabled()) {
-    DeviceInfo info;
-    if (require_sm100(&info) == LA_OK && lead_tokens(bh, n, info.sm_count) > 0)
-      return (state_floats(bh, d_qk, d_v) * sizeof(float) + 255) / 256 * 256;
+int plan_chunked_fwd(const void *q, const void *k, const void *v, const void *out, int64_t bh,
+                     int64_t n, int64_t d_qk, int64_t d_v, int dtype, int segments,
+                     unsigned flags, ChunkedFwdPlan *plan) {
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != LA_OK) return st;
+  ChunkedFwdPlan p;
+  p.identity = (flags & LA_CHUNKED_IDENTITY) != 0;
+  p.features = p.identity ? d_qk : feature_dim(d_qk);
+  p.tc = !p.identity && use_tensor_cores(dtype, d_qk, d_v) && aligned16(q) && aligned16(k) &&
+         aligned16(v) && aligned32(out);
+  if (!p.tc && !chunked_simt_supported(p.features, d_qk, d_v)) return LA_ERR_UNSUPPORTED;
+  const bool reuse = (flags & LA_CHUNKED_REUSE_SEGMENTS) != 0;
+  const size_t head_state_bytes = (size_t)p.features * (size_t)(d_v + 1) * sizeof(float);
+  p.lead = (segments == 0 && p.tc && !reuse && n > 0) ? lead_tokens(bh, n, info.sm_count) : 0;
+  if (p.lead > 0) {
+    p.g = 1;
+    p.seg_len = n;
+    p.scratch = ((size_t)bh * head_state_bytes + 255) / 256 * 256;
+    *plan = p;
+    return LA_OK;
   }
-  int g = 0;
-  size_t need = 0;
-  if (la_based_chunked_plan(bh, n, d_qk, d_v, dtype, segments, &g, &need) != LA_OK) return 0;
-  return need;
+  p.g = segments == 0 ? auto_segments(bh, n, info.sm_count) : effective_segments(n, segments);
+  p.seg_len = p.g > 1 ? segment_len(n, p.g) : n;
+  // With two segments the state pass covers only the first: a long one runs
+  // as two half-length pieces so that it fills as many SMs as the output
+  // pass.  The two half states then need the running-sum launch; below
+  // kMinSplitStateTokens per segment that launch costs more than the halving
+  // saves (measured at B=4, H=16, N=2048: 0.044 ms unsplit vs 0.050 ms).
+  constexpr int64_t kMinSplitStateTokens = 32 * kSegmentTile;
+  p.ratio = (p.tc && p.g == 2 && !reuse && p.seg_len % (2 * kSegmentTile) == 0 &&
+             p.seg_len >= kMinSplitStateTokens)
+                ? 2
+                : 1;
+  p.scratch = p.g > 1 ? ((size_t)bh * p.g * head_state_bytes + 255) / 256 * 256 : 0;
+  *plan = p;
+  return LA_OK;
 }
 }  // namespace la
 
@@ -221,7 +292,7 @@ int la_based_parallel_fwd(const void *q, const void *k, const void *v, void *out
   DeviceInfo info;
   if ((st = require_sm100(&info)) != LA_OK) return st;
   cudaStream_t s = (cudaStream_t)stream;
-  if (use_tensor_cores(dtype, d_qk, d_v) && tc_parallel_enabled() && aligned16(q) &&
+  if (use_tensor_cores(dtype, d_qk, d_v) && aligned16(q) &&
       aligned16(k) && aligned16(v) && aligned32(out))
     return launch_parallel_tc(q, k, v, out, batch * heads, seq_len, eps, info, s);
   return launch_parallel_simt(q, k, v, out, batch * heads, seq_len, (int)d_qk, (int)d_v, dtype,
@@ -239,7 +310,7 @@ int la_based_chunked_plan(int64_t batch_heads, int64_t seq_len, int64_t d_qk, in
     DeviceInfo info;
     int st = require_sm100(&info);
     if (st != LA_OK) return st;
-    if (use_tensor_cores(dtype, d_qk, d_v) && tc_chunked_enabled() &&
+    if (use_tensor_cores(dtype, d_qk, d_v) &&
         lead_tokens(batch_heads, seq_len, info.sm_count) > 0) {
       // the forward's lead/main split: two pieces per head.  The workspace
       // also covers two equal segments, for callers that pass segments_out
@@ -273,19 +344,26 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
   int st = check_common(q, k, v, out, batch, heads, seq_len, d_qk, d_v, dtype);
   if (st != LA_OK) return st;
   if (chunk_size < 1 || segments < 0) return LA_ERR_INVALID_ARGUMENT;
-  if (flags & ~(LA_CHUNKED_NORMALIZE | LA_CHUNKED_REUSE_SEGMENTS)) return LA_ERR_INVALID_ARGUMENT;
+  if (flags & ~(LA_CHUNKED_NORMALIZE | LA_CHUNKED_REUSE_SEGMENTS | LA_CHUNKED_IDENTITY))
+    return LA_ERR_INVALID_ARGUMENT;
+  // the identity feature map has no normalised form (its denominator q.z can
+  // vanish); the reference defines only its numerator
+  if ((flags & LA_CHUNKED_IDENTITY) && (flags & LA_CHUNKED_NORMALIZE))
+    return LA_ERR_INVALID_ARGUMENT;
   const int64_t bh = batch * heads;
   if (bh == 0) return LA_OK;
+  ChunkedFwdPlan plan;
+  if ((st = plan_chunked_fwd(q, k, v, out, bh, seq_len, d_qk, d_v, dtype, segments, flags,
+                             &plan)) != LA_OK)
+    return st;
   DeviceInfo info;
   if ((st = require_sm100(&info)) != LA_OK) return st;
   cudaStream_t s = (cudaStream_t)stream;
-  const bool tc = use_tensor_cores(dtype, d_qk, d_v) && tc_chunked_enabled() && aligned16(q) &&
-                  aligned16(k) && aligned16(v) && aligned32(out);
-  if (!tc && !chunked_simt_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
+  const size_t per_head = (size_t)plan.features * (size_t)(d_v + 1);
   if (seq_len == 0) {
     // no tokens: the final state is the initial state (or zero)
     if (final_state) {
-      const size_t bytes = state_floats(bh, d_qk, d_v) * sizeof(float);
+      const size_t bytes = (size_t)bh * per_head * sizeof(float);
       cudaError_t e = init_state ? cudaMemcpyAsync(final_state, init_state, bytes,
                                                    cudaMemcpyDeviceToDevice, s)
                                  : cudaMemsetAsync(final_state, 0, bytes, s);
@@ -293,62 +371,41 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
     }
     return LA_OK;
   }
-  const int64_t lead = (segments == 0 && tc && !(flags & LA_CHUNKED_REUSE_SEGMENTS))
-                           ? lead_tokens(bh, seq_len, info.sm_count)
-                           : 0;
-  if (lead > 0) {
-    const size_t need = (state_floats(bh, d_qk, d_v) * sizeof(float) + 255) / 256 * 256;
-    if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u))
-      return LA_ERR_WORKSPACE;
+  if (plan.scratch > 0 &&
+      (!workspace || workspace_bytes < plan.scratch || ((uintptr_t)workspace & 255u)))
+    return LA_ERR_WORKSPACE;
+  const bool normalize = (flags & LA_CHUNKED_NORMALIZE) != 0;
+  if (plan.lead > 0) {
     float *lead_states = (float *)workspace;
-    st = launch_chunked_state_tc(k, v, lead_states, bh, seq_len, 1, 1, lead, info, s);
+    st = launch_chunked_state_tc(k, v, lead_states, bh, seq_len, 1, 1, plan.lead, info, s);
     if (st != LA_OK) return st;
     return launch_chunked_output_tc(q, k, v, out, init_state, final_state, lead_states, bh,
-                                    seq_len, eps, (flags & LA_CHUNKED_NORMALIZE) != 0, 1,
-                                    seq_len, lead, info, s);
+                                    seq_len, eps, normalize, 1, seq_len, plan.lead, info, s);
   }
-  const int g = segments == 0 ? auto_segments(bh, seq_len, info.sm_count)
-                              : effective_segments(seq_len, segments);
-  const int64_t seg_len = g > 1 ? segment_len(seq_len, g) : seq_len;
-  float *seg_states = nullptr;
-  if (g > 1) {
-    const size_t need = la_based_chunked_workspace_size(bh, seq_len, d_qk, d_v, g);
-    if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u))
-      return LA_ERR_WORKSPACE;
-    seg_states = (float *)workspace;
-  } else if (flags & LA_CHUNKED_REUSE_SEGMENTS) {
+  const int g = plan.g;
+  float *seg_states = g > 1 ? (float *)workspace : nullptr;
+  if (g == 1 && (flags & LA_CHUNKED_REUSE_SEGMENTS))
     return LA_ERR_INVALID_ARGUMENT;  // nothing to reuse without segments
-  }
-  const bool normalize = (flags & LA_CHUNKED_NORMALIZE) != 0;
-  // With two segments the state pass covers only the first: a long one runs
-  // as two half-length pieces so that it fills as many SMs as the output
-  // pass.  The two half states then need the running-sum launch; below
-  // kMinSplitStateTokens per segment that launch costs more than the halving
-  // saves (measured at B=4, H=16, N=2048: 0.044 ms unsplit vs 0.050 ms).
-  constexpr int64_t kMinSplitStateTokens = 32 * kSegmentTile;
-  const int ratio = (tc && g == 2 && !(flags & LA_CHUNKED_REUSE_SEGMENTS) &&
-                     seg_len % (2 * kSegmentTile) == 0 && seg_len >= kMinSplitStateTokens)
-                        ? 2
-                        : 1;
   if (g > 1 && !(flags & LA_CHUNKED_REUSE_SEGMENTS)) {
     // states of segments 0 .. g-2 (ratio slots each), then their prefix sums:
     // slot g - 1 seeds segment g
-    st = tc ? launch_chunked_state_tc(k, v, seg_states, bh, seq_len, g, (g - 1) * ratio,
-                                      seg_len / ratio, info, s)
-            : launch_chunked_state_simt(k, v, seg_states, bh, seq_len, (int)d_qk, (int)d_v,
-                                        dtype, g, seg_len, s);
+    st = plan.tc ? launch_chunked_state_tc(k, v, seg_states, bh, seq_len, g,
+                                           (g - 1) * plan.ratio, plan.seg_len / plan.ratio,
+                                           info, s)
+                 : launch_chunked_state_simt(k, v, seg_states, bh, seq_len, (int)d_qk, (int)d_v,
+                                             dtype, plan.identity, g, plan.seg_len, s);
     if (st != LA_OK) return st;
-    if ((g - 1) * ratio > 1 &&
-        (st = launch_prefix_segments(seg_states, nullptr, bh, g, g - 1, ratio,
-                                     (int64_t)feature_dim(d_qk) * (d_v + 1), s)) != LA_OK)
+    if ((g - 1) * plan.ratio > 1 &&
+        (st = launch_prefix_segments(seg_states, nullptr, bh, g, g - 1, plan.ratio,
+                                     (int64_t)per_head, s)) != LA_OK)
       return st;
   }
-  if (tc)
+  if (plan.tc)
     return launch_chunked_output_tc(q, k, v, out, init_state, final_state, seg_states, bh,
-                                    seq_len, eps, normalize, g, seg_len, 0, info, s);
+                                    seq_len, eps, normalize, g, plan.seg_len, 0, info, s);
   return launch_chunked_output_simt(q, k, v, out, init_state, final_state, seg_states, bh,
-                                    seq_len, (int)d_qk, (int)d_v, dtype, eps, normalize, g,
-                                    seg_len, s);
+                                    seq_len, (int)d_qk, (int)d_v, dtype, plan.identity, eps,
+                                    normalize, g, plan.seg_len, s);
 }
 
 int la_based_chunked_state(const void *k, const void *v, float *state_out, int64_t batch,
@@ -367,9 +424,9 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
   cudaStream_t s = (cudaStream_t)stream;
   const size_t state_bytes = state_floats(bh, d_qk, d_v) * sizeof(float);
   if (seq_len == 0) return cuda_status(cudaMemsetAsync(state_out, 0, state_bytes, s));
-  const bool tc = use_tensor_cores(dtype, d_qk, d_v) && tc_chunked_enabled() && aligned16(k) &&
+  const bool tc = use_tensor_cores(dtype, d_qk, d_v) && aligned16(k) &&
                   aligned16(v);
-  if (!tc && !chunked_simt_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
+  if (!tc && !chunked_simt_supported(feature_dim(d_qk), d_qk, d_v)) return LA_ERR_UNSUPPORTED;
   int g = segments == 0 ? auto_segments(bh, seq_len, info.sm_count)
                         : effective_segments(seq_len, segments);
   if (g > 1) {
@@ -380,7 +437,7 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
   const int64_t seg_len = g > 1 ? segment_len(seq_len, g) : seq_len;
   float *dst = g > 1 ? (float *)workspace : state_out;
   st = tc ? launch_chunked_state_tc(k, v, dst, bh, seq_len, g, g, seg_len, info, s)
-          : launch_chunked_state_simt(k, v, dst, bh, seq_len, (int)d_qk, (int)d_v, dtype, g,
+          : launch_chunked_state_simt(k, v, dst, bh, seq_len, (int)d_qk, (int)d_v, dtype, false, g,
                                       seg_len, s);
   if (st != LA_OK || g == 1) return st;
   // the total, and in the workspace the prefix slots a forward with
@@ -399,7 +456,7 @@ int la_sliding_window_fwd(const void *q, const void *k, const void *v, void *out
   DeviceInfo info;
   if ((st = require_sm100(&info)) != LA_OK) return st;
   cudaStream_t s = (cudaStream_t)stream;
-  if (dtype == LA_DTYPE_BFLOAT16 && head_dim == 64 && tc_sliding_enabled() &&
+  if (dtype == LA_DTYPE_BFLOAT16 && head_dim == 64 &&
       sliding_tc_supported(window) && aligned16(q) && aligned16(k) && aligned16(v) &&
       aligned32(out))
     return launch_sliding_tc(q, k, v, out, batch * heads, seq_len, window, info, s);

@@ -19,11 +19,10 @@
 //     behind; calls whose kernels overlap on the GPU (e.g. on two streams
 //     without ordering) race on it.  The forward writes every scratch byte it
 //     reads before reading it, so nothing needs clearing between calls.
-//   * the first call on a device resolves the array's device address (a
-//     cudaGetSymbolAddress with that device current); make that first call
-//     before any stream capture.
-#include <mutex>
-
+//   * the array's address belongs to the CUDA context, not to the device: the
+//     first call in each context resolves it (cudaGetSymbolAddress with that
+//     context current) and caches it by the context's unique id; make that
+//     first call before any stream capture.
 #include "common.cuh"
 
 namespace la {
@@ -34,28 +33,6 @@ constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
 // The scratch itself.  In host code this name is only a stand-in for the
 // symbol, not a device address: the address comes from cudaGetSymbolAddress.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-
-// Device address of g_noalloc_scratch on the current device (resolved once
-// per device), or null if it cannot be resolved.
-void *noalloc_scratch_ptr() {
-  static std::mutex mu;
-  static void *cache[64] = {};
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
-    cudaGetLastError();
-    return nullptr;
-  }
-  std::lock_guard<std::mutex> lock(mu);
-  if (!cache[dev]) {
-    void *ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess) {
-      cudaGetLastError();
-      return nullptr;
-    }
-    cache[dev] = ptr;
-  }
-  return cache[dev];
-}
 
 }  // namespace
 }  // namespace la
@@ -70,14 +47,16 @@ extern "C" int la_based_chunked_fwd_noalloc(const void *q, const void *k, const 
   if (flags & LA_CHUNKED_REUSE_SEGMENTS) return LA_ERR_INVALID_ARGUMENT;
   if (batch < 0 || heads < 0 || seq_len < 0 || d_qk < 1 || d_v < 1 || segments < 0)
     return LA_ERR_INVALID_ARGUMENT;
-  int g = segments;
-  const int st = la_based_chunked_plan(batch * heads, seq_len, d_qk, d_v, dtype, segments, &g,
-                                       nullptr);
-  if (st != LA_OK) return st;
-  const size_t need =
-      la::chunked_fwd_scratch_bytes(batch * heads, seq_len, d_qk, d_v, dtype, segments, flags);
-  if (need > la::kNoAllocScratchBytes) return LA_ERR_WORKSPACE;
-  void *scratch = la::noalloc_scratch_ptr();
+  // the scratch this request needs, decided by the same planner as the
+  // forward itself (pointer alignment included)
+  if (batch * heads > 0 && seq_len > 0) {
+    la::ChunkedFwdPlan plan;
+    const int st = la::plan_chunked_fwd(q, k, v, out, batch * heads, seq_len, d_qk, d_v, dtype,
+                                        segments, flags, &plan);
+    if (st != LA_OK) return st;
+    if (plan.scratch > la::kNoAllocScratchBytes) return LA_ERR_WORKSPACE;
+  }
+  void *scratch = la::context_symbol_address(&la::g_noalloc_scratch);
   if (!scratch) return LA_ERR_CUDA;
   return la_based_chunked_fwd(q, k, v, out, batch, heads, seq_len, d_qk, d_v, dtype, chunk_size,
                               eps, flags, init_state, final_state, scratch,

@@ -45,6 +45,15 @@ struct DeviceInfo {
 // Properties of the current device (cached per device ordinal).
 int current_device_info(DeviceInfo *info);
 
+// Device address of the __device__ variable whose host-side name is `symbol`
+// (a stand-in, not an address) in the CUDA context current on the calling
+// thread; null if it cannot be resolved.  A module variable's address
+// belongs to a context, not to a device (a host that makes its own driver
+// contexts on a device gets its own copy of every such variable), so the
+// address is resolved with cudaGetSymbolAddress once per context and cached
+// by the context's unique id.
+void *context_symbol_address(const void *symbol);
+
 inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? LA_OK : LA_ERR_CUDA; }
 
 // Counts one kernel launch (la_launch_count).
@@ -66,23 +75,36 @@ int launch_sliding_simt(const void *q, const void *k, const void *v, void *out, 
                         int64_t n, int d, int dtype, int64_t window, cudaStream_t s);
 
 // Chunked: G segments of `seg_len` tokens each (multiple of the chunk tile).
+// `identity` selects the identity feature map (phi(x) = x, F = d_qk) instead
+// of the Taylor map (F = 1 + d + d(d+1)/2).
 // state pass: per-(head, segment) state -> seg_states[bh][g][F][dv+1]
 int launch_chunked_state_simt(const void *k, const void *v, float *seg_states, int64_t bh,
-                              int64_t n, int dqk, int dv, int dtype, int segments,
+                              int64_t n, int dqk, int dv, int dtype, bool identity, int segments,
                               int64_t seg_len, cudaStream_t s);
 // output pass: prefix = init_state + sum of earlier segments' states.
 int launch_chunked_output_simt(const void *q, const void *k, const void *v, void *out,
                                const float *init_state, float *final_state,
                                const float *seg_states, int64_t bh, int64_t n, int dqk, int dv,
-                               int dtype, float eps, bool normalize, int segments,
+                               int dtype, bool identity, float eps, bool normalize, int segments,
                                int64_t seg_len, cudaStream_t s);
 
-// Largest (d_qk, d_v) the SIMT chunked kernels hold on chip.
-bool chunked_simt_supported(int64_t dqk, int64_t dv);
+// Whether the SIMT chunked kernels hold a (features, d_v + 1) state on chip.
+bool chunked_simt_supported(int64_t features, int64_t dqk, int64_t dv);
 
-// Workspace bytes la_based_chunked_fwd needs for these arguments (the exact
-// need; la_based_chunked_plan may report more).
-size_t chunked_fwd_scratch_bytes(int64_t bh, int64_t n, int64_t d_qk, int64_t d_v, int dtype,
-                                 int segments, unsigned flags);
+// How la_based_chunked_fwd runs a request: the one place that decides the
+// kernels, the segmentation and the scratch it needs.
+struct ChunkedFwdPlan {
+  bool identity = false;  // identity feature map (LA_CHUNKED_IDENTITY)
+  int64_t features = 0;   // F: rows of a head's state
+  bool tc = false;        // tcgen05 kernels (else the SIMT kernels)
+  int64_t lead = 0;       // > 0: lead/main split with a lead of this many tokens
+  int g = 1;              // equal segments per head
+  int64_t seg_len = 0;    // tokens per segment
+  int ratio = 1;          // state-pass pieces per segment
+  size_t scratch = 0;     // workspace bytes the run needs
+};
+int plan_chunked_fwd(const void *q, const void *k, const void *v, const void *out, int64_t bh,
+                     int64_t n, int64_t d_qk, int64_t d_v, int dtype, int segments,
+                     unsigned flags, ChunkedFwdPlan *plan);
 
 }  // namespace la

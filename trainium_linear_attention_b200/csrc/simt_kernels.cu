@@ -218,13 +218,18 @@ __device__ __forceinline__ void load_chunk_kv(const ChunkSmem &c, const T *kh, c
 }
 
 // S[f][e] += sum_{t in chunk} phi_k(k_t)[f] * vaug_t[e]; thread per feature row
-// (rows strided by blockDim), columns in register blocks of 32.
-__device__ void chunk_state_update(const ChunkSmem &c, int F, int dqk, int dv, int rows) {
+// (rows strided by blockDim), columns in register blocks of 32.  The identity
+// map has phi_k(k) = k (F = dqk); the Taylor map [1, k_a, k_a k_b (a <= b)].
+__device__ void chunk_state_update(const ChunkSmem &c, int F, int dqk, int dv, int rows,
+                                   bool identity) {
   const int ldk = dqk + 1, ldv = dv + 1;
   for (int f = threadIdx.x; f < F; f += blockDim.x) {
     // decode feature f -> (a, b) ; kind 0 const, 1 linear, 2 quadratic
     int kind, a = 0, b = 0;
-    if (f == 0) {
+    if (identity) {
+      kind = 1;
+      a = f;
+    } else if (f == 0) {
       kind = 0;
     } else if (f <= dqk) {
       kind = 1;
@@ -262,9 +267,9 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads)
 chunked_state_simt_kernel(const T *__restrict__ k, const T *__restrict__ v,
                           float *__restrict__ seg_states, int64_t n, int dqk, int dv,
-                          int segments, int64_t seg_len) {
+                          int identity, int segments, int64_t seg_len) {
   extern __shared__ float smem[];
-  const int F = (int)feature_dim(dqk);
+  const int F = identity ? dqk : (int)feature_dim(dqk);
   const int ldv = dv + 1;
   ChunkSmem c = carve(smem, F, dqk, dv);
   const int64_t bh = blockIdx.y;
@@ -278,7 +283,7 @@ chunked_state_simt_kernel(const T *__restrict__ k, const T *__restrict__ v,
     __syncthreads();
     load_chunk_kv(c, kh, vh, t0, t_end, dqk, dv);
     __syncthreads();
-    chunk_state_update(c, F, dqk, dv, (int)min64(kChunk, t_end - t0));
+    chunk_state_update(c, F, dqk, dv, (int)min64(kChunk, t_end - t0), identity != 0);
   }
   __syncthreads();
   float *dst = seg_states + (bh * segments + g) * (int64_t)F * ldv;
@@ -291,9 +296,10 @@ chunked_output_simt_kernel(const T *__restrict__ q, const T *__restrict__ k,
                            const T *__restrict__ v, T *__restrict__ out,
                            const float *__restrict__ init_state, float *__restrict__ final_state,
                            const float *__restrict__ seg_states, int64_t n, int dqk, int dv,
-                           float eps, int normalize, int segments, int64_t seg_len) {
+                           int identity, float eps, int normalize, int segments,
+                           int64_t seg_len) {
   extern __shared__ float smem[];
-  const int F = (int)feature_dim(dqk);
+  const int F = identity ? dqk : (int)feature_dim(dqk);
   const int ldv = dv + 1, ldq = dqk + 1;
   ChunkSmem c = carve(smem, F, dqk, dv);
   const int64_t bh = blockIdx.y;
@@ -333,7 +339,17 @@ chunked_output_simt_kernel(const T *__restrict__ q, const T *__restrict__ k,
     for (int i = 0; i < kMaxCols; ++i) acc[i] = 0.f;
     const float *qr = c.qs + row * ldq;
     // inter-chunk: phi_q(q_t) . S (state before this chunk's update)
-    {
+    if (identity) {
+      // phi_q(q) = q / sqrt(d)
+      for (int a = 0; a < dqk; ++a) {
+        const float phi = qr[a] * rsd;
+#pragma unroll
+        for (int i = 0; i < kMaxCols; ++i) {
+          int e = lane + i * kLanesPerRow;
+          if (e < ldv) acc[i] = fmaf(phi, c.S[a * ldv + e], acc[i]);
+        }
+      }
+    } else {
       int f = 0;
 #pragma unroll
       for (int i = 0; i < kMaxCols; ++i) {
@@ -360,14 +376,14 @@ chunked_output_simt_kernel(const T *__restrict__ q, const T *__restrict__ k,
         }
       }
     }
-    // intra-chunk: causal 1 + s + s^2/2 against this chunk's keys.  The loop
-    // bound is uniform over the CTA (the all-reduce is a full-warp shuffle);
-    // keys after the row are masked to weight 0.
+    // intra-chunk: causal 1 + s + s^2/2 (identity map: s) against this
+    // chunk's keys.  The loop bound is uniform over the CTA (the all-reduce is
+    // a full-warp shuffle); keys after the row are masked to weight 0.
     for (int j = 0; j < rows; ++j) {
       float s = 0.f;
       for (int a = lane; a < dqk; a += kLanesPerRow) s = fmaf(qr[a], c.ks[j * ldq + a], s);
       s = row_allreduce(s) * rsd;
-      float p = fmaf(s, fmaf(0.5f, s, 1.f), 1.f);
+      float p = identity ? s : fmaf(s, fmaf(0.5f, s, 1.f), 1.f);
       p = (j <= row) ? p : 0.f;
 #pragma unroll
       for (int i = 0; i < kMaxCols; ++i) {
@@ -391,7 +407,7 @@ chunked_output_simt_kernel(const T *__restrict__ q, const T *__restrict__ k,
       }
     }
     __syncthreads();  // every row read S before the update
-    chunk_state_update(c, F, dqk, dv, rows);
+    chunk_state_update(c, F, dqk, dv, rows, identity != 0);
   }
   if (final_state && g == segments - 1) {
     __syncthreads();
@@ -400,16 +416,15 @@ chunked_output_simt_kernel(const T *__restrict__ q, const T *__restrict__ k,
   }
 }
 
-size_t chunked_simt_smem(int dqk, int dv) {
-  const int64_t F = feature_dim(dqk);
+size_t chunked_simt_smem(int64_t F, int dqk, int dv) {
   return sizeof(float) * (size_t)(F * (dv + 1) + 2 * kChunk * (dqk + 1) + kChunk * (dv + 1));
 }
 
 }  // namespace
 
-bool chunked_simt_supported(int64_t dqk, int64_t dv) {
-  if (dqk < 1 || dqk > kMaxD || dv < 1 || dv > kMaxD) return false;
-  return chunked_simt_smem((int)dqk, (int)dv) <= 200 * 1024;
+bool chunked_simt_supported(int64_t features, int64_t dqk, int64_t dv) {
+  if (dqk < 1 || dqk > kMaxD || dv < 1 || dv > kMaxD || features < 1) return false;
+  return chunked_simt_smem(features, (int)dqk, (int)dv) <= 200 * 1024;
 }
 
 #define LA_DISPATCH_DTYPE(dtype, T, ...)                    \
@@ -462,17 +477,18 @@ int launch_sliding_simt(const void *q, const void *k, const void *v, void *out, 
 }
 
 int launch_chunked_state_simt(const void *k, const void *v, float *seg_states, int64_t bh,
-                              int64_t n, int dqk, int dv, int dtype, int segments,
+                              int64_t n, int dqk, int dv, int dtype, bool identity, int segments,
                               int64_t seg_len, cudaStream_t s) {
-  if (!chunked_simt_supported(dqk, dv)) return LA_ERR_UNSUPPORTED;
-  const size_t smem = chunked_simt_smem(dqk, dv);
+  const int64_t F = identity ? dqk : feature_dim(dqk);
+  if (!chunked_simt_supported(F, dqk, dv)) return LA_ERR_UNSUPPORTED;
+  const size_t smem = chunked_simt_smem(F, dqk, dv);
   dim3 grid((unsigned)segments, (unsigned)bh);
   LA_DISPATCH_DTYPE(dtype, T, {
     cudaError_t e = cudaFuncSetAttribute(chunked_state_simt_kernel<T>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return LA_ERR_CUDA;
     chunked_state_simt_kernel<T><<<grid, kThreads, smem, s>>>(
-        (const T *)k, (const T *)v, seg_states, n, dqk, dv, segments, seg_len);
+        (const T *)k, (const T *)v, seg_states, n, dqk, dv, identity ? 1 : 0, segments, seg_len);
   });
   return check_launch();
 }
@@ -480,10 +496,11 @@ int launch_chunked_state_simt(const void *k, const void *v, float *seg_states, i
 int launch_chunked_output_simt(const void *q, const void *k, const void *v, void *out,
                                const float *init_state, float *final_state,
                                const float *seg_states, int64_t bh, int64_t n, int dqk, int dv,
-                               int dtype, float eps, bool normalize, int segments,
+                               int dtype, bool identity, float eps, bool normalize, int segments,
                                int64_t seg_len, cudaStream_t s) {
-  if (!chunked_simt_supported(dqk, dv)) return LA_ERR_UNSUPPORTED;
-  const size_t smem = chunked_simt_smem(dqk, dv);
+  const int64_t F = identity ? dqk : feature_dim(dqk);
+  if (!chunked_simt_supported(F, dqk, dv)) return LA_ERR_UNSUPPORTED;
+  const size_t smem = chunked_simt_smem(F, dqk, dv);
   dim3 grid((unsigned)segments, (unsigned)bh);
   LA_DISPATCH_DTYPE(dtype, T, {
     cudaError_t e = cudaFuncSetAttribute(chunked_output_simt_kernel<T>,
@@ -491,7 +508,7 @@ int launch_chunked_output_simt(const void *q, const void *k, const void *v, void
     if (e != cudaSuccess) return LA_ERR_CUDA;
     chunked_output_simt_kernel<T><<<grid, kThreads, smem, s>>>(
         (const T *)q, (const T *)k, (const T *)v, (T *)out, init_state, final_state, seg_states,
-        n, dqk, dv, eps, normalize ? 1 : 0, segments, seg_len);
+        n, dqk, dv, identity ? 1 : 0, eps, normalize ? 1 : 0, segments, seg_len);
   });
   return check_launch();
 }

@@ -4,7 +4,7 @@
 //
 // Descriptor bit layouts follow the PTX ISA "tcgen05 shared memory
 // descriptor" and "instruction descriptor" tables (kind::f16, bf16 inputs,
-// fp32 accumulate).  No TMA load here uses .multicast::cluster.
+// fp32 accumulate).  All TMA loads here are plain per-CTA loads.
 #pragma once
 
 #include <cuda.h>

@@ -8,12 +8,7 @@
 
 namespace la {
 
-// Which tensor-core kernels this build contains.
-bool tc_chunked_enabled();
-bool tc_parallel_enabled();
-bool tc_sliding_enabled();
-
-// Device address of the library's error word on the current device (set by a
+// Device address of the library's error word in the current context (set by a
 // kernel whose bounded wait timed out); null if it cannot be resolved.
 int *device_error_word();
 

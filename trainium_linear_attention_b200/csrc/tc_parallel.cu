@@ -582,7 +582,6 @@ parallel_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
 
 }  // namespace
 
-bool tc_parallel_enabled() { return true; }
 
 int launch_parallel_tc(const void *q, const void *k, const void *v, void *out, int64_t bh,
                        int64_t n, float eps, const DeviceInfo &info, cudaStream_t s) {

@@ -11,8 +11,15 @@ benchmarks/chunked_attention_benchmark.py:
   on chip (never written to HBM) and d_v may differ from d_qk.
 * ``based_chunked(q, k, v, chunk_size=64, eps=1e-6)``: the normalised output
   (the reference's chunked kernel has no normaliser).
+* ``based_chunked_host(q, k, v, ...)``: the same on pinned host tensors, with
+  the copies overlapped with the kernels per group of heads.
 * ``based_chunked_state(k, v)``: total per-head state, the quantity the
   sequence-parallel mode exchanges between GPUs.
+* ``ref_identity_numerator(q, k, v)`` (:79-93): the identity-feature-map
+  numerator formula in plain PyTorch, for comparisons only, and
+  ``chunked_identity_numerator(q, k, v, chunk_size=64)``: the same quantity
+  from the chunked kernel with phi(x) = x (the recurrence of the reference's
+  old/identity_linear_attn_nki_CHUNKED.py:26-63).
 """
 
 from __future__ import annotations
@@ -63,6 +70,25 @@ def ref_based_numerator(q, k, v):
     return torch.matmul(masked, v.float()).to(q.dtype)
 
 
+def ref_identity_numerator(q, k, v):
+    """Dense identity-feature-map numerator: tril((q / sqrt(d)) k^T) v, in q.dtype."""
+    d = q.shape[-1]
+    scale = 1.0 / math.sqrt(d)
+    scores = torch.matmul(q * scale, k.transpose(-2, -1))
+    t = q.shape[-2]
+    mask = torch.tril(torch.ones(t, t, device=q.device, dtype=q.dtype))
+    return torch.matmul(scores * mask, v)
+
+
+def chunked_identity_numerator(q, k, v, chunk_size=64):
+    """Chunked identity-feature-map linear attention (numerator) on the sm_100a kernels.
+
+    q, k: (b, h, t, d_qk); v: (b, h, t, d_v).  Returns (b, h, t, d_v) in q.dtype.
+    """
+    return ops.based_chunked(q, k, v, chunk_size=chunk_size, normalize=False,
+                             feature_map="identity")
+
+
 def chunked_nki_numerator(q, k, v, chunk_size=64):
     """Numerator-only chunked BASED on the sm_100a kernel.
 
@@ -74,6 +100,15 @@ def chunked_nki_numerator(q, k, v, chunk_size=64):
 def based_chunked(q, k, v, chunk_size=64, eps=1e-6):
     """Normalised chunked BASED attention on the sm_100a kernel."""
     return ops.based_chunked(q, k, v, chunk_size=chunk_size, eps=eps, normalize=True)
+
+
+def based_chunked_host(q, k, v, chunk_size=64, eps=1e-6, head_groups=8, out=None):
+    """Normalised chunked BASED attention on pinned host tensors, with the
+    host<->device copies of head groups overlapped with the kernels (see
+    ``ops.based_chunked_host``); the result is in ``out`` once the current
+    CUDA stream has reached the end of the call."""
+    return ops.based_chunked_host(q, k, v, chunk_size=chunk_size, eps=eps, normalize=True,
+                                  head_groups=head_groups, out=out)
 
 
 def based_chunked_state(k, v):

@@ -93,11 +93,12 @@ def _workspace(nbytes: int, device) -> torch.Tensor | None:
 def based_chunked(q, k, v, chunk_size: int = 64, eps: float = 1e-6, normalize: bool = True,
                   init_state: torch.Tensor | None = None, return_state: bool = False,
                   segments: int = 0, workspace: torch.Tensor | None = None,
-                  reuse_segments: bool = False):
-    """Chunked recurrent BASED attention.
+                  reuse_segments: bool = False, feature_map: str = "taylor"):
+    """Chunked recurrent linear attention (BASED Taylor features by default).
 
     ``init_state`` / the returned final state are fp32 ``(b*h, F, d_v + 1)``
     in the key-side feature basis documented in ``include/la_attention.h``.
+    ``feature_map="identity"`` uses phi(x) = x (F = d_qk, numerator only).
     """
     code = _check_qkv(q, k, v)
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
@@ -105,7 +106,12 @@ def based_chunked(q, k, v, chunk_size: int = 64, eps: float = 1e-6, normalize: b
     dv = v.shape[-1]
     if chunk_size < 1:
         raise ValueError("chunk_size must be >= 1")
-    F = feature_dim(d)
+    if feature_map not in ("taylor", "identity"):
+        raise ValueError(f"feature_map must be 'taylor' or 'identity', got {feature_map!r}")
+    identity = feature_map == "identity"
+    if identity and normalize:
+        raise ValueError("the identity feature map is numerator-only (normalize=False)")
+    F = d if identity else feature_dim(d)
     if init_state is not None:
         if (init_state.dtype != torch.float32 or init_state.device != q.device
                 or tuple(init_state.shape) != (b * h, F, dv + 1)):
@@ -119,8 +125,9 @@ def based_chunked(q, k, v, chunk_size: int = 64, eps: float = 1e-6, normalize: b
             workspace = _workspace(ws_bytes, q.device)
         elif workspace.numel() * workspace.element_size() < ws_bytes:
             raise ValueError(f"workspace too small: need {ws_bytes} bytes")
-        flags = (N.LA_CHUNKED_NORMALIZE if normalize else 0) | (
-            N.LA_CHUNKED_REUSE_SEGMENTS if reuse_segments else 0)
+        flags = ((N.LA_CHUNKED_NORMALIZE if normalize else 0)
+                 | (N.LA_CHUNKED_REUSE_SEGMENTS if reuse_segments else 0)
+                 | (N.LA_CHUNKED_IDENTITY if identity else 0))
         st = N.lib().la_based_chunked_fwd(
             _ptr(q), _ptr(k), _ptr(v), _ptr(out), b, h, t, d, dv, code, int(chunk_size),
             float(eps), flags, _ptr(init_state), _ptr(final), _ptr(workspace),
@@ -163,4 +170,82 @@ def sliding_window(q, k, v, window_size: int = 64) -> torch.Tensor:
         st = N.lib().la_sliding_window_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(out), b, h, t, d, code,
                                            int(window_size), _stream_ptr(q.device))
     N.check(st, "la_sliding_window_fwd")
+    return out
+
+
+_copy_streams: dict = {}
+
+
+def _side_streams(device):
+    """Two streams per device (host->device, device->host), created once."""
+    key = torch.device(device).index
+    if key not in _copy_streams:
+        _copy_streams[key] = (torch.cuda.Stream(device), torch.cuda.Stream(device))
+    return _copy_streams[key]
+
+
+def based_chunked_host(q, k, v, chunk_size: int = 64, eps: float = 1e-6, normalize: bool = True,
+                       head_groups: int = 8, device=None, out: torch.Tensor | None = None):
+    """Chunked BASED attention on host-resident ``(b, h, t, d)`` tensors.
+
+    The heads are processed in ``head_groups`` groups so that the host-to-
+    device copy of one group, the kernels of the previous group and the
+    device-to-host copy of the group before run at the same time (PCIe is
+    full duplex): the copies run on two side streams of ``device`` and are
+    joined back into its current stream before the call returns.  Inputs
+    should be pinned (``pin_memory()``) for the copies to overlap.  The
+    result is written into ``out`` (a pinned host tensor is allocated if it
+    is None) and is complete once the current stream has reached this point
+    (e.g. after ``torch.cuda.current_stream().synchronize()``).
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.device.type != "cpu":
+            raise ValueError(f"{name} must be a host tensor for based_chunked_host")
+    if q.shape != k.shape or v.shape[:3] != q.shape[:3]:
+        raise ValueError("q, k, v shapes do not match")
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    b, h, t, d = q.shape
+    dv = v.shape[-1]
+    bh = b * h
+    if out is None:
+        out = torch.empty((b, h, t, dv), dtype=q.dtype).pin_memory()
+    elif out.shape != (b, h, t, dv) or out.dtype != q.dtype or out.device.type != "cpu":
+        raise ValueError(f"out must be a host {q.dtype} tensor of shape {(b, h, t, dv)}")
+    qf, kf, vf = (x.reshape(bh, t, x.shape[-1]) for x in (q, k, v))
+    of = out.view(bh, t, dv)
+    groups = max(1, min(int(head_groups), bh))
+    step = -(-bh // groups)
+    with torch.cuda.device(device):
+        compute = torch.cuda.current_stream(device)
+        h2d, d2h = _side_streams(device)
+        qd = torch.empty((bh, t, d), dtype=q.dtype, device=device)
+        kd = torch.empty_like(qd)
+        vd = torch.empty((bh, t, dv), dtype=v.dtype, device=device)
+        start = torch.cuda.Event()
+        start.record(compute)  # the buffers are free once the compute stream is here
+        h2d.wait_event(start)
+        d2h.wait_event(start)
+        for lo in range(0, bh, step):
+            hi = min(bh, lo + step)
+            with torch.cuda.stream(h2d):
+                for dst, src in ((qd, qf), (kd, kf), (vd, vf)):
+                    dst[lo:hi].copy_(src[lo:hi], non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(h2d)
+            compute.wait_event(ready)
+            y = based_chunked(qd[lo:hi].unsqueeze(0), kd[lo:hi].unsqueeze(0),
+                              vd[lo:hi].unsqueeze(0), chunk_size=chunk_size, eps=eps,
+                              normalize=normalize)
+            done = torch.cuda.Event()
+            done.record(compute)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                of[lo:hi].copy_(y[0], non_blocking=True)
+            y.record_stream(d2h)  # its memory is not reused before this copy ends
+        finished = torch.cuda.Event()
+        finished.record(d2h)
+        compute.wait_event(finished)
+        h2d_done = torch.cuda.Event()
+        h2d_done.record(h2d)
+        compute.wait_event(h2d_done)
     return out
