@@ -182,6 +182,27 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out,
                            void *stream);
 
 /* ---------------------------------------------------------------------------
+ * The full BASED layer: causal BASED linear attention plus sliding-window
+ * softmax attention over the same q, k, v,
+ *     out = based(q, k, v, eps) + sliding_window(q, k, v, window),
+ * the composition the reference states at kernels/nki_attention_sliding.py:
+ * 4-5 (and whose two halves its module wrapper benchmarks/
+ * based_attention_benchmark.py:24-69 would call separately), computed in one
+ * pass over q, k and v: each chunk's keys and values serve the chunked
+ * recurrence and, kept on chip, the windows of the next two chunks
+ * (window <= 129).  The sliding half uses the same scale 1/sqrt(d_qk), the
+ * window [i - W + 1, i] and fp32 softmax accumulation.  segments and the
+ * workspace work as for la_based_chunked_fwd (la_based_chunked_plan sizes
+ * it); the window of a segment's first tokens reads the keys before it.
+ * The reference has no kernel for the fused layer.
+ * ------------------------------------------------------------------------- */
+int la_based_layer_fwd(const void *q, const void *k, const void *v, void *out,
+                       int64_t batch, int64_t heads, int64_t seq_len,
+                       int64_t d_qk, int64_t d_v, int dtype, int64_t window,
+                       float eps, void *workspace, size_t workspace_bytes,
+                       int segments, void *stream);
+
+/* ---------------------------------------------------------------------------
  * Sliding-window causal softmax attention, window [i-W+1, i].
  *
  * Replaces nki_sliding_window_attn (benchmarks/sliding_attention_benchmark.py:

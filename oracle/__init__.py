@@ -24,6 +24,7 @@ from .based_oracle import (  # noqa: F401
     sliding_window_attn,
     identity_numerator,
     identity_chunked,
+    based_layer,
     feature_dim,
     rel_l2,
 )

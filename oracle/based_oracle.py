@@ -319,3 +319,14 @@ def sliding_window_attn(q, k, v, window: int = 64, dtype=np.float64):
     p = np.exp(s - m)
     p = p / p.sum(axis=-1, keepdims=True)
     return np.einsum("...tw,...tew->...te", p, vw)
+
+
+def based_layer(q, k, v, window: int = 64, eps: float = 1e-6, dtype=np.float64):
+    """The full BASED layer: BASED attention + sliding-window softmax attention.
+
+    The composition stated at kernels/nki_attention_sliding.py:4-5, each half
+    as restated above (kernels/pytorch_attention.py:27-42 and
+    benchmarks/sliding_attention_benchmark.py:32-56).
+    """
+    return (based_attn_reduced(q, k, v, eps=eps, dtype=dtype)
+            + sliding_window_attn(q, k, v, window, dtype=dtype))

@@ -84,6 +84,16 @@ def main(ref_root: str) -> None:
     out["dense.out"] = cab.ref_based_attn(q, k, v, eps=1e-6).numpy()
     out["dense.num"] = cab.ref_based_numerator(q, k, v).numpy()
 
+    # d_qk = 64: the reference chunked benchmark's default shape (B=1, H=2,
+    # S=256, D=64, N(0,1) inputs; benchmarks/chunked_attention_benchmark.py:13-16)
+    gen = torch.Generator().manual_seed(50)
+    q = _randn(gen, (1, 2, 256, 64), 1.0)
+    k = _randn(gen, (1, 2, 256, 64), 1.0)
+    v = _randn(gen, (1, 2, 256, 64), 1.0)
+    out["dense64.q"], out["dense64.k"], out["dense64.v"] = q.numpy(), k.numpy(), v.numpy()
+    out["dense64.out"] = cab.ref_based_attn(q, k, v, eps=1e-6).numpy()
+    out["dense64.num"] = cab.ref_based_numerator(q, k, v).numpy()
+
     # identity feature map, numerator only (fp32 inputs)
     def identity_case(name, shape_qk, dv, seed):
         gen = torch.Generator().manual_seed(seed)
@@ -106,6 +116,23 @@ def main(ref_root: str) -> None:
         out[f"{name}.q"], out[f"{name}.k"], out[f"{name}.v"] = q.numpy(), k.numpy(), v.numpy()
         out[f"{name}.window"] = np.array(window)
         out[f"{name}.out"] = sab.ref_sliding_window_attn(q, k, v, window_size=window).numpy()
+
+    # the full BASED layer: the composition stated at
+    # kernels/nki_attention_sliding.py:4-5 of the two reference functions
+    def layer_case(name, shape_qk, dv, window, seed, scale):
+        gen = torch.Generator().manual_seed(seed)
+        b, h, t, d = shape_qk
+        q = _randn(gen, (b, h, t, d), scale)
+        k = _randn(gen, (b, h, t, d), scale)
+        v = _randn(gen, (b, h, t, dv), scale)
+        out[f"{name}.q"], out[f"{name}.k"], out[f"{name}.v"] = q.numpy(), k.numpy(), v.numpy()
+        out[f"{name}.window"] = np.array(window)
+        out[f"{name}.out"] = (ref_reduced(q, k, v, eps=1e-6)
+                              + sab.ref_sliding_window_attn(q, k, v, window_size=window)).numpy()
+
+    layer_case("layer_w64", (1, 2, 300, 16), 64, 64, seed=60, scale=0.5)
+    layer_case("layer_w129", (1, 1, 400, 16), 32, 129, seed=61, scale=0.5)
+    layer_case("layer_d32_w7", (2, 2, 77, 32), 32, 7, seed=62, scale=1.0)
 
     slide_case("slide_w64", (1, 1, 256, 64), 64, seed=30)
     slide_case("slide_w16_odd", (2, 2, 77, 32), 16, seed=31)

@@ -144,6 +144,44 @@ def test_chunked_other_widths(dqk, dv, dtype):
     assert O.rel_l2(np64(y), want) <= tol
 
 
+def test_chunked_d64_fp32_golden(golden):
+    """d_qk = 64 (F = 2145: the state is split over a thread-block cluster)
+    at the reference chunked benchmark's default shape, fp32, against the
+    reference's own dense Taylor-feature outputs."""
+    q, k, v = (torch.from_numpy(golden[f"dense64.{n}"]).to(DEV) for n in "qkv")
+    y = T.based_chunked(q, k, v)
+    assert O.rel_l2(y.cpu().numpy(), golden["dense64.out"]) <= TOL_FP32
+    num = T.chunked_nki_numerator(q, k, v)
+    assert O.rel_l2(num.cpu().numpy(), golden["dense64.num"]) <= TOL_FP32
+
+
+@pytest.mark.parametrize("t,dv", [(1, 64), (63, 64), (64, 64), (65, 32), (300, 64), (1000, 64)])
+def test_chunked_d64_bf16(t, dv):
+    q, k, v = inputs((1, 3, t, 64), dv, seed=640 + t)
+    y = T.based_chunked(*cuda(q, k, v))
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+
+
+def test_chunked_d64_segments_and_state():
+    """Segments (the state pass splits the features over independent CTAs),
+    the final state against the oracle's, and a split sequence seeded with
+    the first part's state."""
+    q, k, v = cuda(*inputs((1, 2, 2000, 64), 64, seed=641, dtype=torch.float32))
+    y1, s1 = ops.based_chunked(q, k, v, segments=1, return_state=True)
+    y3, s3 = ops.based_chunked(q, k, v, segments=3, return_state=True)
+    want, s_want = O.based_chunked(np64(q), np64(k), np64(v), return_state=True)
+    assert O.rel_l2(np64(y1), want) <= TOL_FP32
+    assert O.rel_l2(np64(y3), want) <= TOL_FP32
+    assert O.rel_l2(s1.double().cpu().numpy(), s_want.reshape(2, 2145, 65)) <= TOL_FP32
+    assert O.rel_l2(s3.double().cpu().numpy(), s_want.reshape(2, 2145, 65)) <= TOL_FP32
+    st = ops.based_chunked_state(k, v, segments=3)
+    assert O.rel_l2(st.double().cpu().numpy(), s_want.reshape(2, 2145, 65)) <= TOL_FP32
+    a, sa = ops.based_chunked(q[:, :, :700], k[:, :, :700], v[:, :, :700], return_state=True)
+    b = ops.based_chunked(q[:, :, 700:], k[:, :, 700:], v[:, :, 700:], init_state=sa)
+    assert O.rel_l2(np64(torch.cat([a, b], 2)), want) <= TOL_FP32
+
+
 def test_chunked_unaligned_pointers():
     """bf16 tensors whose data is not 16-byte aligned (TMA cannot address
     them) run on the CUDA-core kernels with the same result."""
@@ -378,6 +416,42 @@ def test_deterministic_segment_states_lightly_loaded():
         assert O.rel_l2(np64(y), want) <= 5e-3
 
 
+# --------------------------------------------------------- full BASED layer ---
+
+@pytest.mark.parametrize("case", ["layer_w64", "layer_w129", "layer_d32_w7"])
+def test_layer_fp32_golden(golden, case):
+    """based_layer (BASED + sliding window in one pass) against the reference's
+    own two functions summed."""
+    q, k, v = (torch.from_numpy(golden[f"{case}.{n}"]).to(DEV) for n in "qkv")
+    y = T.based_layer(q, k, v, window_size=int(golden[f"{case}.window"]))
+    assert O.rel_l2(y.cpu().numpy(), golden[f"{case}.out"]) <= TOL_FP32
+
+
+@pytest.mark.parametrize("t,w,segments", [(1, 64, 0), (65, 64, 0), (1000, 64, 0), (2048, 64, 0),
+                                          (3000, 129, 3), (700, 1, 0), (300, 129, 0),
+                                          (129, 500, 0)])
+def test_layer_bf16(t, w, segments):
+    q, k, v = inputs((2, 4, t, 16), 64, seed=700 + t + w)
+    if w > 129:
+        with pytest.raises(RuntimeError):
+            T.based_layer(*cuda(q, k, v), window_size=w)
+        return
+    y = ops.based_layer(*cuda(q, k, v), window_size=w, segments=segments)
+    want = O.based_layer(np64(q), np64(k), np64(v), w)
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+
+
+def test_layer_segments_agree():
+    """Segments seed the state from the earlier segments and read the window
+    keys before their first token from memory: same result as one segment."""
+    q, k, v = cuda(*inputs((1, 3, 2500, 16), 64, seed=710, dtype=torch.float32))
+    y1 = ops.based_layer(q, k, v, window_size=100, segments=1)
+    y4 = ops.based_layer(q, k, v, window_size=100, segments=4)
+    assert O.rel_l2(np64(y4), np64(y1)) <= 1e-5
+    want = O.based_layer(np64(q), np64(k), np64(v), 100)
+    assert O.rel_l2(np64(y4), want) <= TOL_FP32
+
+
 # ----------------------------------------------------------------- sliding ---
 
 @pytest.mark.parametrize("case", ["slide_w64", "slide_w16_odd", "slide_w1", "slide_wbig",
@@ -435,6 +509,9 @@ def test_solution_dispatch_and_errors():
     with pytest.raises(RuntimeError):  # d_qk beyond the kernels: raises, no fallback
         qq = torch.zeros(1, 1, 8, 256, device=DEV, dtype=torch.bfloat16)
         T.solution_nki(qq, qq, qq)
+    with pytest.raises(RuntimeError):  # a state too wide even for a cluster
+        qq = torch.zeros(1, 1, 8, 128, device=DEV, dtype=torch.bfloat16)
+        T.based_chunked(qq, qq, qq)
 
 
 def test_solution_short_sequence_takes_parallel_kernel():
@@ -489,3 +566,22 @@ def test_identity_state_roundtrip():
     assert O.rel_l2(np64(torch.cat([a, b], 2)), want) <= TOL_FP32
     with pytest.raises(ValueError):
         ops.based_chunked(q, k, v, feature_map="identity")  # normalised identity: rejected
+
+
+# ------------------------------------------------------------ traced dispatch ---
+
+@pytest.mark.parametrize("t", [256, 3000])
+def test_traced_solution_matches_eager(t):
+    """trace_solution captures solution() for one shape in a CUDA graph (the
+    parallel kernel at N = 256, the chunked kernel with its segment-state pass
+    at N = 3000); replays on new inputs equal the eager call bit for bit."""
+    from trainium_linear_attention_b200.kernels.pytorch_attention import solution_kind
+    q, k, v = cuda(*inputs((1, 4, t, 16), 64, seed=t + 1))
+    traced = T.trace_solution(q, k, v)
+    assert traced.kind == solution_kind(q, k, v) == ("parallel" if t <= 384 else "chunked")
+    for seed in (1, 2):
+        q2, k2, v2 = cuda(*inputs((1, 4, t, 16), 64, seed=t + 10 * seed))
+        y = traced(q2, k2, v2).clone()
+        assert torch.equal(y, T.solution(q2, k2, v2))
+    with pytest.raises(ValueError):
+        traced(q[:, :, :10], k[:, :, :10], v[:, :, :10])

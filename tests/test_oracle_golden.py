@@ -128,3 +128,23 @@ def test_identity_chunked_state_is_additive():
     b = O.identity_chunked(q[..., 128:, :], k[..., 128:, :], v[..., 128:, :], init_state=s)
     assert s.shape == (1, 2, 16, 25)
     assert O.rel_l2(np.concatenate([a, b], -2), whole) < 1e-12
+
+
+def test_d64_refs_match_reference(golden):
+    """d_qk = 64 (F = 2145), the reference chunked benchmark's default shape:
+    the oracle's chunked recurrence and reduced form against its dense
+    Taylor-feature references (benchmarks/chunked_attention_benchmark.py:55-76)."""
+    q, k, v = (golden[f"dense64.{n}"].astype(np.float64) for n in "qkv")
+    assert O.feature_dim(64) == 2145
+    assert O.rel_l2(O.based_chunked(q, k, v), golden["dense64.out"]) < 1e-5
+    assert O.rel_l2(O.based_chunked(q, k, v, normalize=False), golden["dense64.num"]) < 1e-5
+    assert O.rel_l2(O.based_attn_reduced(q, k, v), golden["dense64.out"]) < 1e-5
+
+
+@pytest.mark.parametrize("case", ["layer_w64", "layer_w129", "layer_d32_w7"])
+def test_layer_matches_reference_composition(golden, case):
+    """oracle.based_layer vs the reference's ref_based_attn +
+    ref_sliding_window_attn on the same inputs (kernels/nki_attention_sliding.py:4-5)."""
+    q, k, v = (golden[f"{case}.{n}"] for n in "qkv")
+    y = O.based_layer(q, k, v, int(golden[f"{case}.window"]))
+    assert O.rel_l2(y, golden[f"{case}.out"]) < 1e-6

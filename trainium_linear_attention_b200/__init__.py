@@ -6,16 +6,19 @@ of the reference's ``kernels/pytorch_attention.py`` in
 :mod:`trainium_linear_attention_b200.kernels`.
 """
 
-from .kernels.pytorch_attention import ref_based_attn, solution_nki, solution  # noqa: F401
+from .kernels.pytorch_attention import (  # noqa: F401
+    ref_based_attn, solution_nki, solution, trace_solution, TracedSolution)
 from .kernels.chunked_attention import (  # noqa: F401
     chunked_nki_numerator, based_chunked, based_chunked_state, taylor_feature_map,
     chunked_identity_numerator, ref_identity_numerator, based_chunked_host)
 from .kernels.sliding_attention import nki_sliding_window_attn, ref_sliding_window_attn  # noqa: F401
+from .kernels.based_layer import based_layer, ref_based_layer  # noqa: F401
 from ._native import LaError  # noqa: F401
 
 __all__ = [
-    "ref_based_attn", "solution_nki", "solution", "chunked_nki_numerator", "based_chunked",
+    "ref_based_attn", "solution_nki", "solution", "trace_solution", "TracedSolution",
+    "chunked_nki_numerator", "based_chunked",
     "based_chunked_state", "taylor_feature_map", "chunked_identity_numerator",
     "ref_identity_numerator", "based_chunked_host", "nki_sliding_window_attn",
-    "ref_sliding_window_attn", "LaError",
+    "ref_sliding_window_attn", "based_layer", "ref_based_layer", "LaError",
 ]

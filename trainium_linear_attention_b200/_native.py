@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "la_based_chunked_fwd_noalloc",
     "la_based_chunked_state",
     "la_sliding_window_fwd",
+    "la_based_layer_fwd",
 )
 
 _lock = threading.Lock()
@@ -92,6 +93,9 @@ def _declare(lib) -> None:
     lib.la_based_chunked_state.restype = _int
     lib.la_sliding_window_fwd.argtypes = [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _i64, _p]
     lib.la_sliding_window_fwd.restype = _int
+    lib.la_based_layer_fwd.argtypes = [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _i64,
+                                       _f, _p, _sz, _int, _p]
+    lib.la_based_layer_fwd.restype = _int
 
 
 def lib():

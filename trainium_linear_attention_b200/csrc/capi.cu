@@ -79,6 +79,34 @@ void *context_symbol_address(const void *symbol) {
 
 int *device_error_word() { return (int *)context_symbol_address(&la_device_error_word); }
 
+int allow_dynamic_smem(const void *func, int bytes) {
+  struct Entry {
+    unsigned long long ctx;
+    const void *func;
+    int bytes;
+  };
+  static std::mutex mu;
+  static Entry cache[128];
+  static int used = 0;
+  unsigned long long ctx = 0;
+  const bool known = current_context_id(&ctx);
+  if (known) {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i)
+      if (cache[i].ctx == ctx && cache[i].func == func && cache[i].bytes >= bytes) return LA_OK;
+  }
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return LA_ERR_CUDA;
+  }
+  if (known) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (used < 128) cache[used++] = Entry{ctx, func, bytes};
+  }
+  return LA_OK;
+}
+
 namespace {
 std::atomic<uint64_t> g_launches{0};
 }  // namespace
@@ -213,7 +241,10 @@ int plan_chunked_fwd(const void *q, const void *k, const void *v, const void *ou
   p.features = p.identity ? d_qk : feature_dim(d_qk);
   p.tc = !p.identity && use_tensor_cores(dtype, d_qk, d_v) && aligned16(q) && aligned16(k) &&
          aligned16(v) && aligned32(out);
-  if (!p.tc && !chunked_simt_supported(p.features, d_qk, d_v)) return LA_ERR_UNSUPPORTED;
+  if (!p.tc && !chunked_simt_supported(p.features, d_qk, d_v)) {
+    if (p.identity || !cluster_chunked_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
+    p.cluster = true;
+  }
   const bool reuse = (flags & LA_CHUNKED_REUSE_SEGMENTS) != 0;
   const size_t head_state_bytes = (size_t)p.features * (size_t)(d_v + 1) * sizeof(float);
   p.lead = (segments == 0 && p.tc && !reuse && n > 0) ? lead_tokens(bh, n, info.sm_count) : 0;
@@ -224,7 +255,10 @@ int plan_chunked_fwd(const void *q, const void *k, const void *v, const void *ou
     *plan = p;
     return LA_OK;
   }
-  p.g = segments == 0 ? auto_segments(bh, n, info.sm_count) : effective_segments(n, segments);
+  // one wave of CTAs: a cluster run places cluster_chunked_ctas_per_segment()
+  // CTAs on every (head, segment)
+  const int wave = p.cluster ? info.sm_count / cluster_chunked_ctas_per_segment() : info.sm_count;
+  p.g = segments == 0 ? auto_segments(bh, n, wave) : effective_segments(n, segments);
   p.seg_len = p.g > 1 ? segment_len(n, p.g) : n;
   // With two segments the state pass covers only the first: a long one runs
   // as two half-length pieces so that it fills as many SMs as the output
@@ -316,6 +350,10 @@ int la_based_chunked_plan(int64_t batch_heads, int64_t seq_len, int64_t d_qk, in
       // also covers two equal segments, for callers that pass segments_out
       // on explicitly (the split itself needs one state per head).
       g = 2;
+    } else if (!use_tensor_cores(dtype, d_qk, d_v) &&
+               !chunked_simt_supported(feature_dim(d_qk), d_qk, d_v) &&
+               cluster_chunked_supported(d_qk, d_v)) {
+      g = auto_segments(batch_heads, seq_len, info.sm_count / cluster_chunked_ctas_per_segment());
     } else {
       g = auto_segments(batch_heads, seq_len, info.sm_count);
     }
@@ -389,11 +427,15 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
   if (g > 1 && !(flags & LA_CHUNKED_REUSE_SEGMENTS)) {
     // states of segments 0 .. g-2 (ratio slots each), then their prefix sums:
     // slot g - 1 seeds segment g
-    st = plan.tc ? launch_chunked_state_tc(k, v, seg_states, bh, seq_len, g,
-                                           (g - 1) * plan.ratio, plan.seg_len / plan.ratio,
-                                           info, s)
-                 : launch_chunked_state_simt(k, v, seg_states, bh, seq_len, (int)d_qk, (int)d_v,
-                                             dtype, plan.identity, g, plan.seg_len, s);
+    st = plan.tc        ? launch_chunked_state_tc(k, v, seg_states, bh, seq_len, g,
+                                                  (g - 1) * plan.ratio,
+                                                  plan.seg_len / plan.ratio, info, s)
+         : plan.cluster ? launch_chunked_state_cluster(k, v, seg_states, bh, seq_len, (int)d_qk,
+                                                       (int)d_v, dtype, g, g - 1, plan.seg_len,
+                                                       s)
+                        : launch_chunked_state_simt(k, v, seg_states, bh, seq_len, (int)d_qk,
+                                                    (int)d_v, dtype, plan.identity, g,
+                                                    plan.seg_len, s);
     if (st != LA_OK) return st;
     if ((g - 1) * plan.ratio > 1 &&
         (st = launch_prefix_segments(seg_states, nullptr, bh, g, g - 1, plan.ratio,
@@ -403,9 +445,48 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
   if (plan.tc)
     return launch_chunked_output_tc(q, k, v, out, init_state, final_state, seg_states, bh,
                                     seq_len, eps, normalize, g, plan.seg_len, 0, info, s);
+  if (plan.cluster)
+    return launch_chunked_output_cluster(q, k, v, out, init_state, final_state, seg_states, bh,
+                                         seq_len, (int)d_qk, (int)d_v, dtype, eps, normalize, g,
+                                         plan.seg_len, s);
   return launch_chunked_output_simt(q, k, v, out, init_state, final_state, seg_states, bh,
                                     seq_len, (int)d_qk, (int)d_v, dtype, plan.identity, eps,
-                                    normalize, g, plan.seg_len, s);
+                                    normalize, g, plan.seg_len, 0, s);
+}
+
+int la_based_layer_fwd(const void *q, const void *k, const void *v, void *out, int64_t batch,
+                       int64_t heads, int64_t seq_len, int64_t d_qk, int64_t d_v, int dtype,
+                       int64_t window, float eps, void *workspace, size_t workspace_bytes,
+                       int segments, void *stream) {
+  int st = check_common(q, k, v, out, batch, heads, seq_len, d_qk, d_v, dtype);
+  if (st != LA_OK) return st;
+  if (window < 1 || segments < 0) return LA_ERR_INVALID_ARGUMENT;
+  const int64_t bh = batch * heads;
+  if (bh == 0 || seq_len == 0) return LA_OK;
+  if (!layer_simt_supported(d_qk, d_v, window)) return LA_ERR_UNSUPPORTED;
+  DeviceInfo info;
+  if ((st = require_sm100(&info)) != LA_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int g = segments == 0 ? auto_segments(bh, seq_len, info.sm_count)
+                              : effective_segments(seq_len, segments);
+  const int64_t seg_len = g > 1 ? segment_len(seq_len, g) : seq_len;
+  const int64_t per_head = feature_dim(d_qk) * (d_v + 1);
+  float *seg_states = nullptr;
+  if (g > 1) {
+    const size_t need = ((size_t)bh * g * per_head * sizeof(float) + 255) / 256 * 256;
+    if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u))
+      return LA_ERR_WORKSPACE;
+    seg_states = (float *)workspace;
+    if ((st = launch_chunked_state_simt(k, v, seg_states, bh, seq_len, (int)d_qk, (int)d_v,
+                                        dtype, false, g, seg_len, s)) != LA_OK)
+      return st;
+    if (g > 2 && (st = launch_prefix_segments(seg_states, nullptr, bh, g, g - 1, 1, per_head,
+                                              s)) != LA_OK)
+      return st;
+  }
+  return launch_chunked_output_simt(q, k, v, out, nullptr, nullptr, seg_states, bh, seq_len,
+                                    (int)d_qk, (int)d_v, dtype, false, eps, true, g, seg_len,
+                                    window, s);
 }
 
 int la_based_chunked_state(const void *k, const void *v, float *state_out, int64_t batch,
@@ -426,9 +507,12 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
   if (seq_len == 0) return cuda_status(cudaMemsetAsync(state_out, 0, state_bytes, s));
   const bool tc = use_tensor_cores(dtype, d_qk, d_v) && aligned16(k) &&
                   aligned16(v);
-  if (!tc && !chunked_simt_supported(feature_dim(d_qk), d_qk, d_v)) return LA_ERR_UNSUPPORTED;
-  int g = segments == 0 ? auto_segments(bh, seq_len, info.sm_count)
-                        : effective_segments(seq_len, segments);
+  const bool cluster = !tc && !chunked_simt_supported(feature_dim(d_qk), d_qk, d_v);
+  if (cluster && !cluster_chunked_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
+  // the same segmentation as la_based_chunked_fwd, so that a forward with
+  // LA_CHUNKED_REUSE_SEGMENTS finds the seeds it expects
+  const int wave = cluster ? info.sm_count / cluster_chunked_ctas_per_segment() : info.sm_count;
+  int g = segments == 0 ? auto_segments(bh, seq_len, wave) : effective_segments(seq_len, segments);
   if (g > 1) {
     const size_t need = la_based_chunked_workspace_size(bh, seq_len, d_qk, d_v, g);
     if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u))
@@ -436,9 +520,11 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
   }
   const int64_t seg_len = g > 1 ? segment_len(seq_len, g) : seq_len;
   float *dst = g > 1 ? (float *)workspace : state_out;
-  st = tc ? launch_chunked_state_tc(k, v, dst, bh, seq_len, g, g, seg_len, info, s)
-          : launch_chunked_state_simt(k, v, dst, bh, seq_len, (int)d_qk, (int)d_v, dtype, false, g,
-                                      seg_len, s);
+  st = tc        ? launch_chunked_state_tc(k, v, dst, bh, seq_len, g, g, seg_len, info, s)
+       : cluster ? launch_chunked_state_cluster(k, v, dst, bh, seq_len, (int)d_qk, (int)d_v,
+                                                dtype, g, g, seg_len, s)
+                 : launch_chunked_state_simt(k, v, dst, bh, seq_len, (int)d_qk, (int)d_v, dtype,
+                                             false, g, seg_len, s);
   if (st != LA_OK || g == 1) return st;
   // the total, and in the workspace the prefix slots a forward with
   // LA_CHUNKED_REUSE_SEGMENTS seeds its segments from

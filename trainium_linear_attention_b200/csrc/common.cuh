@@ -54,6 +54,11 @@ int current_device_info(DeviceInfo *info);
 // by the context's unique id.
 void *context_symbol_address(const void *symbol);
 
+// Raises `func`'s dynamic shared-memory limit to `bytes` in the current
+// context, once: later calls make no CUDA API call, so a launch that follows
+// can be captured into a CUDA graph.
+int allow_dynamic_smem(const void *func, int bytes);
+
 inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? LA_OK : LA_ERR_CUDA; }
 
 // Counts one kernel launch (la_launch_count).
@@ -86,17 +91,35 @@ int launch_chunked_output_simt(const void *q, const void *k, const void *v, void
                                const float *init_state, float *final_state,
                                const float *seg_states, int64_t bh, int64_t n, int dqk, int dv,
                                int dtype, bool identity, float eps, bool normalize, int segments,
-                               int64_t seg_len, cudaStream_t s);
+                               int64_t seg_len, int64_t window, cudaStream_t s);
 
 // Whether the SIMT chunked kernels hold a (features, d_v + 1) state on chip.
 bool chunked_simt_supported(int64_t features, int64_t dqk, int64_t dv);
+// ... and, for the full BASED layer (window > 0: sliding-window softmax added
+// in the same pass), also the K/V of the two chunks before (W <= 129).
+bool layer_simt_supported(int64_t dqk, int64_t dv, int64_t window);
+
+// Chunked kernels whose Taylor state is split by feature rows over a
+// thread-block cluster (cluster_chunked.cu), for widths whose state does not
+// fit one CTA (d_qk = 64: F = 2145).
+bool cluster_chunked_supported(int64_t dqk, int64_t dv);
+int cluster_chunked_ctas_per_segment();
+int launch_chunked_state_cluster(const void *k, const void *v, float *seg_states, int64_t bh,
+                                 int64_t n, int dqk, int dv, int dtype, int segments,
+                                 int n_launch, int64_t seg_len, cudaStream_t s);
+int launch_chunked_output_cluster(const void *q, const void *k, const void *v, void *out,
+                                  const float *init_state, float *final_state,
+                                  const float *seg_states, int64_t bh, int64_t n, int dqk, int dv,
+                                  int dtype, float eps, bool normalize, int segments,
+                                  int64_t seg_len, cudaStream_t s);
 
 // How la_based_chunked_fwd runs a request: the one place that decides the
 // kernels, the segmentation and the scratch it needs.
 struct ChunkedFwdPlan {
   bool identity = false;  // identity feature map (LA_CHUNKED_IDENTITY)
   int64_t features = 0;   // F: rows of a head's state
-  bool tc = false;        // tcgen05 kernels (else the SIMT kernels)
+  bool tc = false;        // tcgen05 kernels (else the SIMT or cluster kernels)
+  bool cluster = false;   // the cluster kernels (state split over kCluster CTAs)
   int64_t lead = 0;       // > 0: lead/main split with a lead of this many tokens
   int g = 1;              // equal segments per head
   int64_t seg_len = 0;    // tokens per segment

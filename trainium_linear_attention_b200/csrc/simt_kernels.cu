@@ -183,37 +183,53 @@ sliding_simt_kernel(const T *__restrict__ q, const T *__restrict__ k, const T *_
 // ---------------------------------------------------------------------------
 constexpr int kChunk = 64;
 
+// With a sliding window (the full BASED layer) the K/V chunks form a ring of
+// kRing buffers: chunk cc (global index t0 / 64) sits in buffer cc % kRing,
+// so the window's keys in the two chunks before stay on chip (W <= 129).
+constexpr int kRing = 3;
+constexpr int kMaxWindow = 2 * kChunk + 1;
+
 struct ChunkSmem {
-  float *S;   // [F][dv+1]
-  float *qs;  // [64][dqk+1]   raw q
-  float *ks;  // [64][dqk+1]   raw k
-  float *vs;  // [64][dv+1]    v with a trailing 1 (normaliser column)
+  float *S;      // [F][dv+1]
+  float *qs;     // [64][dqk+1]   raw q
+  float *ks;     // [64][dqk+1]   raw k of the current chunk
+  float *vs;     // [64][dv+1]    v with a trailing 1 (normaliser column)
+  float *kring;  // ring buffers (window > 0), stride kChunk * (dqk + 1)
+  float *vring;  //                           stride kChunk * (dv + 1)
 };
 
-__device__ __forceinline__ ChunkSmem carve(float *smem, int F, int dqk, int dv) {
+__device__ __forceinline__ ChunkSmem carve(float *smem, int F, int dqk, int dv, bool ring) {
   ChunkSmem c;
   c.S = smem;
   c.qs = c.S + F * (dv + 1);
-  c.ks = c.qs + kChunk * (dqk + 1);
-  c.vs = c.ks + kChunk * (dqk + 1);
+  c.kring = c.ks = c.qs + kChunk * (dqk + 1);
+  c.vring = c.vs = c.ks + (ring ? kRing : 1) * kChunk * (dqk + 1);
   return c;
 }
 
+// chunk cc's buffers (the ring slot cc % kRing; slot 0 without a ring)
+__device__ __forceinline__ void select_chunk(ChunkSmem &c, int64_t cc, int dqk, int dv,
+                                             bool ring) {
+  const int slot = ring ? (int)(cc % kRing) : 0;
+  c.ks = c.kring + slot * kChunk * (dqk + 1);
+  c.vs = c.vring + slot * kChunk * (dv + 1);
+}
+
 template <typename T>
-__device__ __forceinline__ void load_chunk_kv(const ChunkSmem &c, const T *kh, const T *vh,
+__device__ __forceinline__ void load_chunk_kv(float *ks, float *vs, const T *kh, const T *vh,
                                               int64_t t0, int64_t t_end, int dqk, int dv) {
   const int ldk = dqk + 1, ldv = dv + 1;
   for (int idx = threadIdx.x; idx < kChunk * dqk; idx += blockDim.x) {
     int r = idx / dqk, a = idx - r * dqk;
     int64_t t = t0 + r;
-    c.ks[r * ldk + a] = t < t_end ? to_f32(kh[t * dqk + a]) : 0.f;
+    ks[r * ldk + a] = t < t_end ? to_f32(kh[t * dqk + a]) : 0.f;
   }
   for (int idx = threadIdx.x; idx < kChunk * ldv; idx += blockDim.x) {
     int r = idx / ldv, e = idx - r * ldv;
     int64_t t = t0 + r;
     float x = 0.f;
     if (t < t_end) x = (e < dv) ? to_f32(vh[t * dv + e]) : 1.f;
-    c.vs[r * ldv + e] = x;
+    vs[r * ldv + e] = x;
   }
 }
 
@@ -271,7 +287,7 @@ chunked_state_simt_kernel(const T *__restrict__ k, const T *__restrict__ v,
   extern __shared__ float smem[];
   const int F = identity ? dqk : (int)feature_dim(dqk);
   const int ldv = dv + 1;
-  ChunkSmem c = carve(smem, F, dqk, dv);
+  ChunkSmem c = carve(smem, F, dqk, dv, false);
   const int64_t bh = blockIdx.y;
   const int g = blockIdx.x;
   const int64_t t_begin = (int64_t)g * seg_len;
@@ -281,7 +297,7 @@ chunked_state_simt_kernel(const T *__restrict__ k, const T *__restrict__ v,
   for (int i = threadIdx.x; i < F * ldv; i += blockDim.x) c.S[i] = 0.f;
   for (int64_t t0 = t_begin; t0 < t_end; t0 += kChunk) {
     __syncthreads();
-    load_chunk_kv(c, kh, vh, t0, t_end, dqk, dv);
+    load_chunk_kv(c.ks, c.vs, kh, vh, t0, t_end, dqk, dv);
     __syncthreads();
     chunk_state_update(c, F, dqk, dv, (int)min64(kChunk, t_end - t0), identity != 0);
   }
@@ -297,11 +313,12 @@ chunked_output_simt_kernel(const T *__restrict__ q, const T *__restrict__ k,
                            const float *__restrict__ init_state, float *__restrict__ final_state,
                            const float *__restrict__ seg_states, int64_t n, int dqk, int dv,
                            int identity, float eps, int normalize, int segments,
-                           int64_t seg_len) {
+                           int64_t seg_len, int window) {
   extern __shared__ float smem[];
   const int F = identity ? dqk : (int)feature_dim(dqk);
   const int ldv = dv + 1, ldq = dqk + 1;
-  ChunkSmem c = carve(smem, F, dqk, dv);
+  const bool ring = window > 0;
+  ChunkSmem c = carve(smem, F, dqk, dv, ring);
   const int64_t bh = blockIdx.y;
   const int g = blockIdx.x;
   const int64_t t_begin = (int64_t)g * seg_len;
@@ -323,9 +340,19 @@ chunked_output_simt_kernel(const T *__restrict__ q, const T *__restrict__ k,
   const float rsd = 1.f / sqrtf((float)dqk);
   const float w_diag = 1.f / (2.f * dqk), w_off = 1.f / (float)dqk;
 
+  // the window of the segment's first rows reaches into the two chunks
+  // before it: bring them into their ring slots
+  if (ring) {
+    for (int64_t cc = t_begin / kChunk - 2; cc < t_begin / kChunk; ++cc) {
+      if (cc < 0) continue;
+      select_chunk(c, cc, dqk, dv, true);
+      load_chunk_kv(c.ks, c.vs, kh, vh, cc * kChunk, n, dqk, dv);
+    }
+  }
   for (int64_t t0 = t_begin; t0 < t_end; t0 += kChunk) {
     __syncthreads();
-    load_chunk_kv(c, kh, vh, t0, t_end, dqk, dv);
+    select_chunk(c, t0 / kChunk, dqk, dv, ring);
+    load_chunk_kv(c.ks, c.vs, kh, vh, t0, t_end, dqk, dv);
     for (int idx = threadIdx.x; idx < kChunk * dqk; idx += blockDim.x) {
       int r = idx / dqk, a = idx - r * dqk;
       int64_t t = t0 + r;
@@ -397,13 +424,55 @@ chunked_output_simt_kernel(const T *__restrict__ q, const T *__restrict__ k,
     for (int i = 0; i < kMaxCols; ++i)
       if (lane + i * kLanesPerRow == dv) den_part = acc[i];
     const float den = row_allreduce(den_part);
+    const float inv = normalize ? 1.f / (den + eps) : 1.f;
+#pragma unroll
+    for (int i = 0; i < kMaxCols; ++i) acc[i] *= inv;
+    if (ring) {
+      // the full BASED layer: + softmax over the window [t - W + 1, t] of
+      // the same scores s = q.k / sqrt(d) (benchmarks/sliding_attention_
+      // benchmark.py:32-56), online over the keys of this chunk and the two
+      // before it; the key loop bounds are uniform over the CTA
+      const int64_t t_row = t0 + row;
+      float m = -INFINITY, l = 0.f;
+      float sw[kMaxCols];
+#pragma unroll
+      for (int i = 0; i < kMaxCols; ++i) sw[i] = 0.f;
+      for (int64_t kk = max64(0, t0 - window + 1); kk < t0 + rows; ++kk) {
+        const int64_t kc = kk / kChunk;
+        const int kr = (int)(kk - kc * kChunk);
+        const int slot = (int)(kc % kRing);
+        const float *krow = c.kring + (slot * kChunk + kr) * ldq;
+        const float *vrow = c.vring + (slot * kChunk + kr) * ldv;
+        float s = 0.f;
+        for (int a = lane; a < dqk; a += kLanesPerRow) s = fmaf(qr[a], krow[a], s);
+        s = row_allreduce(s) * rsd;
+        if (kk <= t_row && kk > t_row - window && row < rows) {  // uniform per row
+          if (s > m) {
+            const float corr = expf(m - s);  // exp(-inf) = 0 on the first key
+            l *= corr;
+#pragma unroll
+            for (int i = 0; i < kMaxCols; ++i) sw[i] *= corr;
+            m = s;
+          }
+          const float pe = expf(s - m);
+          l += pe;
+#pragma unroll
+          for (int i = 0; i < kMaxCols; ++i) {
+            const int e = lane + i * kLanesPerRow;
+            if (e < dv) sw[i] = fmaf(pe, vrow[e], sw[i]);
+          }
+        }
+      }
+      const float linv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxCols; ++i) acc[i] = fmaf(sw[i], linv, acc[i]);
+    }
     if (row < rows) {
-      const float inv = normalize ? 1.f / (den + eps) : 1.f;
       T *oh = out + (bh * n + t0 + row) * dv;
 #pragma unroll
       for (int i = 0; i < kMaxCols; ++i) {
         int e = lane + i * kLanesPerRow;
-        if (e < dv) oh[e] = from_f32<T>(acc[i] * inv);
+        if (e < dv) oh[e] = from_f32<T>(acc[i]);
       }
     }
     __syncthreads();  // every row read S before the update
@@ -416,8 +485,10 @@ chunked_output_simt_kernel(const T *__restrict__ q, const T *__restrict__ k,
   }
 }
 
-size_t chunked_simt_smem(int64_t F, int dqk, int dv) {
-  return sizeof(float) * (size_t)(F * (dv + 1) + 2 * kChunk * (dqk + 1) + kChunk * (dv + 1));
+size_t chunked_simt_smem(int64_t F, int dqk, int dv, bool ring = false) {
+  const int bufs = ring ? kRing : 1;
+  return sizeof(float) *
+         (size_t)(F * (dv + 1) + (1 + bufs) * kChunk * (dqk + 1) + bufs * kChunk * (dv + 1));
 }
 
 }  // namespace
@@ -425,6 +496,12 @@ size_t chunked_simt_smem(int64_t F, int dqk, int dv) {
 bool chunked_simt_supported(int64_t features, int64_t dqk, int64_t dv) {
   if (dqk < 1 || dqk > kMaxD || dv < 1 || dv > kMaxD || features < 1) return false;
   return chunked_simt_smem(features, (int)dqk, (int)dv) <= 200 * 1024;
+}
+
+bool layer_simt_supported(int64_t dqk, int64_t dv, int64_t window) {
+  if (dqk < 1 || dqk > kMaxD || dv < 1 || dv > kMaxD || window < 1 || window > kMaxWindow)
+    return false;
+  return chunked_simt_smem(feature_dim(dqk), (int)dqk, (int)dv, true) <= 200 * 1024;
 }
 
 #define LA_DISPATCH_DTYPE(dtype, T, ...)                    \
@@ -448,9 +525,7 @@ int launch_parallel_simt(const void *q, const void *k, const void *v, void *out,
   const float scale = 1.f / sqrtf((float)dqk);
   LA_DISPATCH_DTYPE(dtype, T, {
     if (smem > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(based_parallel_simt_kernel<T>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return LA_ERR_CUDA;
+      if (allow_dynamic_smem((const void *)based_parallel_simt_kernel<T>, (int)smem) != LA_OK) return LA_ERR_CUDA;
     }
     based_parallel_simt_kernel<T><<<grid, kThreads, smem, s>>>(
         (const T *)q, (const T *)k, (const T *)v, (T *)out, n, dqk, dv, scale, eps);
@@ -466,9 +541,7 @@ int launch_sliding_simt(const void *q, const void *k, const void *v, void *out, 
   const float scale = 1.f / sqrtf((float)d);
   LA_DISPATCH_DTYPE(dtype, T, {
     if (smem > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(sliding_simt_kernel<T>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return LA_ERR_CUDA;
+      if (allow_dynamic_smem((const void *)sliding_simt_kernel<T>, (int)smem) != LA_OK) return LA_ERR_CUDA;
     }
     sliding_simt_kernel<T><<<grid, kThreads, smem, s>>>((const T *)q, (const T *)k, (const T *)v,
                                                         (T *)out, n, d, window, scale);
@@ -484,9 +557,7 @@ int launch_chunked_state_simt(const void *k, const void *v, float *seg_states, i
   const size_t smem = chunked_simt_smem(F, dqk, dv);
   dim3 grid((unsigned)segments, (unsigned)bh);
   LA_DISPATCH_DTYPE(dtype, T, {
-    cudaError_t e = cudaFuncSetAttribute(chunked_state_simt_kernel<T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return LA_ERR_CUDA;
+    if (allow_dynamic_smem((const void *)chunked_state_simt_kernel<T>, (int)smem) != LA_OK) return LA_ERR_CUDA;
     chunked_state_simt_kernel<T><<<grid, kThreads, smem, s>>>(
         (const T *)k, (const T *)v, seg_states, n, dqk, dv, identity ? 1 : 0, segments, seg_len);
   });
@@ -497,18 +568,18 @@ int launch_chunked_output_simt(const void *q, const void *k, const void *v, void
                                const float *init_state, float *final_state,
                                const float *seg_states, int64_t bh, int64_t n, int dqk, int dv,
                                int dtype, bool identity, float eps, bool normalize, int segments,
-                               int64_t seg_len, cudaStream_t s) {
+                               int64_t seg_len, int64_t window, cudaStream_t s) {
   const int64_t F = identity ? dqk : feature_dim(dqk);
-  if (!chunked_simt_supported(F, dqk, dv)) return LA_ERR_UNSUPPORTED;
-  const size_t smem = chunked_simt_smem(F, dqk, dv);
+  if (window > 0 ? (identity || !layer_simt_supported(dqk, dv, window))
+                 : !chunked_simt_supported(F, dqk, dv))
+    return LA_ERR_UNSUPPORTED;
+  const size_t smem = chunked_simt_smem(F, dqk, dv, window > 0);
   dim3 grid((unsigned)segments, (unsigned)bh);
   LA_DISPATCH_DTYPE(dtype, T, {
-    cudaError_t e = cudaFuncSetAttribute(chunked_output_simt_kernel<T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return LA_ERR_CUDA;
+    if (allow_dynamic_smem((const void *)chunked_output_simt_kernel<T>, (int)smem) != LA_OK) return LA_ERR_CUDA;
     chunked_output_simt_kernel<T><<<grid, kThreads, smem, s>>>(
         (const T *)q, (const T *)k, (const T *)v, (T *)out, init_state, final_state, seg_states,
-        n, dqk, dv, identity ? 1 : 0, eps, normalize ? 1 : 0, segments, seg_len);
+        n, dqk, dv, identity ? 1 : 0, eps, normalize ? 1 : 0, segments, seg_len, (int)window);
   });
   return check_launch();
 }

@@ -1000,9 +1000,8 @@ int launch(const void *q, const void *k, const void *v, const Params &p, int64_t
     return LA_ERR_CUDA;
   }
   constexpr uint32_t kSmemAlloc = Layout<kStateOnly>::kSmemAlloc;
-  cudaError_t e = cudaFuncSetAttribute(chunked_tc_kernel<kStateOnly>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
-  if (e != cudaSuccess) return LA_ERR_CUDA;
+  if (allow_dynamic_smem((const void *)chunked_tc_kernel<kStateOnly>, (int)kSmemAlloc) != LA_OK)
+    return LA_ERR_CUDA;
   const dim3 grid = (!kStateOnly && p.lead_len > 0) ? dim3((unsigned)bh, 2u)
                                                    : dim3((unsigned)n_launch, (unsigned)bh);
   chunked_tc_kernel<kStateOnly><<<grid, kThreads, kSmemAlloc, s>>>(mq, mk, mv, p);

@@ -180,6 +180,13 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t *r) {
         "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(addr));
 }
+// 32 lanes x 32 bits, 8 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld8(uint32_t addr, uint32_t *r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(addr));
+}
 // One 32-bit column per lane.
 __device__ __forceinline__ uint32_t tmem_ld1(uint32_t addr) {
   uint32_t r;

@@ -600,8 +600,7 @@ int launch_parallel_tc(const void *q, const void *k, const void *v, void *out, i
     p.n = n;
     p.eps = eps;
     if (!p.err) return LA_ERR_CUDA;
-    if (cudaFuncSetAttribute(tile::parallel_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             tile::kSmemAlloc) != cudaSuccess)
+    if (allow_dynamic_smem((const void *)tile::parallel_tc_kernel, (int)tile::kSmemAlloc) != LA_OK)
       return LA_ERR_CUDA;
     dim3 grid((unsigned)tiles, (unsigned)bh);
     tile::parallel_tc_kernel<<<grid, 128, tile::kSmemAlloc, s>>>(mq, mk, mv, p);
@@ -616,9 +615,8 @@ int launch_parallel_tc(const void *q, const void *k, const void *v, void *out, i
   p.items = bh * tiles;
   p.eps = eps;
   if (!p.err) return LA_ERR_CUDA;
-  if (cudaFuncSetAttribute(persistent::parallel_tc_kernel,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           persistent::kSmemAlloc) != cudaSuccess)
+  if (allow_dynamic_smem((const void *)persistent::parallel_tc_kernel,
+                         (int)persistent::kSmemAlloc) != LA_OK)
     return LA_ERR_CUDA;
   const int sms = info.sm_count > 0 ? info.sm_count : 1;
   // whole heads per CTA once every SM has at least four (at most one head

@@ -370,8 +370,7 @@ int launch(const void *q, const void *k, const void *v, const SlidingParams &p, 
       !make_tmap_3d(&mk, k, bh, p.n, kD, kSpan, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_tmap_3d(&mv, v, bh, p.n, kD, kSpan, CU_TENSOR_MAP_SWIZZLE_128B))
     return LA_ERR_CUDA;
-  if (cudaFuncSetAttribute(sliding_tc_kernel<kSpan>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           L::kSmemAlloc) != cudaSuccess)
+  if (allow_dynamic_smem((const void *)sliding_tc_kernel<kSpan>, (int)L::kSmemAlloc) != LA_OK)
     return LA_ERR_CUDA;
   const int64_t grid = p.tiles < sm_count ? p.tiles : sm_count;
   sliding_tc_kernel<kSpan><<<(unsigned)grid, kThreadsSl, L::kSmemAlloc, s>>>(mq, mk, mv, p);

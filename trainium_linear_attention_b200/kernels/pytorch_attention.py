@@ -14,6 +14,10 @@ reference:
   RAISES on failure; unlike the reference it never falls back to PyTorch.
 * ``_check_nki()`` -- whether the native kernels can run here
   (kernels/pytorch_attention.py:16-24).
+* ``trace_solution(q, k, v, eps=1e-6)`` -- ``solution`` for one fixed shape
+  captured in a CUDA graph, the counterpart of the traced dispatch the
+  reference's crossover study measures against lazy dispatch
+  (benchmarks/crossover_benchmark.py:98-165, ``torch_neuronx.trace``).
 """
 
 from __future__ import annotations
@@ -91,3 +95,66 @@ def solution(q, k, v, eps=1e-6):
     if t <= limit:
         return ops.based_parallel(q, k, v, eps=eps)
     return ops.based_chunked(q, k, v, eps=eps)
+
+
+def solution_kind(q, k, v) -> str:
+    """Which kernel ``solution`` runs for these inputs: "parallel" or "chunked"."""
+    t = q.shape[-2]
+    if q.dtype == torch.float32:
+        limit = CROSSOVER_SEQ_LEN_FP32
+    elif q.shape[-1] == 16 and v.shape[-1] == 64:
+        limit = CROSSOVER_SEQ_LEN_BF16_TC
+    else:
+        limit = CROSSOVER_SEQ_LEN_BF16
+    return "parallel" if t <= limit else "chunked"
+
+
+class TracedSolution:
+    """``solution`` for one shape, dtype and device, captured in a CUDA graph.
+
+    The capture records the kernels ``solution`` launches for the example
+    inputs (including the chunked path's segment-state pass) against static
+    input and output buffers; a call copies new inputs into the static
+    buffers (skipped for inputs that already are them) and replays the graph,
+    removing the host-side dispatch of every later call.  The returned
+    tensor is the static output buffer, overwritten by the next call: clone
+    it to keep it.  Replays run on the current stream.
+    """
+
+    def __init__(self, q, k, v, eps=1e-6, warmup: int = 2):
+        if q.device.type != "cuda":
+            raise ValueError("trace_solution needs CUDA tensors")
+        self.eps = float(eps)
+        self.kind = solution_kind(q, k, v)
+        self.q = q.detach().clone().contiguous()
+        self.k = k.detach().clone().contiguous()
+        self.v = v.detach().clone().contiguous()
+        with torch.cuda.device(q.device):
+            side = torch.cuda.Stream(q.device)
+            side.wait_stream(torch.cuda.current_stream(q.device))
+            with torch.cuda.stream(side):  # resolve symbols and kernel attributes first
+                for _ in range(max(1, int(warmup))):
+                    solution(self.q, self.k, self.v, eps=self.eps)
+            torch.cuda.current_stream(q.device).wait_stream(side)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self.out = solution(self.q, self.k, self.v, eps=self.eps)
+
+    def replay(self):
+        """Re-run the captured kernels on the static inputs; returns the static output."""
+        self.graph.replay()
+        return self.out
+
+    def __call__(self, q, k, v):
+        for dst, src in ((self.q, q), (self.k, k), (self.v, v)):
+            if src.shape != dst.shape or src.dtype != dst.dtype or src.device != dst.device:
+                raise ValueError(f"traced for {tuple(dst.shape)} {dst.dtype} on {dst.device}, "
+                                 f"got {tuple(src.shape)} {src.dtype} on {src.device}")
+            if src.data_ptr() != dst.data_ptr():
+                dst.copy_(src)
+        return self.replay()
+
+
+def trace_solution(q, k, v, eps=1e-6) -> TracedSolution:
+    """Capture ``solution`` for the shape of the example inputs (see TracedSolution)."""
+    return TracedSolution(q, k, v, eps=eps)

@@ -173,6 +173,30 @@ def sliding_window(q, k, v, window_size: int = 64) -> torch.Tensor:
     return out
 
 
+def based_layer(q, k, v, window_size: int = 64, eps: float = 1e-6, segments: int = 0,
+                workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The full BASED layer: chunked BASED attention plus sliding-window
+    softmax attention over the same q, k, v, in one pass (window <= 129)."""
+    code = _check_qkv(q, k, v)
+    if int(window_size) < 1:
+        raise ValueError("window_size must be >= 1")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    b, h, t, d = q.shape
+    dv = v.shape[-1]
+    out = torch.empty((b, h, t, dv), dtype=q.dtype, device=q.device)
+    with torch.cuda.device(q.device):
+        g, ws_bytes = chunked_plan(b * h, t, d, dv, q.dtype, segments)
+        if workspace is None:
+            workspace = _workspace(ws_bytes, q.device)
+        st = N.lib().la_based_layer_fwd(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(out), b, h, t, d, dv, code, int(window_size),
+            float(eps), _ptr(workspace),
+            0 if workspace is None else workspace.numel() * workspace.element_size(),
+            int(segments), _stream_ptr(q.device))
+    N.check(st, "la_based_layer_fwd")
+    return out
+
+
 _copy_streams: dict = {}
 
 
