@@ -448,11 +448,13 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     }
   } else if (warp == kWarpUpd || warp == kWarpOut) {
     // ------------------------------------------------------------ MMA issuers
-    // Two threads issue into the same tensor pipe so each one's commits and
+    // Two warps issue into the same tensor pipe so each one's commits and
     // waits hide behind the other's MMAs:
-    //   update issuer (warp 1): S^T += [V 1 0]^T phi(K) for every tile;
-    //   output issuer (warp 2): per tile O = phi(Q) S_c, O += P [V 1], then
-    //                           the scores of the next tile.
+    //   update issuer (warp 23): S^T += [V 1 0]^T phi(K) for every tile;
+    //   output issuer (warp 24): per tile O = phi(Q) S_c, O += P [V 1], then
+    //                            the scores of the next tile.
+    // Each warp runs its loop converged (every lane waits, the warp agrees on
+    // the outcome) and one elected lane issues the MMAs and their commits.
     constexpr uint32_t id_sc = make_idesc_bf16(128, 128, false, false);
     constexpr uint32_t id_qs = make_idesc_bf16(128, kNO, false, false);
     constexpr uint32_t id_pv = make_idesc_bf16(128, kNO, false, true);
@@ -461,71 +463,79 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     constexpr uint64_t kStep = (uint64_t)(2048 >> 4) - ((uint64_t)(2048 >> 4) << 16);
     const uint32_t a_ones = sb + kOffOnes;
     // The state-only kernel has no other MMAs, so its updates are split over
-    // both issuing threads: tokens 0..63 of each tile into S^T, tokens
-    // 64..127 into a second accumulator (the full kernel's O columns) that
-    // starts at zero; the two are summed when the state is written out.
+    // both issuing warps: tokens 0..63 of each tile into S^T, tokens 64..127
+    // into a second accumulator (the full kernel's O columns) that starts at
+    // zero; the two are summed when the state is written out.
     auto update_loop = [&](int j0, int j1, uint32_t dcol, bool second) {
       for (int c = 0; c < n_chunks; ++c) {
         const int b = c & 1;          // phi(K) buffer
         const int sv = c % kVStages;  // V stage
-        if (!mbar_wait(&bars[kVFull + sv], (c / kVStages) & 1, abort_flag)) break;
+        if (!mbar_wait_warp(&bars[kVFull + sv], (c / kVStages) & 1, abort_flag)) break;
         LA_TRACE_AT(0, c, 7);
-        if (!mbar_wait(&bars[kPhiKReady0 + b], (c >> 1) & 1, abort_flag)) break;
+        if (!mbar_wait_warp(&bars[kPhiKReady0 + b], (c >> 1) & 1, abort_flag)) break;
         // S^T may change once the state warps have read S_c out of it
-        if (!second && (c == 0 || !kStateOnly) && !mbar_wait(&bars[kSRead], c & 1, abort_flag))
+        if (!second && (c == 0 || !kStateOnly) &&
+            !mbar_wait_warp(&bars[kSRead], c & 1, abort_flag))
           break;
         tc_fence_after();
         LA_TRACE_AT(0, c, 0);
         const uint32_t v_base = sb + kOffV + sv * kVBytes;
         const uint64_t db0 = make_sdesc(sb + kOffPhiK + b * kPhiBytes, kPhiBlock, 1024, kSwizzle128B);
         const uint64_t da0 = make_sdesc(v_base, a_ones - v_base, 1024, kSwizzle128B);
+        if (elect_one()) {
 #pragma unroll
-        for (int j = j0; j < j1; ++j)
-          umma_ss(tmem + dcol, da0 + kStep * j, db0 + (uint64_t)((j * 2048) >> 4), id_up,
-                  (second && c == 0 && j == j0) ? 0u : 1u);
-        if (!kStateOnly) umma_commit(&bars[kSReady]);
-        umma_commit(&bars[kUpDone0 + b]);
-        umma_commit(&bars[kVEmpty + sv]);
-        if (!second) *up_issued = c + 1;  // the state update of tile c is in the pipe
+          for (int j = j0; j < j1; ++j)
+            umma_ss(tmem + dcol, da0 + kStep * j, db0 + (uint64_t)((j * 2048) >> 4), id_up,
+                    (second && c == 0 && j == j0) ? 0u : 1u);
+          if (!kStateOnly) umma_commit(&bars[kSReady]);
+          umma_commit(&bars[kUpDone0 + b]);
+          umma_commit(&bars[kVEmpty + sv]);
+          if (!second) *up_issued = c + 1;  // the state update of tile c is in the pipe
+        }
+        __syncwarp();
       }
-      umma_commit(&bars[kDone]);
+      if (elect_one()) umma_commit(&bars[kDone]);
+      __syncwarp();
     };
-    if (lane == 0 && warp == kWarpUpd) {
+    if (warp == kWarpUpd) {
       update_loop(0, kStateOnly ? kT / 32 : kT / 16, kColS, false);
-    } else if (lane == 0 && kStateOnly) {
+    } else if (kStateOnly) {
       update_loop(kT / 32, kT / 16, kColO, true);
-    } else if (lane == 0) {
-      if (!kStateOnly) {
-        const uint64_t qs_b_desc0 = make_sdesc(sb + kOffSnap, 16, 1024, kSwizzle128B);
-        const uint64_t qs_b_desc1 = make_sdesc(sb + kOffSnap + kSnapBytes, 16, 1024, kSwizzle128B);
-        auto issue_scores = [&](int c) {
-          const int s = c % kQKStages;
-          const uint64_t da = make_sdesc(sb + kOffQ + s * kQBytes, 16, 256, kSwizzle32B);
-          const uint64_t db = make_sdesc(sb + kOffK + s * kQBytes, 16, 256, kSwizzle32B);
+    } else {
+      const uint64_t qs_b_desc0 = make_sdesc(sb + kOffSnap, 16, 1024, kSwizzle128B);
+      const uint64_t qs_b_desc1 = make_sdesc(sb + kOffSnap + kSnapBytes, 16, 1024, kSwizzle128B);
+      auto issue_scores = [&](int c) {
+        const int s = c % kQKStages;
+        const uint64_t da = make_sdesc(sb + kOffQ + s * kQBytes, 16, 256, kSwizzle32B);
+        const uint64_t db = make_sdesc(sb + kOffK + s * kQBytes, 16, 256, kSwizzle32B);
+        if (elect_one()) {
           umma_ss(tmem + kColSc, da, db, id_sc, 0);
           umma_commit(&bars[kScReady]);
           umma_commit(&bars[kQKEmpty + s]);
-        };
-        bool ok = mbar_wait(&bars[kQKFull], 0, abort_flag);
-        if (ok) {
-          tc_fence_after();
-          issue_scores(0);
         }
-        for (int c = 0; ok && c < n_chunks; ++c) {
-          const int b = c & 1;
-          // O = phi(Q) S_c   (K = 160 features in 10 steps; S_c is snapshot b)
-          if (!mbar_wait(&bars[kPhiQReady], c & 1, abort_flag)) break;
-          LA_TRACE_AT(0, c, 4);
-          if (!mbar_wait(&bars[kSnapReady0 + b], (c >> 1) & 1, abort_flag)) break;
-          LA_TRACE_AT(0, c, 5);
-          if (c > 0 && !mbar_wait(&bars[kOFree], (c - 1) & 1, abort_flag)) break;
-          LA_TRACE_AT(0, c, 6);
-          // let the update of tile c enter the pipe first: the next snapshot,
-          // and so the next tile, waits on it
-          if (!spin_until_at_least(up_issued, c + 1, abort_flag)) break;
-          tc_fence_after();
-          LA_TRACE_AT(0, c, 1);
-          const uint64_t qs_b_desc = b ? qs_b_desc1 : qs_b_desc0;
+        __syncwarp();
+      };
+      bool ok = mbar_wait_warp(&bars[kQKFull], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_scores(0);
+      }
+      for (int c = 0; ok && c < n_chunks; ++c) {
+        const int b = c & 1;
+        // O = phi(Q) S_c   (K = 160 features in 10 steps; S_c is snapshot b)
+        if (!mbar_wait_warp(&bars[kPhiQReady], c & 1, abort_flag)) break;
+        LA_TRACE_AT(0, c, 4);
+        if (!mbar_wait_warp(&bars[kSnapReady0 + b], (c >> 1) & 1, abort_flag)) break;
+        LA_TRACE_AT(0, c, 5);
+        if (c > 0 && !mbar_wait_warp(&bars[kOFree], (c - 1) & 1, abort_flag)) break;
+        LA_TRACE_AT(0, c, 6);
+        // let the update of tile c enter the pipe first: the next snapshot,
+        // and so the next tile, waits on it
+        if (!__all_sync(0xffffffffu, spin_until_at_least(up_issued, c + 1, abort_flag))) break;
+        tc_fence_after();
+        LA_TRACE_AT(0, c, 1);
+        const uint64_t qs_b_desc = b ? qs_b_desc1 : qs_b_desc0;
+        if (elect_one()) {
 #pragma unroll
           for (int j = 0; j < kFPad / 16; ++j) {
             const uint32_t boff = (j >> 2) * kSnapKBlock + (j & 3) * 32;
@@ -533,33 +543,39 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
                     j > 0 ? 1u : 0u);
           }
           umma_commit(&bars[kQSDone0 + b]);
-          // O += P [V 1]: B = V (64 columns) with the ones block as its second
-          // 64-column block (LBO), so O[:, 64] also collects the row sum of P.
-          if (!mbar_wait(&bars[kPReady], c & 1, abort_flag)) break;
-          const int sv = c % kVStages;
-          if (!mbar_wait(&bars[kVFull + sv], (c / kVStages) & 1, abort_flag)) break;
-          tc_fence_after();
-          LA_TRACE_AT(0, c, 2);
-          const uint32_t v_base = sb + kOffV + sv * kVBytes;
-          const uint64_t db0 = make_sdesc(v_base, a_ones - v_base, 1024, kSwizzle128B);
+        }
+        __syncwarp();
+        // O += P [V 1]: B = V (64 columns) with the ones block as its second
+        // 64-column block (LBO), so O[:, 64] also collects the row sum of P.
+        if (!mbar_wait_warp(&bars[kPReady], c & 1, abort_flag)) break;
+        const int sv = c % kVStages;
+        if (!mbar_wait_warp(&bars[kVFull + sv], (c / kVStages) & 1, abort_flag)) break;
+        tc_fence_after();
+        LA_TRACE_AT(0, c, 2);
+        const uint32_t v_base = sb + kOffV + sv * kVBytes;
+        const uint64_t db0 = make_sdesc(v_base, a_ones - v_base, 1024, kSwizzle128B);
+        if (elect_one()) {
 #pragma unroll
           for (int j = 0; j < kT / 16; ++j)
             umma_ts(tmem + kColO, tmem + kColSc + 8 * j, db0 + kStep * j, id_pv, 1u);
           umma_commit(&bars[kOReady]);
-          // the scores of tile c+1 overwrite P(c): wait for P V to finish;
-          // that also ends this issuer's use of TMA stage b
-          if (!mbar_wait(&bars[kOReady], c & 1, abort_flag)) break;
-          mbar_arrive(&bars[kVEmpty + sv]);
-          LA_TRACE_AT(0, c, 3);
-          if (c + 1 < n_chunks) {
-            const int c1 = c + 1;
-            if (!mbar_wait(&bars[kQKFull + c1 % kQKStages], (c1 / kQKStages) & 1, abort_flag)) break;
-            tc_fence_after();
-            issue_scores(c + 1);
-          }
+        }
+        __syncwarp();
+        // the scores of tile c+1 overwrite P(c): wait for P V to finish;
+        // that also ends this issuer's use of TMA stage b
+        if (!mbar_wait_warp(&bars[kOReady], c & 1, abort_flag)) break;
+        if (lane == 0) mbar_arrive(&bars[kVEmpty + sv]);
+        LA_TRACE_AT(0, c, 3);
+        if (c + 1 < n_chunks) {
+          const int c1 = c + 1;
+          if (!mbar_wait_warp(&bars[kQKFull + c1 % kQKStages], (c1 / kQKStages) & 1, abort_flag))
+            break;
+          tc_fence_after();
+          issue_scores(c + 1);
         }
       }
-      umma_commit(&bars[kDone]);
+      if (elect_one()) umma_commit(&bars[kDone]);
+      __syncwarp();
     }
   } else if (warp < kWarpPoly) {
     // ------------------------------------------------------------ features

@@ -116,6 +116,30 @@ __device__ __forceinline__ bool spin_until_at_least(volatile int *counter, int t
   return true;
 }
 
+// Bounded wait by a whole converged warp: every lane waits on the barrier
+// and the warp agrees on the outcome (false if any lane gave up), so the
+// warp's control flow stays uniform.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity,
+                                               volatile int *abort_flag) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+}
+
+// True in exactly one lane of a converged warp (elect.sync): the lane that
+// issues a single-thread tcgen05 instruction for the warp.  A warp that runs
+// its MMA loop converged and issues through the elected lane issues
+// tile-shaped tcgen05.mma sequences 18-38% faster than the same loop run by
+// lane 0 alone (measured on B200: 8 ss N=160 MMAs 1096 -> 898 cycles, 10 ts
+// N=80 MMAs 978 -> 606 cycles, each with its commit and wait).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // ------------------------------------------------------------------- fences ---
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
