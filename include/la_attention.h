@@ -190,8 +190,10 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out,
  * based_attention_benchmark.py:24-69 would call separately), computed in one
  * pass over q, k and v: each chunk's keys and values serve the chunked
  * recurrence and, kept on chip, the windows of the next two chunks
- * (window <= 129).  The sliding half uses the same scale 1/sqrt(d_qk), the
- * window [i - W + 1, i] and fp32 softmax accumulation.  segments and the
+ * (window <= 129); states too wide for one CTA (d_qk = 64) are split over a
+ * thread-block cluster as in la_based_chunked_fwd.  The sliding half uses the
+ * same scale 1/sqrt(d_qk), the window [i - W + 1, i] and fp32 softmax
+ * accumulation.  segments and the
  * workspace work as for la_based_chunked_fwd (la_based_chunked_plan sizes
  * it); the window of a segment's first tokens reads the keys before it.
  * The reference has no kernel for the fused layer.

@@ -441,6 +441,18 @@ def test_layer_bf16(t, w, segments):
     assert O.rel_l2(np64(y), want) <= TOL_BF16
 
 
+@pytest.mark.parametrize("t,w,segments,dtype", [(256, 64, 0, torch.float32), (1000, 64, 0, torch.bfloat16),
+                                                (1500, 129, 3, torch.bfloat16), (70, 7, 0, torch.float32)])
+def test_layer_d64(t, w, segments, dtype):
+    """The full BASED layer at d_qk = 64 (the reference module's head width,
+    F = 2145): the state is split over a cluster, the window keys before a
+    chunk come from memory."""
+    q, k, v = inputs((1, 2, t, 64), 64, seed=750 + t, scale=0.5, dtype=dtype)
+    y = ops.based_layer(*cuda(q, k, v), window_size=w, segments=segments)
+    want = O.based_layer(np64(q), np64(k), np64(v), w)
+    assert O.rel_l2(np64(y), want) <= (TOL_FP32 if dtype == torch.float32 else TOL_BF16)
+
+
 def test_layer_segments_agree():
     """Segments seed the state from the earlier segments and read the window
     keys before their first token from memory: same result as one segment."""

@@ -418,7 +418,8 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
     st = launch_chunked_state_tc(k, v, lead_states, bh, seq_len, 1, 1, plan.lead, info, s);
     if (st != LA_OK) return st;
     return launch_chunked_output_tc(q, k, v, out, init_state, final_state, lead_states, bh,
-                                    seq_len, eps, normalize, 1, seq_len, plan.lead, info, s);
+                                    seq_len, eps, normalize, 1, seq_len, plan.lead, true, info,
+                                    s);
   }
   const int g = plan.g;
   float *seg_states = g > 1 ? (float *)workspace : nullptr;
@@ -439,16 +440,18 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
     if (st != LA_OK) return st;
     if ((g - 1) * plan.ratio > 1 &&
         (st = launch_prefix_segments(seg_states, nullptr, bh, g, g - 1, plan.ratio,
-                                     (int64_t)per_head, s)) != LA_OK)
+                                     (int64_t)per_head, s, plan.tc)) != LA_OK)
       return st;
   }
+  const bool after_state_pass = g > 1 && !(flags & LA_CHUNKED_REUSE_SEGMENTS);
   if (plan.tc)
     return launch_chunked_output_tc(q, k, v, out, init_state, final_state, seg_states, bh,
-                                    seq_len, eps, normalize, g, plan.seg_len, 0, info, s);
+                                    seq_len, eps, normalize, g, plan.seg_len, 0,
+                                    after_state_pass, info, s);
   if (plan.cluster)
     return launch_chunked_output_cluster(q, k, v, out, init_state, final_state, seg_states, bh,
                                          seq_len, (int)d_qk, (int)d_v, dtype, eps, normalize, g,
-                                         plan.seg_len, s);
+                                         plan.seg_len, 0, s);
   return launch_chunked_output_simt(q, k, v, out, init_state, final_state, seg_states, bh,
                                     seq_len, (int)d_qk, (int)d_v, dtype, plan.identity, eps,
                                     normalize, g, plan.seg_len, 0, s);
@@ -463,11 +466,15 @@ int la_based_layer_fwd(const void *q, const void *k, const void *v, void *out, i
   if (window < 1 || segments < 0) return LA_ERR_INVALID_ARGUMENT;
   const int64_t bh = batch * heads;
   if (bh == 0 || seq_len == 0) return LA_OK;
-  if (!layer_simt_supported(d_qk, d_v, window)) return LA_ERR_UNSUPPORTED;
+  // one CTA per (head, segment) holds the state and the window's two
+  // previous chunks; wider states split over a cluster
+  const bool simt = layer_simt_supported(d_qk, d_v, window);
+  if (!simt && (window > 129 || !cluster_chunked_supported(d_qk, d_v))) return LA_ERR_UNSUPPORTED;
   DeviceInfo info;
   if ((st = require_sm100(&info)) != LA_OK) return st;
   cudaStream_t s = (cudaStream_t)stream;
-  const int g = segments == 0 ? auto_segments(bh, seq_len, info.sm_count)
+  const int wave = simt ? info.sm_count : info.sm_count / cluster_chunked_ctas_per_segment();
+  const int g = segments == 0 ? auto_segments(bh, seq_len, wave)
                               : effective_segments(seq_len, segments);
   const int64_t seg_len = g > 1 ? segment_len(seq_len, g) : seq_len;
   const int64_t per_head = feature_dim(d_qk) * (d_v + 1);
@@ -477,13 +484,19 @@ int la_based_layer_fwd(const void *q, const void *k, const void *v, void *out, i
     if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u))
       return LA_ERR_WORKSPACE;
     seg_states = (float *)workspace;
-    if ((st = launch_chunked_state_simt(k, v, seg_states, bh, seq_len, (int)d_qk, (int)d_v,
-                                        dtype, false, g, seg_len, s)) != LA_OK)
-      return st;
+    st = simt ? launch_chunked_state_simt(k, v, seg_states, bh, seq_len, (int)d_qk, (int)d_v,
+                                          dtype, false, g, seg_len, s)
+              : launch_chunked_state_cluster(k, v, seg_states, bh, seq_len, (int)d_qk, (int)d_v,
+                                             dtype, g, g - 1, seg_len, s);
+    if (st != LA_OK) return st;
     if (g > 2 && (st = launch_prefix_segments(seg_states, nullptr, bh, g, g - 1, 1, per_head,
                                               s)) != LA_OK)
       return st;
   }
+  if (!simt)
+    return launch_chunked_output_cluster(q, k, v, out, nullptr, nullptr, seg_states, bh, seq_len,
+                                         (int)d_qk, (int)d_v, dtype, eps, true, g, seg_len,
+                                         window, s);
   return launch_chunked_output_simt(q, k, v, out, nullptr, nullptr, seg_states, bh, seq_len,
                                     (int)d_qk, (int)d_v, dtype, false, eps, true, g, seg_len,
                                     window, s);
@@ -529,7 +542,7 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
   // the total, and in the workspace the prefix slots a forward with
   // LA_CHUNKED_REUSE_SEGMENTS seeds its segments from
   return launch_prefix_segments(dst, state_out, bh, g, g, 1,
-                                (int64_t)feature_dim(d_qk) * (d_v + 1), s);
+                                (int64_t)feature_dim(d_qk) * (d_v + 1), s, tc);
 }
 
 int la_sliding_window_fwd(const void *q, const void *k, const void *v, void *out, int64_t batch,

@@ -18,7 +18,11 @@
 //   every CTA     S_r += phi_k(K)[:, rows of r]^T [V 1]
 //
 // The partials are double-buffered by chunk parity, so one cluster barrier
-// per chunk orders both their writes and their reads.  All arithmetic is
+// per chunk orders both their writes and their reads.  With a window W > 0
+// (the full BASED layer) CTA r adds, for its rows, the softmax over the keys
+// [t - W + 1, t] of the same scores (one warp per row; keys of this chunk from
+// shared memory, earlier keys from global memory, where all CTAs of the
+// cluster have just read them).  All arithmetic is
 // fp32 on CUDA cores, in a fixed order (deterministic).  A segmented run
 // seeds each segment from the running sums of the earlier segments' states
 // (state pass below, which splits the features over independent CTAs).
@@ -38,6 +42,7 @@ constexpr int kRowsPerRank = kCT / kCluster;  // output rows each CTA finishes
 constexpr int kMaxD = 128;
 constexpr int kMaxCols = (kMaxD + 1 + 3) / 4;  // value columns per thread (4 lanes per token)
 constexpr size_t kSmemLimit = 200 * 1024;
+constexpr int64_t kMaxWindow = 129;  // the full BASED layer's window (as the SIMT path)
 
 // One feature of the Taylor basis: phi_k = ka * kb (a factor with index < 0
 // is 1), phi_q = wq * qa * qb.
@@ -144,7 +149,8 @@ cluster_chunked_output_kernel(const T *__restrict__ q, const T *__restrict__ k,
                               const float *__restrict__ init_state,
                               float *__restrict__ final_state,
                               const float *__restrict__ seg_states, int64_t n, int dqk, int dv,
-                              float eps, int normalize, int segments, int64_t seg_len) {
+                              float eps, int normalize, int segments, int64_t seg_len,
+                              int window) {
   extern __shared__ float smem[];
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
@@ -241,12 +247,57 @@ cluster_chunked_output_kernel(const T *__restrict__ q, const T *__restrict__ k,
       tmp[il * ldv + e] = acc;
     }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < kRowsPerRank * dv; idx += kThr) {
-      const int il = idx / dv, e = idx - il * dv, i = r0 + il;
+    if (window > 0) {
+      // warp il: row r0 + il; lanes split the q.k dot product and own value
+      // columns e = lane + 32 m
+      const int il = threadIdx.x >> 5, ln = threadIdx.x & 31, i = r0 + il;
+      const int64_t t_row = t0 + i;
+      float m = -INFINITY, l = 0.f, sw[kMaxD / 32];
+#pragma unroll
+      for (int u = 0; u < kMaxD / 32; ++u) sw[u] = 0.f;
       if (i < rows) {
+        for (int64_t kk = max64(0, t_row - window + 1); kk <= t_row; ++kk) {
+          const bool here = kk >= t0;
+          float sp = 0.f;
+          for (int a = ln; a < dqk; a += 32) {
+            const float kv = here ? ks[(kk - t0) * ldq + a] : to_f32(kh[kk * dqk + a]);
+            sp = fmaf(qs[i * ldq + a], kv, sp);
+          }
+#pragma unroll
+          for (int o = 16; o >= 1; o >>= 1) sp += __shfl_xor_sync(0xffffffffu, sp, o);
+          const float sc = sp * rsd;
+          if (sc > m) {
+            const float corr = expf(m - sc);  // exp(-inf) = 0 on the first key
+            l *= corr;
+#pragma unroll
+            for (int u = 0; u < kMaxD / 32; ++u) sw[u] *= corr;
+            m = sc;
+          }
+          const float pe = expf(sc - m);
+          l += pe;
+#pragma unroll
+          for (int u = 0; u < kMaxD / 32; ++u) {
+            const int e = ln + 32 * u;
+            if (e < dv) sw[u] = fmaf(pe, here ? vs[(kk - t0) * ldv + e] : to_f32(vh[kk * dv + e]),
+                                     sw[u]);
+          }
+        }
         const float den = tmp[il * ldv + dv] + eps;
-        const float y = normalize ? tmp[il * ldv + e] / den : tmp[il * ldv + e];
-        out[(bh * n + t0 + i) * dv + e] = from_f32<T>(y);
+#pragma unroll
+        for (int u = 0; u < kMaxD / 32; ++u) {
+          const int e = ln + 32 * u;
+          if (e < dv)
+            out[(bh * n + t0 + i) * dv + e] = from_f32<T>(tmp[il * ldv + e] / den + sw[u] / l);
+        }
+      }
+    } else {
+      for (int idx = threadIdx.x; idx < kRowsPerRank * dv; idx += kThr) {
+        const int il = idx / dv, e = idx - il * dv, i = r0 + il;
+        if (i < rows) {
+          const float den = tmp[il * ldv + dv] + eps;
+          const float y = normalize ? tmp[il * ldv + e] / den : tmp[il * ldv + e];
+          out[(bh * n + t0 + i) * dv + e] = from_f32<T>(y);
+        }
       }
     }
     // the state update of this CTA's features (reads ks / vs, writes S)
@@ -342,8 +393,9 @@ int launch_chunked_output_cluster(const void *q, const void *k, const void *v, v
                                   const float *init_state, float *final_state,
                                   const float *seg_states, int64_t bh, int64_t n, int dqk, int dv,
                                   int dtype, float eps, bool normalize, int segments,
-                                  int64_t seg_len, cudaStream_t s) {
+                                  int64_t seg_len, int64_t window, cudaStream_t s) {
   if (!cluster_chunked_supported(dqk, dv)) return LA_ERR_UNSUPPORTED;
+  if (window < 0 || window > kMaxWindow) return LA_ERR_UNSUPPORTED;
   const size_t smem = ClusterSmem((int)feature_dim(dqk), dqk, dv, true).bytes;
   const dim3 grid((unsigned)(kCluster * segments), (unsigned)bh);
   LA_CLUSTER_DISPATCH(dtype, T, {
@@ -351,7 +403,7 @@ int launch_chunked_output_cluster(const void *q, const void *k, const void *v, v
       return LA_ERR_CUDA;
     cluster_chunked_output_kernel<T><<<grid, kThr, smem, s>>>(
         (const T *)q, (const T *)k, (const T *)v, (T *)out, init_state, final_state, seg_states,
-        n, dqk, dv, eps, normalize ? 1 : 0, segments, seg_len);
+        n, dqk, dv, eps, normalize ? 1 : 0, segments, seg_len, (int)window);
   });
   return check_launch();
 }

@@ -111,7 +111,7 @@ int launch_chunked_output_cluster(const void *q, const void *k, const void *v, v
                                   const float *init_state, float *final_state,
                                   const float *seg_states, int64_t bh, int64_t n, int dqk, int dv,
                                   int dtype, float eps, bool normalize, int segments,
-                                  int64_t seg_len, cudaStream_t s);
+                                  int64_t seg_len, int64_t window, cudaStream_t s);
 
 // How la_based_chunked_fwd runs a request: the one place that decides the
 // kernels, the segmentation and the scratch it needs.

@@ -591,6 +591,10 @@ namespace {
 __global__ void prefix_segments_kernel(float *__restrict__ seg, float *__restrict__ total,
                                        int stride, int groups, int ratio, int64_t per_head) {
   constexpr int kMaxSlots = 16;
+  // launched as the programmatic dependent of the state pass: wait for its
+  // states, and let the output pass after this kernel be scheduled
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int64_t bh = blockIdx.y;
   const int slots = groups * ratio;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per_head;
@@ -622,9 +626,22 @@ __global__ void prefix_segments_kernel(float *__restrict__ seg, float *__restric
 }  // namespace
 
 int launch_prefix_segments(float *seg, float *total, int64_t bh, int stride, int groups,
-                           int ratio, int64_t per_head, cudaStream_t s) {
-  dim3 grid((unsigned)((per_head + 255) / 256), (unsigned)bh);
-  prefix_segments_kernel<<<grid, 256, 0, s>>>(seg, total, stride, groups, ratio, per_head);
+                           int ratio, int64_t per_head, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((per_head + 255) / 256), (unsigned)bh);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, prefix_segments_kernel, seg, total, stride, groups, ratio,
+                         per_head) != cudaSuccess) {
+    note_launch();
+    cudaGetLastError();
+    return LA_ERR_CUDA;
+  }
   return check_launch();
 }
 }  // namespace la

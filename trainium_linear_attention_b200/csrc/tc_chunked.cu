@@ -89,8 +89,11 @@ constexpr uint32_t kTmemCols = 512;
 // Shared memory (offsets from a 1024-byte aligned base)
 constexpr uint32_t kQBytes = kT * kDqk * 2;         // 4 KB, 32B-swizzled rows
 constexpr uint32_t kVBytes = kT * kDv * 2;          // 16 KB, 128B-swizzled rows
-constexpr uint32_t kPhiBlock = kT * 128;            // 64 features of 128 tokens
-constexpr uint32_t kPhiBytes = 3 * kPhiBlock;       // 160 features (3 blocks)
+// phi(K): the MN-major B operand of the update, 64B-swizzled rows of 32
+// features (5 blocks of 128 tokens x 64 B hold the 160 feature slots exactly;
+// 128B rows would leave half of a third 64-feature block empty)
+constexpr uint32_t kPhiBlock = kT * 64;             // 32 features of 128 tokens
+constexpr uint32_t kPhiBytes = 5 * kPhiBlock;       // 160 features (5 blocks)
 // Snapshots of S: the K-major B operand of phi(Q) S, 80 rows x 160 features
 // in three 64-feature blocks of 80 x 128 B.  (Letting the two buffers share
 // their half-used third block was measured 19% slower: the state warps then
@@ -105,9 +108,10 @@ constexpr int kMaxStages = 6;
 // room on deeper K and V rings, since nothing else hides its load latency.
 template <bool kStateOnly>
 struct Layout {
-  // (full kernel: V is released only after P V, late in the tile, so its
-  // ring is the deeper one: measured 3% faster than 3 Q/K and 2 V stages)
-  static constexpr int kQKStages = kStateOnly ? 6 : 2;
+  // (full kernel: a Q/K copy takes ~2,200 cycles to land under load and its
+  // stage is released only by the scores MMA of its tile, late in the
+  // tile, so both rings are several tiles deep)
+  static constexpr int kQKStages = kStateOnly ? 6 : 4;
   static constexpr int kVStages = kStateOnly ? 6 : 3;
   static constexpr uint32_t kOffQ = 0;
   static constexpr uint32_t kOffK = kOffQ + (kStateOnly ? 0 : kQKStages * kQBytes);
@@ -131,7 +135,7 @@ struct Layout {
 enum Bar { kQKFull = 0, kQKEmpty = kQKFull + kMaxStages, kVFull = kQKEmpty + kMaxStages,
            kVEmpty = kVFull + kMaxStages, kPhiKReady0 = kVEmpty + kMaxStages, kPhiKReady1,
            kUpDone0, kUpDone1, kQSDone0, kQSDone1, kSnapReady0, kSnapReady1, kSRead, kPhiQReady, kScReady,
-           kPReady, kOReady, kOFree, kSReady, kDone, kNumBars };
+           kPReadyLo, kPReadyHi, kOReady, kOFree, kSReady, kDone, kNumBars };
 static_assert(8 * kNumBars + 12 <= 512, "barrier area");
 
 // Optional per-role timeline of CTA (0, 0), compiled in with -DLA_TRACE only.
@@ -267,11 +271,11 @@ __device__ __forceinline__ uint32_t pair_val(const FeatIn &s) {
 }
 
 // Slots 8J .. 8J+7 (pairs 4J .. 4J+3, one 16-byte chunk) of token `row` ->
-// 128B-swizzled smem, 64 slots per 16 KB block: the MN-major B layout of
+// 64B-swizzled smem, 32 slots per 8 KB block: the MN-major B layout of
 // phi(K) for the update MMA.
 template <int J>
 __device__ __forceinline__ void store_phik_chunk(const FeatIn &s, uint32_t base, int row) {
-  st_shared_v4(base + (J >> 3) * kPhiBlock + sw128_offset(row, J & 7), pair_val<false, 4 * J + 0>(s),
+  st_shared_v4(base + (J >> 2) * kPhiBlock + sw64_offset(row, J & 3), pair_val<false, 4 * J + 0>(s),
                pair_val<false, 4 * J + 1>(s), pair_val<false, 4 * J + 2>(s),
                pair_val<false, 4 * J + 3>(s));
 }
@@ -367,18 +371,22 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     // every barrier: one arrival (a leader thread, a TMA expect-tx or a
     // tcgen05.commit), except: a Q/K stage is released by the features and
     // (full kernel) the scores MMA, a V stage by the update and (full kernel)
-    // P V, `done` by both MMA issuers
+    // P V, `done` by both MMA issuers, each half of P by the four lane
+    // quarters' polynomial warp pairs
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t count = 1;
       if (i >= kQKEmpty && i < kQKEmpty + kMaxStages) count = kStateOnly ? 1 : 2;
       if (i >= kVEmpty && i < kVEmpty + kMaxStages) count = 2;
       if ((i == kUpDone0 || i == kUpDone1) && kStateOnly) count = 2;
       if (i == kDone) count = 2;
+      if (i == kPReadyLo || i == kPReadyHi) count = 4;  // one polynomial warp pair per quarter
       mbar_init(&bars[i], count);
     }
     *abort_flag = 0;
     *up_issued = 0;
     fence_barrier_init();
+    // the output pass that follows a state pass may take SMs as they free up
+    if (kStateOnly) grid_dependents_launch();
   }
   if (threadIdx.x < kFPad / 2)
     ((uint32_t *)(smem + kOffSlot))[threadIdx.x] = ((const uint32_t *)g_slot_map.f)[threadIdx.x];
@@ -480,12 +488,14 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         tc_fence_after();
         LA_TRACE_AT(0, c, 0);
         const uint32_t v_base = sb + kOffV + sv * kVBytes;
-        const uint64_t db0 = make_sdesc(sb + kOffPhiK + b * kPhiBytes, kPhiBlock, 1024, kSwizzle128B);
+        // phi(K): 32-feature blocks kPhiBlock apart (LBO), 8-token groups 512 B
+        // apart (SBO); a K-step of 16 tokens advances 1024 B
+        const uint64_t db0 = make_sdesc(sb + kOffPhiK + b * kPhiBytes, kPhiBlock, 512, kSwizzle64B);
         const uint64_t da0 = make_sdesc(v_base, a_ones - v_base, 1024, kSwizzle128B);
         if (elect_one()) {
 #pragma unroll
           for (int j = j0; j < j1; ++j)
-            umma_ss(tmem + dcol, da0 + kStep * j, db0 + (uint64_t)((j * 2048) >> 4), id_up,
+            umma_ss(tmem + dcol, da0 + kStep * j, db0 + (uint64_t)((j * 1024) >> 4), id_up,
                     (second && c == 0 && j == j0) ? 0u : 1u);
           if (!kStateOnly) umma_commit(&bars[kSReady]);
           umma_commit(&bars[kUpDone0 + b]);
@@ -547,20 +557,30 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         __syncwarp();
         // O += P [V 1]: B = V (64 columns) with the ones block as its second
         // 64-column block (LBO), so O[:, 64] also collects the row sum of P.
-        if (!mbar_wait_warp(&bars[kPReady], c & 1, abort_flag)) break;
+        // P arrives in two halves (keys 0..63, then 64..127): the first
+        // half's MMAs run while the polynomial warps finish the second.
         const int sv = c % kVStages;
         if (!mbar_wait_warp(&bars[kVFull + sv], (c / kVStages) & 1, abort_flag)) break;
-        tc_fence_after();
-        LA_TRACE_AT(0, c, 2);
         const uint32_t v_base = sb + kOffV + sv * kVBytes;
         const uint64_t db0 = make_sdesc(v_base, a_ones - v_base, 1024, kSwizzle128B);
-        if (elect_one()) {
+        bool pv_ok = true;
 #pragma unroll
-          for (int j = 0; j < kT / 16; ++j)
-            umma_ts(tmem + kColO, tmem + kColSc + 8 * j, db0 + kStep * j, id_pv, 1u);
-          umma_commit(&bars[kOReady]);
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait_warp(&bars[h ? kPReadyHi : kPReadyLo], c & 1, abort_flag)) {
+            pv_ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (h == 0) LA_TRACE_AT(0, c, 2);
+          if (elect_one()) {
+#pragma unroll
+            for (int j = 4 * h; j < 4 * h + 4; ++j)
+              umma_ts(tmem + kColO, tmem + kColSc + 8 * j, db0 + kStep * j, id_pv, 1u);
+            if (h == 1) umma_commit(&bars[kOReady]);
+          }
+          __syncwarp();
         }
-        __syncwarp();
+        if (!pv_ok) break;
         // the scores of tile c+1 overwrite P(c): wait for P V to finish;
         // that also ends this issuer's use of TMA stage b
         if (!mbar_wait_warp(&bars[kOReady], c & 1, abort_flag)) break;
@@ -579,10 +599,14 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     }
   } else if (warp < kWarpPoly) {
     // ------------------------------------------------------------ features
+    // phi(K) of tile c + 1 is produced before phi(Q) of tile c: the update
+    // of tile c + 1 (the state chain) waits on the former, while phi(Q) S of
+    // tile c has slack; both tiles' Q/K stages are resident (the ring is
+    // deeper than two tiles, and a stage is released only after its phi(Q)).
     const int wq = warp & 3;
     const int row = wq * 32 + lane;  // token within the tile == TMEM lane
     const bool leader = (warp == kWarpFeat && lane == 0);
-    for (int c = 0; c < n_chunks; ++c) {
+    auto do_phik = [&](int c) {
       const int s = c & 1;           // phi(K) buffer
       const int sq = c % kQKStages;  // Q/K stage
       mbar_wait(&bars[kQKFull + sq], (c / kQKStages) & 1, abort_flag);
@@ -590,15 +614,10 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       LA_TRACE_AT(1, c, 0);
       const int valid = (int)min64(kT, t_end - (t_begin + (int64_t)c * kT));
       const bool vrow = row < valid;
-      uint32_t kw[8], qw[8];
+      uint32_t kw[8];
       const uint32_t kt = sb + kOffK + sq * kQBytes;
       ld_shared_v4(kt + sw32_offset(row, 0), kw[0], kw[1], kw[2], kw[3]);
       ld_shared_v4(kt + sw32_offset(row, 1), kw[4], kw[5], kw[6], kw[7]);
-      if (!kStateOnly) {
-        const uint32_t qt = sb + kOffQ + sq * kQBytes;
-        ld_shared_v4(qt + sw32_offset(row, 0), qw[0], qw[1], qw[2], qw[3]);
-        ld_shared_v4(qt + sw32_offset(row, 1), qw[4], qw[5], qw[6], qw[7]);
-      }
       // phi(K) into buffer c&1 once the update of tile c-2 has read it
       if (c >= 2) mbar_wait(&bars[kUpDone0 + s], ((c >> 1) - 1) & 1, abort_flag);
       named_barrier_sync(1, 128);
@@ -615,37 +634,45 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       named_barrier_sync(1, 128);
       if (leader) {
         mbar_arrive(&bars[kPhiKReady0 + s]);
-        // kw has been consumed (and, in the state pass, the stage is done):
-        // the next TMA copy may overwrite it
+        // kw has been consumed; in the state pass the stage is done with
         if (kStateOnly) mbar_arrive(&bars[kQKEmpty + sq]);
       }
       LA_TRACE_AT(1, c, 1);
-      if (!kStateOnly) {
-        // phi(Q) -> TMEM once phi(Q) S of the previous tile has read it
-        if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
-        named_barrier_sync(1, 128);
-        tc_fence_after();
-        LA_TRACE_AT(1, c, 5);
-        FeatIn fs;
+    };
+    auto do_phiq = [&](int c) {
+      const int sq = c % kQKStages;  // Q/K stage (still holds Q of tile c)
+      uint32_t qw[8];
+      const uint32_t qt = sb + kOffQ + sq * kQBytes;
+      ld_shared_v4(qt + sw32_offset(row, 0), qw[0], qw[1], qw[2], qw[3]);
+      ld_shared_v4(qt + sw32_offset(row, 1), qw[4], qw[5], qw[6], qw[7]);
+      // phi(Q) -> TMEM once phi(Q) S of the previous tile has read it
+      if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
+      named_barrier_sync(1, 128);
+      tc_fence_after();
+      LA_TRACE_AT(1, c, 5);
+      FeatIn fs;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          fs.w[i] = qw[i];
-          fs.s16[i] = hmul2_bf16(qw[i], 0x3D803D80u);  // x / 16  (exact)
-          fs.s32[i] = hmul2_bf16(qw[i], 0x3D003D00u);  // x / 32  (exact)
-        }
-        fs.one = 0x3F80u;
-        store_phiq(fs, taddr(tmem, wq * 32, kColPhiQ), std::make_integer_sequence<int, kFPad / 32>{});
-        tmem_wait_st();
-        LA_TRACE_AT(1, c, 6);
-        tc_fence_before();
-        fence_proxy_async_smem();
-        named_barrier_sync(1, 128);
-        if (leader) {
-          mbar_arrive(&bars[kPhiQReady]);
-          mbar_arrive(&bars[kQKEmpty + sq]);  // qw consumed too: release the stage
-        }
-        LA_TRACE_AT(1, c, 2);
+      for (int i = 0; i < 8; ++i) {
+        fs.w[i] = qw[i];
+        fs.s16[i] = hmul2_bf16(qw[i], 0x3D803D80u);  // x / 16  (exact)
+        fs.s32[i] = hmul2_bf16(qw[i], 0x3D003D00u);  // x / 32  (exact)
       }
+      fs.one = 0x3F80u;
+      store_phiq(fs, taddr(tmem, wq * 32, kColPhiQ), std::make_integer_sequence<int, kFPad / 32>{});
+      tmem_wait_st();
+      LA_TRACE_AT(1, c, 6);
+      tc_fence_before();
+      named_barrier_sync(1, 128);
+      if (leader) {
+        mbar_arrive(&bars[kPhiQReady]);
+        mbar_arrive(&bars[kQKEmpty + sq]);  // Q and K of tile c consumed: release the stage
+      }
+      LA_TRACE_AT(1, c, 2);
+    };
+    if (n_chunks > 0) do_phik(0);
+    for (int c = 0; c < n_chunks; ++c) {
+      if (c + 1 < n_chunks) do_phik(c + 1);
+      if (!kStateOnly) do_phiq(c);
     }
   } else if (warp < kWarpEpi) {
     // ------------------------------------------------------------ polynomial
@@ -653,7 +680,6 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       const int wq = warp & 3;              // TMEM lane quarter: query rows 32wq ..
       const int half = (warp - kWarpPoly) >> 2;  // this warp's key groups: G = half, half + 2
       const int row = wq * 32 + lane;
-      const bool leader = (warp == kWarpPoly && lane == 0);
       const uint64_t c32 = f2pack(0.03125f, 0.03125f), c4 = f2pack(0.25f, 0.25f);
       const uint64_t one2 = f2pack(1.f, 1.f);
       for (int c = 0; c < n_chunks; ++c) {
@@ -701,11 +727,12 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
             LA_TRACE_AT(2, c, 3);
           }
           tmem_st16(taddr(tmem, wq * 32, kColSc + 16 * G), w);
+          // this quarter's half of P (keys 64 G2 .. 64 G2 + 63) is in TMEM
+          tmem_wait_st();
+          tc_fence_before();
+          named_barrier_sync(5 + wq, 64);
+          if (half == 0 && lane == 0) mbar_arrive(&bars[G2 ? kPReadyHi : kPReadyLo]);
         }
-        tmem_wait_st();
-        tc_fence_before();
-        named_barrier_sync(2, 256);
-        if (leader) mbar_arrive(&bars[kPReady]);
         LA_TRACE_AT(2, c, 1);
       }
     }
@@ -728,6 +755,9 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     const float *head_b =
         !kStateOnly && g > 0 ? p.seg_states + ((uint64_t)bh * p.segments + (g - 1)) * kF * kSV
                              : nullptr;
+    // the seeds may come from the kernels launched just before this one on
+    // the stream (state pass, running sums), which this grid may overlap
+    if (!kStateOnly) grid_dependency_wait();
     if (leader) {  // the seeds, into L2 while the first group's loads are in flight
       if (head_a) prefetch_l2(head_a, sizeof(float) * kF * kSV);
       if (head_b) prefetch_l2(head_b, sizeof(float) * kF * kSV);
@@ -1002,9 +1032,12 @@ bool make_map(CUtensorMap *map, const void *base, int64_t bh, int64_t n, int d,
   return make_tmap_3d(map, base, bh, n, d, kT, swz);
 }
 
+// pdl: launched as the programmatic dependent of the kernel before it on the
+// stream (this library's state pass or running sums): its CTAs may start
+// while that kernel drains and wait only where they read the seeds.
 template <bool kStateOnly>
 int launch(const void *q, const void *k, const void *v, const Params &p, int64_t bh, int n_launch,
-           cudaStream_t s) {
+           bool pdl, cudaStream_t s) {
   if (bh > 65535 || p.n > INT32_MAX) return LA_ERR_UNSUPPORTED;
   CUtensorMap mq, mk, mv;
   if (!make_map(&mk, k, bh, p.n, kDqk, CU_TENSOR_MAP_SWIZZLE_32B) ||
@@ -1020,7 +1053,21 @@ int launch(const void *q, const void *k, const void *v, const Params &p, int64_t
     return LA_ERR_CUDA;
   const dim3 grid = (!kStateOnly && p.lead_len > 0) ? dim3((unsigned)bh, 2u)
                                                    : dim3((unsigned)n_launch, (unsigned)bh);
-  chunked_tc_kernel<kStateOnly><<<grid, kThreads, kSmemAlloc, s>>>(mq, mk, mv, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemAlloc;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, chunked_tc_kernel<kStateOnly>, mq, mk, mv, p) != cudaSuccess) {
+    note_launch();
+    cudaGetLastError();
+    return LA_ERR_CUDA;
+  }
   return check_launch();
 }
 
@@ -1050,14 +1097,14 @@ int launch_chunked_state_tc(const void *k, const void *v, float *seg_states, int
   p.seg_len = seg_len;
   p.segments = segments;
   if (!p.err) return LA_ERR_CUDA;
-  return launch<true>(nullptr, k, v, p, bh, n_launch, s);
+  return launch<true>(nullptr, k, v, p, bh, n_launch, false, s);
 }
 
 int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *out,
                              const float *init_state, float *final_state,
                              const float *seg_states, int64_t bh, int64_t n, float eps,
                              bool normalize, int segments, int64_t seg_len, int64_t lead_len,
-                             const DeviceInfo &info, cudaStream_t s) {
+                             bool after_own_kernel, const DeviceInfo &info, cudaStream_t s) {
   (void)info;
   Params p{};
   p.out = (__nv_bfloat16 *)out;
@@ -1072,7 +1119,7 @@ int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *
   p.eps = eps;
   p.normalize = normalize ? 1 : 0;
   if (!p.err) return LA_ERR_CUDA;
-  return launch<false>(q, k, v, p, bh, segments, s);
+  return launch<false>(q, k, v, p, bh, segments, after_own_kernel, s);
 }
 
 }  // namespace la

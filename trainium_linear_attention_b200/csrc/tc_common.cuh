@@ -140,6 +140,19 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// Programmatic dependent launch.  A kernel launched as the dependent of the
+// kernel before it on the stream may start while that kernel still runs; it
+// calls grid_dependency_wait() before reading anything that kernel wrote.
+// grid_dependents_launch() lets this kernel's dependent be scheduled (its
+// CTAs then take SMs as this kernel's CTAs leave).  Both are no-ops for a
+// kernel launched without such a dependency.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------------- fences ---
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -370,6 +383,11 @@ __device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t &a, uint32_
 // region whose rows are 128 bytes and whose 8-row atoms are 1024 bytes apart.
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t chunk) {
   return (row >> 3) * 1024u + (row & 7u) * 128u + (((chunk ^ row) & 7u) << 4);
+}
+// Same for 64B swizzle with 64-byte rows (four 16-byte chunks per row; the
+// pattern repeats every 8 rows = 512 bytes).
+__device__ __forceinline__ uint32_t sw64_offset(uint32_t row, uint32_t chunk) {
+  return row * 64u + (((chunk ^ (row >> 1)) & 3u) << 4);
 }
 // Same for 32B swizzle with 32-byte rows (two 16-byte chunks per row).
 __device__ __forceinline__ uint32_t sw32_offset(uint32_t row, uint32_t chunk) {

@@ -32,7 +32,7 @@ int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *
                              const float *init_state, float *final_state,
                              const float *seg_states, int64_t bh, int64_t n, float eps,
                              bool normalize, int segments, int64_t seg_len, int64_t lead_len,
-                             const DeviceInfo &info, cudaStream_t s);
+                             bool after_own_kernel, const DeviceInfo &info, cudaStream_t s);
 
 // Windows the tensor-core sliding kernel handles (W <= 129 at head_dim 64).
 bool sliding_tc_supported(int64_t window);
@@ -45,6 +45,6 @@ int launch_sliding_tc(const void *q, const void *k, const void *v, void *out, in
 // not null) receives the sum of all groups * ratio slots.  Fixed order,
 // deterministic.
 int launch_prefix_segments(float *seg, float *total, int64_t bh, int stride, int groups,
-                           int ratio, int64_t per_head, cudaStream_t s);
+                           int ratio, int64_t per_head, cudaStream_t s, bool pdl = false);
 
 }  // namespace la

@@ -7,6 +7,10 @@ c3   sliding-window softmax attention, B=4, H=16, N=4096, d=64, W=64 (config 3)
 c5   parallel and chunked BASED at B*N = 262144, H=16, N = 512 .. 65536 (by
      default; --c5-min-n / --c5-max-n): the crossover that ``solution()``
      dispatches on (config 5)
+ident   chunked identity-feature-map numerator, B=4, H=16, N=2048, d_qk=16, d_v=64
+d64     chunked BASED at d_qk = d_v = 64 (F = 2145, cluster kernels), B=1, H=16, N=4096
+layer   the full BASED layer (chunked BASED + sliding window W=64 in one pass):
+        B=4, H=16, N=2048, d_qk=16, d_v=64, and at d_qk = d_v = 64, B=1, H=16, N=4096
 
 All inputs are bf16, iid N(0,1) * scale (0.5 for BASED, 1 for sliding),
 generated on the device from a fixed seed.  Each point: warm-up calls, then
@@ -86,7 +90,7 @@ def line(name, op, b, h, n, dqk, dv, ms, steps, bytes_per_token, flop_per_token,
 def main():
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--what", default="c2,c3,c5")
+    ap.add_argument("--what", default="c2,c3,c5,ident,d64,layer")
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--c5-min-n", type=int, default=512)
     ap.add_argument("--c5-max-n", type=int, default=65536)
@@ -105,6 +109,26 @@ def main():
         ms, st = time_calls(lambda: ops.sliding_window(q, k, v, window_size=w), args.steps)
         line("c3", "sliding", b, h, n, d, d, ms, st, h * (3 * d * 2 + d * 2), h * w * 4 * d,
              {"window": w})
+    if "ident" in what:
+        b, n = 4, 2048
+        q, k, v = inputs(b, h, n, dqk, dv, 0.5)
+        ms, st = time_calls(lambda: ops.based_chunked(q, k, v, normalize=False,
+                                                      feature_map="identity"), args.steps)
+        line("ident", "chunked_identity", b, h, n, dqk, dv, ms, st, based_bytes, None)
+    if "d64" in what:
+        b, n, d = 1, 4096, 64
+        q, k, v = inputs(b, h, n, d, d, 0.5)
+        ms, st = time_calls(lambda: ops.based_chunked(q, k, v), args.steps)
+        f = 1 + d + d * (d + 1) // 2
+        line("d64", "chunked_cluster", b, h, n, d, d, ms, st, h * (4 * d * 2),
+             h * (4 * f * (d + 1) + (64 + 1) / 2 * (2 * d + 2 * d + 4)))
+    if "layer" in what:
+        for b, n, d_qk, d_v in ((4, 2048, 16, 64), (1, 4096, 64, 64)):
+            q, k, v = inputs(b, h, n, d_qk, d_v, 0.5)
+            ms, st = time_calls(lambda: ops.based_layer(q, k, v, window_size=64), args.steps)
+            line("layer", "based_plus_sliding", b, h, n, d_qk, d_v, ms, st,
+                 h * ((2 * d_qk + d_v) * 2 + d_v * 2), None, {"window": 64})
+            del q, k, v
     if "c5" in what:
         n = args.c5_min_n
         while n <= args.c5_max_n:
