@@ -13,9 +13,11 @@ sequence-parallel variant (B=1, H=16, N=262144 split over the ranks, one
 NCCL all-gather of per-rank states per step).
 
 Timing: W untimed warm-up steps, then exactly K steps, each bracketed by CUDA
-events on the launching stream; L2 is flushed (256 MB write) before every
-timed step, outside the events; the per-rank sum is max-reduced over ranks
-after a barrier.  ``value`` = B*N tokens (heads not counted, the reference's
+events on the launching stream; the per-rank sum is max-reduced over ranks
+after a barrier.  L2: a step streams 1.34 GB (config 4) through the 126 MB
+L2, so no data of a step survives to the next; ``--l2 flush`` additionally
+writes a 256 MB buffer before every timed step (outside the events; its dirty
+lines are then written back during the step).  ``value`` = B*N tokens (heads not counted, the reference's
 convention) / that time.  ``e2e`` repeats the measurement through the public
 API with pinned host inputs copied in and the output copied back every step
 (heads mode: ``based_chunked_host``, which copies one group of heads while
@@ -66,6 +68,9 @@ def parse_args():
     ap.add_argument("--e2e-groups", type=int, default=8,
                     help="head groups of the end-to-end leg (copies overlap the kernels)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--l2", choices=["none", "flush"], default="none",
+                    help="none: the inputs (1.34 GB per step) exceed L2; flush: also write 256 MB "
+                         "before every timed step")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -247,7 +252,9 @@ def config_dict(args, b, h, n, dqk, dv):
             "global_batch": b, "parallelism": (f"heads{args.gpus}" if args.mode == "heads"
                                                else f"sp{args.gpus}"),
             "inputs": "iid N(0,1)*0.5, seeded, bf16 (the reference arm: fp32 numpy sample)",
-            "l2": "flushed (256 MB write) before every timed step"}
+            "l2": ("flushed (256 MB write) before every timed step" if args.l2 == "flush" else
+                   "not flushed: a rank's step reads and writes its share of config 4's "
+                   "1.34 GB (>= 168 MB at 8 GPUs), more than the 126 MB L2")}
 
 
 # --------------------------------------------------------------------------- our arm
@@ -331,7 +338,8 @@ def run_ours(args):
             sp_sums[key] = 0.0 if key != "steps" else 0
     with ClockSampler(local) as clk:
         for i in range(args.steps):
-            flush.zero_()
+            if args.l2 == "flush":
+                flush.zero_()
             starts[i].record(stream)
             step()
             ends[i].record(stream)

