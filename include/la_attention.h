@@ -108,7 +108,10 @@ int la_based_parallel_fwd(const void *q, const void *k, const void *v, void *out
  *
  * With LA_CHUNKED_IDENTITY the feature map is the identity (the reference's
  * ref_identity_numerator): phi_k(k) = k, phi_q(q) = q / sqrt(d_qk), F = d_qk,
- * and only the numerator is returned (NORMALIZE is rejected).
+ * and only the numerator is returned (NORMALIZE is rejected).  Either map
+ * runs on the tcgen05 tensor-core kernel for bf16 inputs with d_qk = 16,
+ * d_v = 64 (q/k/v 16-byte, out 32-byte aligned); other shapes compute in
+ * fp32 on CUDA cores (d_qk = 64 on a thread-block cluster).
  *
  * State layout (init_state / final_state / la_based_chunked_state): fp32
  * (batch*heads, F, d_v + 1) in the key-side feature basis
@@ -187,11 +190,16 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out,
  *     out = based(q, k, v, eps) + sliding_window(q, k, v, window),
  * the composition the reference states at kernels/nki_attention_sliding.py:
  * 4-5 (and whose two halves its module wrapper benchmarks/
- * based_attention_benchmark.py:24-69 would call separately), computed in one
- * pass over q, k and v: each chunk's keys and values serve the chunked
- * recurrence and, kept on chip, the windows of the next two chunks
- * (window <= 129); states too wide for one CTA (d_qk = 64) are split over a
- * thread-block cluster as in la_based_chunked_fwd.  The sliding half uses the
+ * based_attention_benchmark.py:24-69 would call separately).  bf16 inputs
+ * with d_qk = 16, d_v = 64 and window <= 129 (aligned as for the chunked
+ * tensor-core path) run two tensor-core kernels: the chunked kernel writes
+ * the normalised BASED term to out, then the sliding-window kernel adds its
+ * term in fp32 before the one rounding to bf16 (q, k and v are read twice).
+ * Other shapes run in one pass over q, k and v on CUDA cores: each chunk's
+ * keys and values serve the chunked recurrence and, kept on chip, the
+ * windows of the next two chunks (window <= 129); states too wide for one CTA
+ * (d_qk = 64) are split over a thread-block cluster as in
+ * la_based_chunked_fwd.  The sliding half uses the
  * same scale 1/sqrt(d_qk), the window [i - W + 1, i] and fp32 softmax
  * accumulation.  segments and the
  * workspace work as for la_based_chunked_fwd (la_based_chunked_plan sizes

@@ -429,8 +429,11 @@ def test_layer_fp32_golden(golden, case):
 
 @pytest.mark.parametrize("t,w,segments", [(1, 64, 0), (65, 64, 0), (1000, 64, 0), (2048, 64, 0),
                                           (3000, 129, 3), (700, 1, 0), (300, 129, 0),
-                                          (129, 500, 0)])
+                                          (129, 500, 0), (4100, 65, 0), (4100, 66, 2)])
 def test_layer_bf16(t, w, segments):
+    """bf16, d_qk = 16, d_v = 64: the chunked tensor-core kernel, then the
+    sliding kernel adding the window term (spans of 192 keys for W <= 65, 256
+    above)."""
     q, k, v = inputs((2, 4, t, 16), 64, seed=700 + t + w)
     if w > 129:
         with pytest.raises(RuntimeError):
@@ -578,6 +581,27 @@ def test_identity_state_roundtrip():
     assert O.rel_l2(np64(torch.cat([a, b], 2)), want) <= TOL_FP32
     with pytest.raises(ValueError):
         ops.based_chunked(q, k, v, feature_map="identity")  # normalised identity: rejected
+
+
+@pytest.mark.parametrize("heads,t", [(2, 900), (100, 8192)])
+def test_identity_bf16_tensor_core_state(heads, t):
+    """The identity map on the tensor-core kernel (bf16, d_qk = 16, d_v = 64):
+    output and final state against the chunked restatement, and a split at a
+    token boundary seeded with the first half's state.  100 heads of 8192
+    tokens take the lead/main split (a state pass over each head's lead)."""
+    q, k, v = inputs((1, heads, t, 16), 64, seed=78 + heads)
+    qd, kd, vd = cuda(q, k, v)
+    y, s = ops.based_chunked(qd, kd, vd, normalize=False, feature_map="identity",
+                             return_state=True)
+    want, s_want = O.identity_chunked(np64(q), np64(k), np64(v), return_state=True)
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+    assert O.rel_l2(s.double().cpu().numpy(), s_want.reshape(heads, 16, 65)) <= 1e-4
+    h = t // 2
+    a, sa = ops.based_chunked(qd[:, :, :h], kd[:, :, :h], vd[:, :, :h], normalize=False,
+                              feature_map="identity", return_state=True)
+    b = ops.based_chunked(qd[:, :, h:], kd[:, :, h:], vd[:, :, h:], normalize=False,
+                          feature_map="identity", init_state=sa)
+    assert O.rel_l2(np64(torch.cat([a, b], 2)), want) <= TOL_BF16
 
 
 # ------------------------------------------------------------ traced dispatch ---

@@ -239,7 +239,7 @@ int plan_chunked_fwd(const void *q, const void *k, const void *v, const void *ou
   ChunkedFwdPlan p;
   p.identity = (flags & LA_CHUNKED_IDENTITY) != 0;
   p.features = p.identity ? d_qk : feature_dim(d_qk);
-  p.tc = !p.identity && use_tensor_cores(dtype, d_qk, d_v) && aligned16(q) && aligned16(k) &&
+  p.tc = use_tensor_cores(dtype, d_qk, d_v) && aligned16(q) && aligned16(k) &&
          aligned16(v) && aligned32(out);
   if (!p.tc && !chunked_simt_supported(p.features, d_qk, d_v)) {
     if (p.identity || !cluster_chunked_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
@@ -415,11 +415,12 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
   const bool normalize = (flags & LA_CHUNKED_NORMALIZE) != 0;
   if (plan.lead > 0) {
     float *lead_states = (float *)workspace;
-    st = launch_chunked_state_tc(k, v, lead_states, bh, seq_len, 1, 1, plan.lead, info, s);
+    st = launch_chunked_state_tc(k, v, lead_states, bh, seq_len, 1, 1, plan.lead, plan.identity,
+                                 info, s);
     if (st != LA_OK) return st;
     return launch_chunked_output_tc(q, k, v, out, init_state, final_state, lead_states, bh,
-                                    seq_len, eps, normalize, 1, seq_len, plan.lead, true, info,
-                                    s);
+                                    seq_len, eps, normalize, plan.identity, 1, seq_len, plan.lead,
+                                    true, info, s);
   }
   const int g = plan.g;
   float *seg_states = g > 1 ? (float *)workspace : nullptr;
@@ -430,7 +431,8 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
     // slot g - 1 seeds segment g
     st = plan.tc        ? launch_chunked_state_tc(k, v, seg_states, bh, seq_len, g,
                                                   (g - 1) * plan.ratio,
-                                                  plan.seg_len / plan.ratio, info, s)
+                                                  plan.seg_len / plan.ratio, plan.identity, info,
+                                                  s)
          : plan.cluster ? launch_chunked_state_cluster(k, v, seg_states, bh, seq_len, (int)d_qk,
                                                        (int)d_v, dtype, g, g - 1, plan.seg_len,
                                                        s)
@@ -446,7 +448,7 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
   const bool after_state_pass = g > 1 && !(flags & LA_CHUNKED_REUSE_SEGMENTS);
   if (plan.tc)
     return launch_chunked_output_tc(q, k, v, out, init_state, final_state, seg_states, bh,
-                                    seq_len, eps, normalize, g, plan.seg_len, 0,
+                                    seq_len, eps, normalize, plan.identity, g, plan.seg_len, 0,
                                     after_state_pass, info, s);
   if (plan.cluster)
     return launch_chunked_output_cluster(q, k, v, out, init_state, final_state, seg_states, bh,
@@ -466,6 +468,21 @@ int la_based_layer_fwd(const void *q, const void *k, const void *v, void *out, i
   if (window < 1 || segments < 0) return LA_ERR_INVALID_ARGUMENT;
   const int64_t bh = batch * heads;
   if (bh == 0 || seq_len == 0) return LA_OK;
+  // Tensor-core shape (bf16, d_qk = 16, d_v = 64, window <= 129): the chunked
+  // kernel writes the normalised BASED term, then the sliding kernel adds the
+  // window term to it in its epilogue (q, k and v are read twice; on CUDA
+  // cores one pass is slower by far).
+  if (use_tensor_cores(dtype, d_qk, d_v) && sliding_tc_supported(window) && aligned16(q) &&
+      aligned16(k) && aligned16(v) && aligned32(out)) {
+    st = la_based_chunked_fwd(q, k, v, out, batch, heads, seq_len, d_qk, d_v, dtype, 64, eps,
+                              LA_CHUNKED_NORMALIZE, nullptr, nullptr, workspace, workspace_bytes,
+                              segments, stream);
+    if (st != LA_OK) return st;
+    DeviceInfo info;
+    if ((st = require_sm100(&info)) != LA_OK) return st;
+    return launch_sliding_tc(q, k, v, out, bh, seq_len, d_qk, window, out, info,
+                             (cudaStream_t)stream);
+  }
   // one CTA per (head, segment) holds the state and the window's two
   // previous chunks; wider states split over a cluster
   const bool simt = layer_simt_supported(d_qk, d_v, window);
@@ -533,7 +550,7 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
   }
   const int64_t seg_len = g > 1 ? segment_len(seq_len, g) : seq_len;
   float *dst = g > 1 ? (float *)workspace : state_out;
-  st = tc        ? launch_chunked_state_tc(k, v, dst, bh, seq_len, g, g, seg_len, info, s)
+  st = tc        ? launch_chunked_state_tc(k, v, dst, bh, seq_len, g, g, seg_len, false, info, s)
        : cluster ? launch_chunked_state_cluster(k, v, dst, bh, seq_len, (int)d_qk, (int)d_v,
                                                 dtype, g, g, seg_len, s)
                  : launch_chunked_state_simt(k, v, dst, bh, seq_len, (int)d_qk, (int)d_v, dtype,
@@ -558,7 +575,8 @@ int la_sliding_window_fwd(const void *q, const void *k, const void *v, void *out
   if (dtype == LA_DTYPE_BFLOAT16 && head_dim == 64 &&
       sliding_tc_supported(window) && aligned16(q) && aligned16(k) && aligned16(v) &&
       aligned32(out))
-    return launch_sliding_tc(q, k, v, out, batch * heads, seq_len, window, info, s);
+    return launch_sliding_tc(q, k, v, out, batch * heads, seq_len, head_dim, window, nullptr,
+                             info, s);
   return launch_sliding_simt(q, k, v, out, batch * heads, seq_len, (int)head_dim, dtype, window,
                              s);
 }

@@ -236,6 +236,18 @@ static_assert(slot_map_is_bijection(), "every feature has exactly one slot");
 // read of constant memory per slot costs a constant-cache miss per line and
 // serialises; the copy is one coalesced load).
 __device__ const SlotMap g_slot_map = make_slot_map();
+// Identity feature map (phi(x) = x): slots 0..15 are x_0..x_15, the linear
+// pairs 0..7 of the Taylor order, and every other slot is padding.  Its state
+// keeps the d_qk features in input order.
+__host__ __device__ constexpr SlotMap make_identity_slot_map() {
+  SlotMap m{};
+  for (int s = 0; s < kFPad; ++s) m.f[s] = (short)(s < kDqk ? s : -1);
+  return m;
+}
+__device__ const SlotMap g_identity_slot_map = make_identity_slot_map();
+// Feature slots the identity map uses: one 32-slot block of phi(K) (N of the
+// update), two K-steps of phi(Q) S
+constexpr int kIdSlots = 32;
 
 // A token's inputs as bf16x2 words (x_2i lo, x_2i+1 hi): raw, and (query side)
 // divided by 16 and by 32.  `one` is {1, 0}, or 0 for a padding key.
@@ -270,32 +282,44 @@ __device__ __forceinline__ uint32_t pair_val(const FeatIn &s) {
   }
 }
 
+// A feature pair under either map: the identity map keeps the linear pairs
+// (x_2i, x_2i+1; x / 4 on the query side, the 1/sqrt(d_qk) of its scores)
+// and zeroes the rest.
+template <bool kIdentity, bool kQ, int P>
+__device__ __forceinline__ uint32_t feature_pair(const FeatIn &s) {
+  if constexpr (kIdentity && pair_desc(P).type != kPairLin) return 0u;
+  else return pair_val<kQ, P>(s);
+}
+
 // Slots 8J .. 8J+7 (pairs 4J .. 4J+3, one 16-byte chunk) of token `row` ->
 // 64B-swizzled smem, 32 slots per 8 KB block: the MN-major B layout of
 // phi(K) for the update MMA.
-template <int J>
+template <bool kIdentity, int J>
 __device__ __forceinline__ void store_phik_chunk(const FeatIn &s, uint32_t base, int row) {
-  st_shared_v4(base + (J >> 2) * kPhiBlock + sw64_offset(row, J & 3), pair_val<false, 4 * J + 0>(s),
-               pair_val<false, 4 * J + 1>(s), pair_val<false, 4 * J + 2>(s),
-               pair_val<false, 4 * J + 3>(s));
+  st_shared_v4(base + (J >> 2) * kPhiBlock + sw64_offset(row, J & 3),
+               feature_pair<kIdentity, false, 4 * J + 0>(s),
+               feature_pair<kIdentity, false, 4 * J + 1>(s),
+               feature_pair<kIdentity, false, 4 * J + 2>(s),
+               feature_pair<kIdentity, false, 4 * J + 3>(s));
 }
-template <int... J>
+template <bool kIdentity, int... J>
 __device__ __forceinline__ void store_phik(const FeatIn &s, uint32_t base, int row,
                                            std::integer_sequence<int, J...>) {
-  (store_phik_chunk<J>(s, base, row), ...);
+  (store_phik_chunk<kIdentity, J>(s, base, row), ...);
 }
 
 // phi(Q) TMEM columns [16G, 16G+16) = pairs 16G .. 16G+15 of TMEM lane `row`
-template <int G, int... I>
+template <bool kIdentity, int G, int... I>
 __device__ __forceinline__ void store_phiq_group(const FeatIn &s, uint32_t addr,
                                                  std::integer_sequence<int, I...>) {
-  const uint32_t w[16] = {pair_val<true, 16 * G + I>(s)...};
+  const uint32_t w[16] = {feature_pair<kIdentity, true, 16 * G + I>(s)...};
   tmem_st16(addr, w);
 }
-template <int... G>
+template <bool kIdentity, int... G>
 __device__ __forceinline__ void store_phiq(const FeatIn &s, uint32_t addr0,
                                            std::integer_sequence<int, G...>) {
-  (store_phiq_group<G>(s, addr0 + 16 * G, std::make_integer_sequence<int, 16>{}), ...);
+  (store_phiq_group<kIdentity, G>(s, addr0 + 16 * G, std::make_integer_sequence<int, 16>{}),
+   ...);
 }
 
 // Shared-memory address of the 16-byte chunk holding features f0 .. f0+7
@@ -327,12 +351,18 @@ __device__ __forceinline__ bool wait_teardown(uint64_t *bar, uint32_t parity) {
   return true;
 }
 
-template <bool kStateOnly>
+// kIdentity: the identity feature map (numerator only): phi(K) and phi(Q)
+// hold the 16 linear slots, the update runs at N = 32, phi(Q) S at K = 32 and
+// P = tril(s / 4).
+template <bool kStateOnly, bool kIdentity>
 __global__ void __launch_bounds__(kThreads, 1)
 chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const Params p) {
   using L = Layout<kStateOnly>;
   constexpr int kQKStages = L::kQKStages, kVStages = L::kVStages;
+  // features per head in global memory, feature slots the MMAs span
+  constexpr int kFeat = kIdentity ? kDqk : kF;
+  constexpr int kSlots = kIdentity ? kIdSlots : kFPad;
   constexpr uint32_t kOffQ = L::kOffQ, kOffK = L::kOffK, kOffV = L::kOffV, kOffOnes = L::kOffOnes,
                      kOffPhiK = L::kOffPhiK, kOffSnap = L::kOffSnap, kOffBar = L::kOffBar,
                      kOffSlot = L::kOffSlot;
@@ -389,7 +419,8 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     if (kStateOnly) grid_dependents_launch();
   }
   if (threadIdx.x < kFPad / 2)
-    ((uint32_t *)(smem + kOffSlot))[threadIdx.x] = ((const uint32_t *)g_slot_map.f)[threadIdx.x];
+    ((uint32_t *)(smem + kOffSlot))[threadIdx.x] =
+        ((const uint32_t *)(kIdentity ? g_identity_slot_map.f : g_slot_map.f))[threadIdx.x];
   // constant "ones" block: A-operand rows 64..127 of [V 1 0]^T for 16 tokens;
   // row 64 (element 0 of each token row, 128B-swizzled) is 1, the rest 0.
   for (int i = threadIdx.x; i < 2048 / 4; i += kThreads) {
@@ -466,7 +497,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     constexpr uint32_t id_sc = make_idesc_bf16(128, 128, false, false);
     constexpr uint32_t id_qs = make_idesc_bf16(128, kNO, false, false);
     constexpr uint32_t id_pv = make_idesc_bf16(128, kNO, false, true);
-    constexpr uint32_t id_up = make_idesc_bf16(128, kFPad, true, true);
+    constexpr uint32_t id_up = make_idesc_bf16(128, kSlots, true, true);
     // a K-step of 16 tokens: start address +2048 B, LBO (distance to the ones block) -2048 B
     constexpr uint64_t kStep = (uint64_t)(2048 >> 4) - ((uint64_t)(2048 >> 4) << 16);
     const uint32_t a_ones = sb + kOffOnes;
@@ -547,7 +578,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         const uint64_t qs_b_desc = b ? qs_b_desc1 : qs_b_desc0;
         if (elect_one()) {
 #pragma unroll
-          for (int j = 0; j < kFPad / 16; ++j) {
+          for (int j = 0; j < kSlots / 16; ++j) {
             const uint32_t boff = (j >> 2) * kSnapKBlock + (j & 3) * 32;
             umma_ts(tmem + kColO, tmem + kColPhiQ + 8 * j, qs_b_desc + (boff >> 4), id_qs,
                     j > 0 ? 1u : 0u);
@@ -627,7 +658,8 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
 #pragma unroll
         for (int i = 0; i < 8; ++i) fk.w[i] = vrow ? kw[i] : 0u;
         fk.one = vrow ? 0x3F80u : 0u;  // padding tokens add nothing to the state
-        store_phik(fk, sb + kOffPhiK + s * kPhiBytes, row, std::make_integer_sequence<int, kFPad / 8>{});
+        store_phik<kIdentity>(fk, sb + kOffPhiK + s * kPhiBytes, row,
+                              std::make_integer_sequence<int, kSlots / 8>{});
       }
       LA_TRACE_AT(1, c, 4);
       fence_proxy_async_smem();
@@ -658,7 +690,8 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         fs.s32[i] = hmul2_bf16(qw[i], 0x3D003D00u);  // x / 32  (exact)
       }
       fs.one = 0x3F80u;
-      store_phiq(fs, taddr(tmem, wq * 32, kColPhiQ), std::make_integer_sequence<int, kFPad / 32>{});
+      store_phiq<kIdentity>(fs, taddr(tmem, wq * 32, kColPhiQ),
+                            std::make_integer_sequence<int, kSlots / 32>{});
       tmem_wait_st();
       LA_TRACE_AT(1, c, 6);
       tc_fence_before();
@@ -680,8 +713,10 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       const int wq = warp & 3;              // TMEM lane quarter: query rows 32wq ..
       const int half = (warp - kWarpPoly) >> 2;  // this warp's key groups: G = half, half + 2
       const int row = wq * 32 + lane;
-      const uint64_t c32 = f2pack(0.03125f, 0.03125f), c4 = f2pack(0.25f, 0.25f);
-      const uint64_t one2 = f2pack(1.f, 1.f);
+      // Taylor: p = 1 + s/4 + s^2/32; identity: p = s/4 (= s * (0 s + 1/4) + 0, exact)
+      const uint64_t c32 = kIdentity ? f2pack(0.f, 0.f) : f2pack(0.03125f, 0.03125f);
+      const uint64_t c4 = f2pack(0.25f, 0.25f);
+      const uint64_t one2 = kIdentity ? f2pack(0.f, 0.f) : f2pack(1.f, 1.f);
       for (int c = 0; c < n_chunks; ++c) {
         const int64_t t0 = t_begin + (int64_t)c * kT;
         const int valid = (int)min64(kT, t_end - t0);
@@ -750,17 +785,17 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     // The seed is init_state + the prefix slot g - 1; the 32 loads of a
     // group of 16 columns are independent and issued together.
     LA_TRACE_AT(3, 0, 3);
-    const float *head_a = !kStateOnly && p.init_state ? p.init_state + (uint64_t)bh * kF * kSV
-                                                      : nullptr;
+    const float *head_a =
+        !kStateOnly && p.init_state ? p.init_state + (uint64_t)bh * kFeat * kSV : nullptr;
     const float *head_b =
-        !kStateOnly && g > 0 ? p.seg_states + ((uint64_t)bh * p.segments + (g - 1)) * kF * kSV
+        !kStateOnly && g > 0 ? p.seg_states + ((uint64_t)bh * p.segments + (g - 1)) * kFeat * kSV
                              : nullptr;
     // the seeds may come from the kernels launched just before this one on
     // the stream (state pass, running sums), which this grid may overlap
     if (!kStateOnly) grid_dependency_wait();
     if (leader) {  // the seeds, into L2 while the first group's loads are in flight
-      if (head_a) prefetch_l2(head_a, sizeof(float) * kF * kSV);
-      if (head_b) prefetch_l2(head_b, sizeof(float) * kF * kSV);
+      if (head_a) prefetch_l2(head_a, sizeof(float) * kFeat * kSV);
+      if (head_b) prefetch_l2(head_b, sizeof(float) * kFeat * kSV);
     }
     // Loads are unconditional (padding slots read feature 0 and are zeroed
     // after), so that all 32 of a group are in flight together.
@@ -824,7 +859,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       named_barrier_sync(3, kStateThreads);
       {
         tc_fence_after();
-        float *dst = p.seg_out + ((uint64_t)bh * p.segments + g) * kF * kSV;
+        float *dst = p.seg_out + ((uint64_t)bh * p.segments + g) * kFeat * kSV;
         for (int grp = 0; grp < 5; ++grp) {
           uint32_t r[16], r2[16];
           tmem_ld16(taddr(tmem, wq * 32, kColS + col0 + 16 * grp), r);
@@ -858,7 +893,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         }
       };
       auto put_final = [&](int f0, const uint32_t *r) {
-        float *dst = p.final_state + (uint64_t)bh * kF * kSV;
+        float *dst = p.final_state + (uint64_t)bh * kFeat * kSV;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int f = slot_map[f0 + i];
@@ -894,24 +929,28 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         // TMEM load has landed, before the last group is stored.
         if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
         {
+          // groups of 16 columns that carry features: all 5 of each warp's 80
+          // (Taylor); the first 2 of the column-0 warps (identity)
+          constexpr int kGroups = kIdentity ? kIdSlots / 16 : 5;
+          const bool active = !kIdentity || col0 == 0;
           const uint32_t snap = sb + kOffSnap + ((c + 1) & 1) * kSnapBytes;
           const uint32_t base = taddr(tmem, wq * 32, kColS + col0);
           uint32_t r0[16], r1[16];
-          tmem_ld16(base, r0);
+          if (active) tmem_ld16(base, r0);
 #pragma unroll
-          for (int grp = 0; grp < 5; ++grp) {
+          for (int grp = 0; grp < kGroups; ++grp) {
             uint32_t *cur = (grp & 1) ? r1 : r0;
             uint32_t *nxt = (grp & 1) ? r0 : r1;
-            tmem_wait_ld();
-            if (grp + 1 < 5) {
-              tmem_ld16(base + 16 * (grp + 1), nxt);
+            if (active) tmem_wait_ld();
+            if (grp + 1 < kGroups) {
+              if (active) tmem_ld16(base + 16 * (grp + 1), nxt);
             } else {
               tc_fence_before();
               named_barrier_sync(3, kStateThreads);
               if (leader) mbar_arrive(&bars[kSRead]);
               LA_TRACE_AT(3, c, 6);
             }
-            put(snap, col0 + 16 * grp, cur);
+            if (active) put(snap, col0 + 16 * grp, cur);
           }
         }
         LA_TRACE_AT(3, c, 7);
@@ -1035,7 +1074,7 @@ bool make_map(CUtensorMap *map, const void *base, int64_t bh, int64_t n, int d,
 // pdl: launched as the programmatic dependent of the kernel before it on the
 // stream (this library's state pass or running sums): its CTAs may start
 // while that kernel drains and wait only where they read the seeds.
-template <bool kStateOnly>
+template <bool kStateOnly, bool kIdentity>
 int launch(const void *q, const void *k, const void *v, const Params &p, int64_t bh, int n_launch,
            bool pdl, cudaStream_t s) {
   if (bh > 65535 || p.n > INT32_MAX) return LA_ERR_UNSUPPORTED;
@@ -1049,7 +1088,8 @@ int launch(const void *q, const void *k, const void *v, const Params &p, int64_t
     return LA_ERR_CUDA;
   }
   constexpr uint32_t kSmemAlloc = Layout<kStateOnly>::kSmemAlloc;
-  if (allow_dynamic_smem((const void *)chunked_tc_kernel<kStateOnly>, (int)kSmemAlloc) != LA_OK)
+  if (allow_dynamic_smem((const void *)chunked_tc_kernel<kStateOnly, kIdentity>, (int)kSmemAlloc) !=
+      LA_OK)
     return LA_ERR_CUDA;
   const dim3 grid = (!kStateOnly && p.lead_len > 0) ? dim3((unsigned)bh, 2u)
                                                    : dim3((unsigned)n_launch, (unsigned)bh);
@@ -1063,7 +1103,8 @@ int launch(const void *q, const void *k, const void *v, const Params &p, int64_t
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, chunked_tc_kernel<kStateOnly>, mq, mk, mv, p) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, chunked_tc_kernel<kStateOnly, kIdentity>, mq, mk, mv, p) !=
+      cudaSuccess) {
     note_launch();
     cudaGetLastError();
     return LA_ERR_CUDA;
@@ -1087,7 +1128,7 @@ extern "C" int la_debug_read_cta_trace(long long *dst, int count) {
 #endif
 
 int launch_chunked_state_tc(const void *k, const void *v, float *seg_states, int64_t bh,
-                            int64_t n, int segments, int n_launch, int64_t seg_len,
+                            int64_t n, int segments, int n_launch, int64_t seg_len, bool identity,
                             const DeviceInfo &info, cudaStream_t s) {
   (void)info;
   Params p{};
@@ -1097,14 +1138,16 @@ int launch_chunked_state_tc(const void *k, const void *v, float *seg_states, int
   p.seg_len = seg_len;
   p.segments = segments;
   if (!p.err) return LA_ERR_CUDA;
-  return launch<true>(nullptr, k, v, p, bh, n_launch, false, s);
+  return identity ? launch<true, true>(nullptr, k, v, p, bh, n_launch, false, s)
+                  : launch<true, false>(nullptr, k, v, p, bh, n_launch, false, s);
 }
 
 int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *out,
                              const float *init_state, float *final_state,
                              const float *seg_states, int64_t bh, int64_t n, float eps,
-                             bool normalize, int segments, int64_t seg_len, int64_t lead_len,
-                             bool after_own_kernel, const DeviceInfo &info, cudaStream_t s) {
+                             bool normalize, bool identity, int segments, int64_t seg_len,
+                             int64_t lead_len, bool after_own_kernel, const DeviceInfo &info,
+                             cudaStream_t s) {
   (void)info;
   Params p{};
   p.out = (__nv_bfloat16 *)out;
@@ -1119,7 +1162,9 @@ int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *
   p.eps = eps;
   p.normalize = normalize ? 1 : 0;
   if (!p.err) return LA_ERR_CUDA;
-  return launch<false>(q, k, v, p, bh, segments, after_own_kernel, s);
+  if (identity && normalize) return LA_ERR_UNSUPPORTED;  // the identity map has no normaliser
+  return identity ? launch<false, true>(q, k, v, p, bh, segments, after_own_kernel, s)
+                  : launch<false, false>(q, k, v, p, bh, segments, after_own_kernel, s);
 }
 
 }  // namespace la

@@ -1,16 +1,17 @@
 // Sliding-window causal softmax attention on tcgen05 tensor cores (sm_100a).
 //
-// Fast path: bf16 q/k/v, head_dim 64, window W <= 129.  A tile is one
-// (head, 128-query block).  Its queries [q0, q0+128) see keys
+// Fast path: bf16 q/k/v, d_qk 64 or 16, d_v 64, window W <= 129.  A tile is
+// one (head, 128-query block).  Its queries [q0, q0+128) see keys
 // [q0 - W + 1, q0 + 127], which fit in one span of kSpan keys starting at
 // k0 = q0 + 128 - kSpan (192 keys for W <= 65, 256 for W <= 129):
 //
-//   S   = Q K^T          tcgen05 M=128 N=kSpan K=64   -> TMEM (fp32)
-//   P   = exp(S/8 - m)   CUDA cores (as 2^x, ex2.approx), row max m over the
+//   S   = Q K^T          tcgen05 M=128 N=kSpan K=d_qk -> TMEM (fp32)
+//   P   = exp(S/sqrt(d_qk) - m)  CUDA cores (as 2^x, ex2.approx), row max m over the
 //                        row's window, masked to [max(0, i-W+1), i]; bf16 P
 //                        written over S
 //   O   = P V            tcgen05 M=128 N=64 K=kSpan   (A = P in TMEM)
-//   out = O / sum(P)
+//   out = O / sum(P)  [+ addend: the BASED layer adds the window term to the
+//                      chunked kernel's output, read in the epilogue]
 //
 // which is ref_sliding_window_attn (benchmarks/sliding_attention_benchmark.py:
 // 32-56) and the NKI kernel of kernels/nki_attention_sliding.py:30-132
@@ -39,17 +40,30 @@ namespace {
 using namespace tc;
 
 constexpr int kT = 128;  // queries per tile
-constexpr int kD = 64;   // head dim
-constexpr int kMaxStages = 3;
+constexpr int kD = 64;   // value head dim
+constexpr int kMaxStages = 6;
 constexpr int kThreadsSl = 14 * 32;
+constexpr uint32_t kStageOverhead = 256 + 2 * kT * 4 + 1024;  // barriers, row sums, alignment
 
-template <int kSpan>
+// kDqk: query/key head dim, 64 (128-byte, 128B-swizzled rows) or 16 (32-byte,
+// 32B-swizzled rows)
+template <int kSpan, int kDqk>
 struct SlidingLayout {
-  static constexpr uint32_t kQBytes = kT * 128;      // 128 rows x 128 B
-  static constexpr uint32_t kKVBytes = kSpan * 128;  // kSpan rows x 128 B
-  static constexpr uint32_t kStageBytes = kQBytes + 2 * kKVBytes;
-  // as many TMA stages as shared memory holds (3 at kSpan 192, 2 at 256)
-  static constexpr int kStages = 3 * kStageBytes + 2048 <= 227 * 1024 ? 3 : 2;
+  static constexpr uint32_t kQBytes = kT * kDqk * 2;
+  static constexpr uint32_t kKBytes = kSpan * kDqk * 2;
+  static constexpr uint32_t kVBytes = kSpan * kD * 2;  // kSpan rows x 128 B
+  static constexpr uint32_t kOffK = kQBytes;
+  static constexpr uint32_t kOffV = kQBytes + kKBytes;
+  static constexpr uint32_t kStageBytes = kQBytes + kKBytes + kVBytes;
+  // as many TMA stages as shared memory holds (at most kMaxStages); at
+  // d_qk = 16 that is 6 or 5, which also keeps the CTA alone on its SM
+  // (it allocates all 512 TMEM columns)
+  static constexpr int fit_stages() {
+    int n = kMaxStages;
+    while (n > 2 && n * kStageBytes + kStageOverhead > 227 * 1024) --n;
+    return n;
+  }
+  static constexpr int kStages = fit_stages();
   static constexpr uint32_t kOffBar = kStages * kStageBytes;
   static constexpr uint32_t kOffRowSum = kOffBar + 256;  // fp32 row sums, per TMEM buffer
   static constexpr uint32_t kSmemAlloc = kOffRowSum + 2 * kT * 4 + 1024;  // + alignment slack
@@ -57,20 +71,22 @@ struct SlidingLayout {
   static constexpr int kBufs = 2 * kBufCols <= 512 ? 2 : 1;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kLoadBytes = kStageBytes;
-  static_assert(kQBytes % 1024 == 0 && kKVBytes % 1024 == 0,
+  static_assert(kOffV % 1024 == 0 && kStageBytes % 1024 == 0,
                 "128B-swizzled tiles need 1024-byte alignment");
   static_assert(kSmemAlloc <= 227 * 1024, "shared memory budget");
+  static_assert(kSmemAlloc > 114 * 1024, "one CTA per SM (all TMEM columns)");
   static_assert(kLoadBytes < (1u << 20), "one TMA transaction count");
 };
 
 struct SlidingParams {
   __nv_bfloat16 *out;
+  const __nv_bfloat16 *addend;  // null, or (bh, n, 64) added to the output (may be out)
   int *err;
   int64_t n;
   int64_t tiles;       // bh * tiles_per_head
   int tiles_per_head;
   int window;
-  float scale_log2;    // log2(e) / sqrt(head_dim)
+  float scale_log2;    // log2(e) / sqrt(d_qk)
 };
 
 // barriers: TMA stage full / empty, then per TMEM buffer: S ready, P ready,
@@ -103,11 +119,11 @@ __device__ __forceinline__ bool wait_teardown(uint64_t *bar, uint32_t parity) {
   return true;
 }
 
-template <int kSpan>
+template <int kSpan, int kDqk>
 __global__ void __launch_bounds__(kThreadsSl, 1)
 sliding_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const SlidingParams p) {
-  using L = SlidingLayout<kSpan>;
+  using L = SlidingLayout<kSpan, kDqk>;
   constexpr int kBufs = L::kBufs;
   constexpr int kStages = L::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -152,8 +168,8 @@ sliding_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         uint8_t *st = smem + s * L::kStageBytes;
         mbar_arrive_expect_tx(&bars[kFull + s], L::kLoadBytes);
         tma_load_3d(st, &tm_q, &bars[kFull + s], 0, q0, bh);
-        tma_load_3d(st + L::kQBytes, &tm_k, &bars[kFull + s], 0, k0, bh);
-        tma_load_3d(st + L::kQBytes + L::kKVBytes, &tm_v, &bars[kFull + s], 0, k0, bh);
+        tma_load_3d(st + L::kOffK, &tm_k, &bars[kFull + s], 0, k0, bh);
+        tma_load_3d(st + L::kOffV, &tm_v, &bars[kFull + s], 0, k0, bh);
       }
       // every issued copy must land before the CTA can exit
       for (int c = j - kStages < 0 ? 0 : j - kStages; c < j; ++c)
@@ -173,10 +189,14 @@ sliding_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           return false;
         tc_fence_after();
         const uint32_t st = sb + s * L::kStageBytes;
-        const uint64_t qd = make_sdesc(st, 16, 1024, kSwizzle128B);
-        const uint64_t kd = make_sdesc(st + L::kQBytes, 16, 1024, kSwizzle128B);
+        // K-major Q and K: 128-byte rows (8-row groups 1024 B apart) at
+        // d_qk = 64, 32-byte rows (groups 256 B apart) at d_qk = 16
+        constexpr uint32_t kSbo = kDqk == 64 ? 1024 : 256;
+        constexpr auto kSw = kDqk == 64 ? kSwizzle128B : kSwizzle32B;
+        const uint64_t qd = make_sdesc(st, 16, kSbo, kSw);
+        const uint64_t kd = make_sdesc(st + L::kOffK, 16, kSbo, kSw);
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)  // K steps of 16 along the 128-byte rows
+        for (int kk = 0; kk < kDqk / 16; ++kk)  // K steps of 16 (32 bytes) along the rows
           umma_ss(tmem + b * L::kBufCols, qd + 2 * kk, kd + 2 * kk, id_s, kk > 0 ? 1u : 0u);
         umma_commit(&bars[kSReady + b]);
         return true;
@@ -185,8 +205,7 @@ sliding_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         const int s = j % kStages, b = j % kBufs;
         if (!mbar_wait(&bars[kPReady + b], (j / kBufs) & 1, abort_flag)) return false;
         tc_fence_after();
-        const uint64_t vd =
-            make_sdesc(sb + s * L::kStageBytes + L::kQBytes + L::kKVBytes, 16, 1024, kSwizzle128B);
+        const uint64_t vd = make_sdesc(sb + s * L::kStageBytes + L::kOffV, 16, 1024, kSwizzle128B);
         const uint32_t sp = tmem + b * L::kBufCols;
 #pragma unroll
         for (int jj = 0; jj < kSpan / 16; ++jj)  // 16 keys (2048 bytes of V) per step
@@ -302,16 +321,29 @@ sliding_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       const uint64_t inv2 = f2pack(inv, inv);
       uint32_t w[32];
       const uint32_t orow = taddr(tmem, wq * 32, b * L::kBufCols + kSpan);
+      // the addend's row q0 + r (this lane's row before the transpose below),
+      // added in fp32 before the single rounding to bf16
+      const bool add_row = p.addend != nullptr && q0 + r < p.n;
+      const uint4 *arow = (const uint4 *)(p.addend + ((uint64_t)bh * p.n + (add_row ? q0 + r : 0)) * kD);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t o[32];
+        uint4 a[4] = {};
+        if (add_row) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a[i] = arow[4 * h + i];
+        }
         tmem_ld16(orow + 32 * h, o);
         tmem_ld16(orow + 32 * h + 16, o + 16);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          w[16 * h + i] = pack_bf16x2(
-              fmul2(f2pack(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), inv2));
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t aw = i % 4 == 0 ? a[i / 4].x : i % 4 == 1 ? a[i / 4].y
+                            : i % 4 == 2 ? a[i / 4].z : a[i / 4].w;
+          const uint64_t add2 = f2pack(__uint_as_float(aw << 16), __uint_as_float(aw & 0xFFFF0000u));
+          w[16 * h + i] = pack_bf16x2(ffma2(
+              f2pack(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), inv2, add2));
+        }
       }
       // O and the row sums of buffer b are in registers: the buffer is free
       tc_fence_before();
@@ -361,19 +393,22 @@ sliding_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, kErrTimeout);
 }
 
-template <int kSpan>
+template <int kSpan, int kDqk>
 int launch(const void *q, const void *k, const void *v, const SlidingParams &p, int64_t bh,
            int sm_count, cudaStream_t s) {
-  using L = SlidingLayout<kSpan>;
+  using L = SlidingLayout<kSpan, kDqk>;
+  constexpr CUtensorMapSwizzle kQKSwizzle =
+      kDqk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B;
   CUtensorMap mq, mk, mv;
-  if (!make_tmap_3d(&mq, q, bh, p.n, kD, kT, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_tmap_3d(&mk, k, bh, p.n, kD, kSpan, CU_TENSOR_MAP_SWIZZLE_128B) ||
+  if (!make_tmap_3d(&mq, q, bh, p.n, kDqk, kT, kQKSwizzle) ||
+      !make_tmap_3d(&mk, k, bh, p.n, kDqk, kSpan, kQKSwizzle) ||
       !make_tmap_3d(&mv, v, bh, p.n, kD, kSpan, CU_TENSOR_MAP_SWIZZLE_128B))
     return LA_ERR_CUDA;
-  if (allow_dynamic_smem((const void *)sliding_tc_kernel<kSpan>, (int)L::kSmemAlloc) != LA_OK)
+  if (allow_dynamic_smem((const void *)sliding_tc_kernel<kSpan, kDqk>, (int)L::kSmemAlloc) !=
+      LA_OK)
     return LA_ERR_CUDA;
   const int64_t grid = p.tiles < sm_count ? p.tiles : sm_count;
-  sliding_tc_kernel<kSpan><<<(unsigned)grid, kThreadsSl, L::kSmemAlloc, s>>>(mq, mk, mv, p);
+  sliding_tc_kernel<kSpan, kDqk><<<(unsigned)grid, kThreadsSl, L::kSmemAlloc, s>>>(mq, mk, mv, p);
   return check_launch();
 }
 
@@ -382,22 +417,26 @@ int launch(const void *q, const void *k, const void *v, const SlidingParams &p, 
 bool sliding_tc_supported(int64_t window) { return window >= 1 && window <= 2 * kT - kT + 1; }
 
 int launch_sliding_tc(const void *q, const void *k, const void *v, void *out, int64_t bh,
-                      int64_t n, int64_t window, const DeviceInfo &info, cudaStream_t s) {
-  if (!sliding_tc_supported(window)) return LA_ERR_UNSUPPORTED;
+                      int64_t n, int64_t d_qk, int64_t window, const void *addend,
+                      const DeviceInfo &info, cudaStream_t s) {
+  if (!sliding_tc_supported(window) || (d_qk != 16 && d_qk != 64)) return LA_ERR_UNSUPPORTED;
   if (bh > 65535 || n > INT32_MAX - 2 * kT) return LA_ERR_UNSUPPORTED;
   SlidingParams p{};
   p.out = (__nv_bfloat16 *)out;
+  p.addend = (const __nv_bfloat16 *)addend;
   p.err = device_error_word();
   p.n = n;
   p.tiles_per_head = (int)((n + kT - 1) / kT);
   p.tiles = bh * p.tiles_per_head;
   p.window = (int)window;
-  p.scale_log2 = 1.4426950408889634f / 8.0f;  // log2(e) / sqrt(64)
+  p.scale_log2 = 1.4426950408889634f / (d_qk == 64 ? 8.0f : 4.0f);  // log2(e) / sqrt(d_qk)
   if (!p.err) return LA_ERR_CUDA;
   if (p.tiles == 0) return LA_OK;
   const int sms = info.sm_count > 0 ? info.sm_count : 1;
-  return window <= kT / 2 + 1 ? launch<192>(q, k, v, p, bh, sms, s)
-                              : launch<256>(q, k, v, p, bh, sms, s);
+  const bool narrow = window <= kT / 2 + 1;
+  if (d_qk == 64)
+    return narrow ? launch<192, 64>(q, k, v, p, bh, sms, s) : launch<256, 64>(q, k, v, p, bh, sms, s);
+  return narrow ? launch<192, 16>(q, k, v, p, bh, sms, s) : launch<256, 16>(q, k, v, p, bh, sms, s);
 }
 
 }  // namespace la

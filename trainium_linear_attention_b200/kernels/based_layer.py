@@ -9,8 +9,11 @@ calls one attention function.
 * ``ref_based_layer(q, k, v, window_size=64, eps=1e-6)`` -- the composition of
   the reference's two PyTorch formulas (kernels/pytorch_attention.py:27-42
   and benchmarks/sliding_attention_benchmark.py:32-56), for comparisons only.
-* ``based_layer(q, k, v, window_size=64, chunk_size=64, eps=1e-6)`` -- the
-  sm_100a kernel computing both in one pass over q, k, v (window <= 129).
+* ``based_layer(q, k, v, window_size=64, chunk_size=64, eps=1e-6)`` -- both
+  terms on sm_100a (window <= 129): for bf16, d_qk = 16, d_v = 64 the chunked
+  tensor-core kernel followed by the sliding-window kernel, which adds its
+  term to the first one's output; other shapes in one pass over q, k, v on
+  CUDA cores.
 """
 
 from __future__ import annotations

@@ -176,7 +176,9 @@ def sliding_window(q, k, v, window_size: int = 64) -> torch.Tensor:
 def based_layer(q, k, v, window_size: int = 64, eps: float = 1e-6, segments: int = 0,
                 workspace: torch.Tensor | None = None) -> torch.Tensor:
     """The full BASED layer: chunked BASED attention plus sliding-window
-    softmax attention over the same q, k, v, in one pass (window <= 129)."""
+    softmax attention over the same q, k, v (window <= 129): two tensor-core
+    kernels for bf16, d_qk = 16, d_v = 64 (the second adds its term to the
+    first's output), one pass on CUDA cores otherwise."""
     code = _check_qkv(q, k, v)
     if int(window_size) < 1:
         raise ValueError("window_size must be >= 1")
