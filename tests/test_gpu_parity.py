@@ -182,6 +182,32 @@ def test_chunked_d64_segments_and_state():
     assert O.rel_l2(np64(torch.cat([a, b], 2)), want) <= TOL_FP32
 
 
+@pytest.mark.parametrize("heads,t", [(2, 2000), (3, 4100)])
+def test_chunked_d64_bf16_tensor_core_state(heads, t):
+    """bf16 d_qk = 64 on the tensor-core kernel (16-CTA cluster, 160 feature
+    slots per CTA): normalised and numerator outputs, one and three segments
+    (the state pass), final states against the oracle's, the state entry
+    point, and a split at a ragged token boundary seeded with the first
+    part's state.  States carry bf16-rounded features: within 2e-3."""
+    q, k, v = inputs((1, heads, t, 64), 64, seed=642 + t)
+    qd, kd, vd = cuda(q, k, v)
+    want, s_want = O.based_chunked(np64(q), np64(k), np64(v), return_state=True)
+    s_want = s_want.reshape(heads, 2145, 65)
+    for g in (1, 3):
+        y, s = ops.based_chunked(qd, kd, vd, segments=g, return_state=True)
+        assert O.rel_l2(np64(y), want) <= TOL_BF16
+        assert O.rel_l2(s.double().cpu().numpy(), s_want) <= 2e-3
+    num = ops.based_chunked(qd, kd, vd, normalize=False)
+    num_want = O.based_chunked(np64(q), np64(k), np64(v), normalize=False)
+    assert O.rel_l2(np64(num), num_want) <= TOL_BF16
+    st = ops.based_chunked_state(kd, vd, segments=3)
+    assert O.rel_l2(st.double().cpu().numpy(), s_want) <= 2e-3
+    cut = 1000
+    a, sa = ops.based_chunked(qd[:, :, :cut], kd[:, :, :cut], vd[:, :, :cut], return_state=True)
+    b = ops.based_chunked(qd[:, :, cut:], kd[:, :, cut:], vd[:, :, cut:], init_state=sa)
+    assert O.rel_l2(np64(torch.cat([a, b], 2)), want) <= TOL_BF16
+
+
 def test_chunked_unaligned_pointers():
     """bf16 tensors whose data is not 16-byte aligned (TMA cannot address
     them) run on the CUDA-core kernels with the same result."""

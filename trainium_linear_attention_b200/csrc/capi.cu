@@ -219,6 +219,12 @@ bool use_tensor_cores(int dtype, int64_t dqk, int64_t dv) {
   return dtype == LA_DTYPE_BFLOAT16 && dqk == 16 && dv == 64;
 }
 
+// d_qk = 64 (F = 2145) on tensor cores: bf16, d_v = 64, the state split over a
+// 16-CTA cluster (tc_cluster64.cu), where the device can hold such a cluster
+bool use_tc64(int dtype, int64_t dqk, int64_t dv) {
+  return dtype == LA_DTYPE_BFLOAT16 && dqk == 64 && dv == 64 && chunked64_tc_available();
+}
+
 // TMA needs 16-byte aligned inputs and the tensor-core epilogues store the
 // output in 32-byte pieces; other pointers take the SIMT kernels
 bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
@@ -241,7 +247,9 @@ int plan_chunked_fwd(const void *q, const void *k, const void *v, const void *ou
   p.features = p.identity ? d_qk : feature_dim(d_qk);
   p.tc = use_tensor_cores(dtype, d_qk, d_v) && aligned16(q) && aligned16(k) &&
          aligned16(v) && aligned32(out);
-  if (!p.tc && !chunked_simt_supported(p.features, d_qk, d_v)) {
+  p.tc64 = !p.identity && use_tc64(dtype, d_qk, d_v) && aligned16(q) && aligned16(k) &&
+           aligned16(v) && aligned16(out);
+  if (!p.tc && !p.tc64 && !chunked_simt_supported(p.features, d_qk, d_v)) {
     if (p.identity || !cluster_chunked_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
     p.cluster = true;
   }
@@ -255,9 +263,11 @@ int plan_chunked_fwd(const void *q, const void *k, const void *v, const void *ou
     *plan = p;
     return LA_OK;
   }
-  // one wave of CTAs: a cluster run places cluster_chunked_ctas_per_segment()
-  // CTAs on every (head, segment)
-  const int wave = p.cluster ? info.sm_count / cluster_chunked_ctas_per_segment() : info.sm_count;
+  // one wave of CTAs: a cluster run places its cluster size of CTAs on every
+  // (head, segment)
+  const int wave = p.tc64      ? info.sm_count / chunked64_tc_ctas_per_segment()
+                   : p.cluster ? info.sm_count / cluster_chunked_ctas_per_segment()
+                               : info.sm_count;
   p.g = segments == 0 ? auto_segments(bh, n, wave) : effective_segments(n, segments);
   p.seg_len = p.g > 1 ? segment_len(n, p.g) : n;
   // With two segments the state pass covers only the first: a long one runs
@@ -350,6 +360,8 @@ int la_based_chunked_plan(int64_t batch_heads, int64_t seq_len, int64_t d_qk, in
       // also covers two equal segments, for callers that pass segments_out
       // on explicitly (the split itself needs one state per head).
       g = 2;
+    } else if (use_tc64(dtype, d_qk, d_v)) {
+      g = auto_segments(batch_heads, seq_len, info.sm_count / chunked64_tc_ctas_per_segment());
     } else if (!use_tensor_cores(dtype, d_qk, d_v) &&
                !chunked_simt_supported(feature_dim(d_qk), d_qk, d_v) &&
                cluster_chunked_supported(d_qk, d_v)) {
@@ -433,6 +445,8 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
                                                   (g - 1) * plan.ratio,
                                                   plan.seg_len / plan.ratio, plan.identity, info,
                                                   s)
+         : plan.tc64    ? launch_chunked64_state_tc(k, v, seg_states, bh, seq_len, g, g - 1,
+                                                    plan.seg_len, s)
          : plan.cluster ? launch_chunked_state_cluster(k, v, seg_states, bh, seq_len, (int)d_qk,
                                                        (int)d_v, dtype, g, g - 1, plan.seg_len,
                                                        s)
@@ -442,9 +456,12 @@ int la_based_chunked_fwd(const void *q, const void *k, const void *v, void *out,
     if (st != LA_OK) return st;
     if ((g - 1) * plan.ratio > 1 &&
         (st = launch_prefix_segments(seg_states, nullptr, bh, g, g - 1, plan.ratio,
-                                     (int64_t)per_head, s, plan.tc)) != LA_OK)
+                                     (int64_t)per_head, s, plan.tc || plan.tc64)) != LA_OK)
       return st;
   }
+  if (plan.tc64)
+    return launch_chunked64_output_tc(q, k, v, out, init_state, final_state, seg_states, bh,
+                                      seq_len, eps, normalize, g, plan.seg_len, s);
   const bool after_state_pass = g > 1 && !(flags & LA_CHUNKED_REUSE_SEGMENTS);
   if (plan.tc)
     return launch_chunked_output_tc(q, k, v, out, init_state, final_state, seg_states, bh,
@@ -468,12 +485,13 @@ int la_based_layer_fwd(const void *q, const void *k, const void *v, void *out, i
   if (window < 1 || segments < 0) return LA_ERR_INVALID_ARGUMENT;
   const int64_t bh = batch * heads;
   if (bh == 0 || seq_len == 0) return LA_OK;
-  // Tensor-core shape (bf16, d_qk = 16, d_v = 64, window <= 129): the chunked
-  // kernel writes the normalised BASED term, then the sliding kernel adds the
-  // window term to it in its epilogue (q, k and v are read twice; on CUDA
-  // cores one pass is slower by far).
-  if (use_tensor_cores(dtype, d_qk, d_v) && sliding_tc_supported(window) && aligned16(q) &&
-      aligned16(k) && aligned16(v) && aligned32(out)) {
+  // Tensor-core shapes (bf16, d_qk = 16 or 64, d_v = 64, window <= 129): the
+  // chunked kernel writes the normalised BASED term, then the sliding kernel
+  // adds the window term to it in its epilogue (q, k and v are read twice; on
+  // CUDA cores one pass is slower by far).
+  if ((use_tensor_cores(dtype, d_qk, d_v) || use_tc64(dtype, d_qk, d_v)) &&
+      sliding_tc_supported(window) && aligned16(q) && aligned16(k) && aligned16(v) &&
+      aligned32(out)) {
     st = la_based_chunked_fwd(q, k, v, out, batch, heads, seq_len, d_qk, d_v, dtype, 64, eps,
                               LA_CHUNKED_NORMALIZE, nullptr, nullptr, workspace, workspace_bytes,
                               segments, stream);
@@ -537,11 +555,14 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
   if (seq_len == 0) return cuda_status(cudaMemsetAsync(state_out, 0, state_bytes, s));
   const bool tc = use_tensor_cores(dtype, d_qk, d_v) && aligned16(k) &&
                   aligned16(v);
-  const bool cluster = !tc && !chunked_simt_supported(feature_dim(d_qk), d_qk, d_v);
+  const bool tc64 = use_tc64(dtype, d_qk, d_v) && aligned16(k) && aligned16(v);
+  const bool cluster = !tc && !tc64 && !chunked_simt_supported(feature_dim(d_qk), d_qk, d_v);
   if (cluster && !cluster_chunked_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
   // the same segmentation as la_based_chunked_fwd, so that a forward with
   // LA_CHUNKED_REUSE_SEGMENTS finds the seeds it expects
-  const int wave = cluster ? info.sm_count / cluster_chunked_ctas_per_segment() : info.sm_count;
+  const int wave = tc64      ? info.sm_count / chunked64_tc_ctas_per_segment()
+                   : cluster ? info.sm_count / cluster_chunked_ctas_per_segment()
+                             : info.sm_count;
   int g = segments == 0 ? auto_segments(bh, seq_len, wave) : effective_segments(seq_len, segments);
   if (g > 1) {
     const size_t need = la_based_chunked_workspace_size(bh, seq_len, d_qk, d_v, g);
@@ -551,6 +572,7 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
   const int64_t seg_len = g > 1 ? segment_len(seq_len, g) : seq_len;
   float *dst = g > 1 ? (float *)workspace : state_out;
   st = tc        ? launch_chunked_state_tc(k, v, dst, bh, seq_len, g, g, seg_len, false, info, s)
+       : tc64    ? launch_chunked64_state_tc(k, v, dst, bh, seq_len, g, g, seg_len, s)
        : cluster ? launch_chunked_state_cluster(k, v, dst, bh, seq_len, (int)d_qk, (int)d_v,
                                                 dtype, g, g, seg_len, s)
                  : launch_chunked_state_simt(k, v, dst, bh, seq_len, (int)d_qk, (int)d_v, dtype,
@@ -559,7 +581,7 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
   // the total, and in the workspace the prefix slots a forward with
   // LA_CHUNKED_REUSE_SEGMENTS seeds its segments from
   return launch_prefix_segments(dst, state_out, bh, g, g, 1,
-                                (int64_t)feature_dim(d_qk) * (d_v + 1), s, tc);
+                                (int64_t)feature_dim(d_qk) * (d_v + 1), s, tc || tc64);
 }
 
 int la_sliding_window_fwd(const void *q, const void *k, const void *v, void *out, int64_t batch,

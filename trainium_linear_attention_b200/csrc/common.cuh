@@ -119,7 +119,8 @@ struct ChunkedFwdPlan {
   bool identity = false;  // identity feature map (LA_CHUNKED_IDENTITY)
   int64_t features = 0;   // F: rows of a head's state
   bool tc = false;        // tcgen05 kernels (else the SIMT or cluster kernels)
-  bool cluster = false;   // the cluster kernels (state split over kCluster CTAs)
+  bool tc64 = false;      // d_qk = 64 tcgen05 kernels (state split over a 16-CTA cluster)
+  bool cluster = false;   // the CUDA-core cluster kernels (state split over 8 CTAs)
   int64_t lead = 0;       // > 0: lead/main split with a lead of this many tokens
   int g = 1;              // equal segments per head
   int64_t seg_len = 0;    // tokens per segment

@@ -38,6 +38,21 @@ int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *
                              int64_t lead_len, bool after_own_kernel, const DeviceInfo &info,
                              cudaStream_t s);
 
+// d_qk = 64, d_v = 64 (F = 2145): chunked forward with the state split over a
+// 16-CTA cluster (tc_cluster64.cu).  Available where the device can hold one
+// such cluster (the non-portable cluster size is enabled on first use).
+// Segment, seed and state conventions as launch_chunked_{state,output}_tc;
+// out needs 16-byte alignment.
+bool chunked64_tc_available();
+int chunked64_tc_ctas_per_segment();
+int launch_chunked64_state_tc(const void *k, const void *v, float *seg_states, int64_t bh,
+                              int64_t n, int segments, int n_launch, int64_t seg_len,
+                              cudaStream_t s);
+int launch_chunked64_output_tc(const void *q, const void *k, const void *v, void *out,
+                               const float *init_state, float *final_state,
+                               const float *seg_states, int64_t bh, int64_t n, float eps,
+                               bool normalize, int segments, int64_t seg_len, cudaStream_t s);
+
 // Windows the tensor-core sliding kernel handles (W <= 129).  It takes d_qk
 // 64 or 16 with d_v 64; addend (null, or (bh, n, 64) bf16, may be out) is
 // added to the output in fp32 before its rounding to bf16.

@@ -8,11 +8,13 @@ c5   parallel and chunked BASED at B*N = 262144, H=16, N = 512 .. 65536 (by
      default; --c5-min-n / --c5-max-n): the crossover that ``solution()``
      dispatches on (config 5)
 ident   chunked identity-feature-map numerator, B=4, H=16, N=2048, d_qk=16, d_v=64
-d64     chunked BASED at d_qk = d_v = 64 (F = 2145, cluster kernels), B=1, H=16, N=4096
+d64     chunked BASED at d_qk = d_v = 64 (F = 2145, the state split over a 16-CTA
+        cluster), B=1, H=16, N=4096
 share   configuration 4's per-rank work at 2, 4 and 8 GPUs (64, 32, 16 heads of
         N = 32768, heads sharded, no collective), timed on one GPU
-layer   the full BASED layer (chunked BASED + sliding window W=64 in one pass):
-        B=4, H=16, N=2048, d_qk=16, d_v=64, and at d_qk = d_v = 64, B=1, H=16, N=4096
+layer   the full BASED layer (chunked BASED + sliding window W=64; the sliding
+        kernel adds into the chunked kernel's output): B=4, H=16, N=2048,
+        d_qk=16, d_v=64, and at d_qk = d_v = 64, B=1, H=16, N=4096
 
 All inputs are bf16, iid N(0,1) * scale (0.5 for BASED, 1 for sliding),
 generated on the device from a fixed seed.  Each point: warm-up calls, then
@@ -134,7 +136,7 @@ def main():
         q, k, v = inputs(b, h, n, d, d, 0.5)
         ms, st = time_calls(lambda: ops.based_chunked(q, k, v), args.steps)
         f = 1 + d + d * (d + 1) // 2
-        line("d64", "chunked_cluster", b, h, n, d, d, ms, st, h * (4 * d * 2),
+        line("d64", "chunked_d64", b, h, n, d, d, ms, st, h * (4 * d * 2),
              h * (4 * f * (d + 1) + (64 + 1) / 2 * (2 * d + 2 * d + 4)))
     if "layer" in what:
         for b, n, d_qk, d_v in ((4, 2048, 16, 64), (1, 4096, 64, 64)):
