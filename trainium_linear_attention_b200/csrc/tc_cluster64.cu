@@ -12,40 +12,45 @@
 //   every CTA   phi_r(K) -> smem, phi_r(Q) -> TMEM   (CUDA cores, its slots)
 //               O_r    = phi_r(Q) S_r,c          M=128 N=80  K=160 (bf16 snapshot of S_r,c)
 //               S_r^T += [V 1 0]^T phi_r(K)       M=128 N=160 K=128
-//   CTA 0       scores = Q K^T                    M=128 N=128 K=64
-//               P      = tril(1 + s/8 + s^2/128)   (CUDA cores, written over the scores)
-//               O_0   += P [V 1]                  M=128 N=80  K=128
-//   every CTA   O_r -> shared memory (fp32); cluster barrier
-//   CTA r       rows 8r .. 8r+7: sum of the 16 partial rows (read from the other
-//               CTAs' shared memory in rank order), / (O[:, 64] + eps); stored
-//   cluster barrier (the partials may be overwritten)
+//   CTA r < 8   the intra-tile term of keys 16r .. 16r+15:
+//               scores = Q K_r^T                  M=128 N=16  K=64
+//               P      = tril(1 + s/8 + s^2/128)   (CUDA cores, over the scores)
+//               O_r   += P [V_r 1]                M=128 N=80  K=16
+//   every CTA   row i of O_r -> shared memory of CTA i / 8 (remote stores);
+//               cluster barrier
+//   CTA r       rows 8r .. 8r+7: sum of the 16 partial rows in rank order,
+//               / (O[:, 64] + eps); stored
 //
 // which is the reference recurrence of kernels/nki_attention_chunked.py:71-109
 // with the normaliser, as in the d_qk = 16 kernel (tc_chunked.cu), whose
-// operand layouts this kernel reuses: the sum over the cluster of phi_r(q) .
-// phi_r(k) is the full Taylor kernel 1 + s + s^2/2 of s = q.k / 8.
+// operand layouts this kernel reuses: summed over the cluster, phi_r(q) .
+// phi_r(k) is the full Taylor kernel 1 + s + s^2/2 of s = q.k / 8, and the
+// intra-tile partials sum to tril(P) [V 1].  The partials land in one of two
+// buffers by tile parity, so one cluster barrier per tile orders their
+// writes before their reads, and a buffer is rewritten only two tiles later,
+// after every owner has passed the next barrier.
 //
 // Features.  Slot s of CTA r is feature f = 135 r + s in the documented order
-// [1, x_0 .. x_63, x_a x_b (a <= b) row-major]; it is the product of two
-// entries of the token's row extended by x_64 = 1 and x_65 = 0 (constant,
-// linear and padding slots use those), scaled on the query side by 1/8
-// (linear), 1/64 (a < b) or 1/128 (a = b): exact powers of two, so each
-// feature is the fp32 product of bf16 inputs rounded once to bf16, as in the
-// d_qk = 16 kernel.  The token rows are first copied into a column-major
-// bf16 table so that every thread reads its token's entries without bank
-// conflicts.
+// [1, x_0 .. x_63, x_a x_b (a <= b) row-major].  Four threads share a token;
+// each holds the token's 64 (q_a, k_a) pairs in registers as bf16x2 words
+// (plus u = (1, 1) for a token in the sequence, (1, 0) past its end) and
+// computes a fixed quarter of the CTA's slots with code generated for that
+// (CTA rank, quarter) from the compile-time slot list: one bf16x2 multiply
+// x_a * x_b (or x_a * u, u * u) makes the query and the key feature, each the
+// fp32 product of bf16 inputs rounded once to bf16; the query side is then
+// scaled by 1/8 (linear), 1/64 (a < b) or 1/128 (a = b), exact powers of
+// two, as in the d_qk = 16 kernel.
 //
 // The phases of a tile run one after another (barriers between them); the
-// next tile's Q, K, V load by TMA meanwhile.  The state-only variant
-// (kStateOnly) runs the phi(K) / update path without a cluster (every CTA
-// is independent) and writes its slots of the segment's state.
-#include <cooperative_groups.h>
+// next tile's Q, K, V load by TMA from the end of this tile's MMAs.  The
+// state-only variant (kStateOnly) runs the phi(K) / update path without a
+// cluster (every CTA is independent) and writes its slots of the segment's
+// state.
+#include <utility>
 
 #include "tc_common.cuh"
 #include "tc_kernels.cuh"
 #include "tma_host.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace la {
 namespace {
@@ -60,15 +65,18 @@ constexpr int kFr = 135;       // features per CTA (16 * 135 = 2160 >= 2145)
 constexpr int kSlots = 160;    // slots per CTA: five 32-slot blocks
 constexpr int kSV = kDv + 1;   // state columns in global memory
 constexpr int kNO = 80;        // N of phi(Q) S and P [V 1]
-constexpr int kThreads = 256;
-constexpr int kRowsPerRank = kT / kCl;  // output rows each CTA finishes
+constexpr int kThreads = 512;
+constexpr int kRowsPerRank = kT / kCl;  // output rows each CTA finishes (8)
+constexpr int kIntraRanks = 8;          // CTAs that take 16 keys of the intra-tile term
+constexpr int kRecvLd = 68;             // floats per received partial row (65 + pad, 16 B)
 static_assert(kCl * kFr >= kF && kFr <= kSlots && kSlots % 32 == 0, "feature split");
+static_assert(kIntraRanks * 16 == kT && kIntraRanks <= kCl, "intra-tile split");
 
 // TMEM columns (one CTA per SM owns all 512)
 constexpr uint32_t kColS = 0;       // S^T    128 lanes x 160 fp32
 constexpr uint32_t kColO = 160;     // O      128 lanes x 80 fp32
 constexpr uint32_t kColPhiQ = 256;  // phi(Q) 128 lanes x 80 bf16 pairs
-constexpr uint32_t kColSc = 384;    // scores 128 fp32 / P 64 bf16 pairs (CTA 0)
+constexpr uint32_t kColSc = 384;    // scores 16 fp32 / P 8 bf16 pairs (CTAs r < 8)
 constexpr uint32_t kTmemCols = 512;
 
 // Shared memory (offsets from a 1024-byte aligned base)
@@ -77,55 +85,77 @@ constexpr uint32_t kPhiBlock = kT * 64;              // 32 slots of 128 tokens, 
 constexpr uint32_t kPhiBytes = (kSlots / 32) * kPhiBlock;
 constexpr uint32_t kSnapKBlock = kNO * 128;          // 64 slots of the 80 snapshot rows
 constexpr uint32_t kSnapBytes = 3 * kSnapKBlock;
-constexpr int kXRows = kDqk + 2;                     // x_0 .. x_63, 1, 0
-constexpr int kStages = 2;
+constexpr uint32_t kRecvBytes = kCl * kRowsPerRank * kRecvLd * 4;  // one tile's partials
 
+// The output pass holds one tile of Q, K and V (the next tile loads during
+// the partial-sum exchange); the state pass keeps three tiles of K and V in
+// flight (and so needs more than half the SM's shared memory: it runs alone
+// on its SM, whose 512 TMEM columns it allocates).
 template <bool kStateOnly>
 struct Layout64 {
-  static constexpr uint32_t kOffQ = 0;
-  static constexpr uint32_t kOffK = kOffQ + (kStateOnly ? 0 : kStages * kTileBytes);
-  static constexpr uint32_t kOffV = kOffK + kStages * kTileBytes;
-  static constexpr uint32_t kOffOnes = kOffV + kStages * kTileBytes;  // 16 rows x 128 B
+  static constexpr int kStages = kStateOnly ? 3 : 1;
+  static constexpr uint32_t kStageBytes = (kStateOnly ? 2 : 3) * kTileBytes;
+  static constexpr uint32_t kOffQ = 0;                               // stage: [Q] K V
+  static constexpr uint32_t kOffK = kStateOnly ? 0 : kTileBytes;
+  static constexpr uint32_t kOffV = kOffK + kTileBytes;
+  static constexpr uint32_t kOffOnes = kStages * kStageBytes;         // 16 rows x 128 B
   static constexpr uint32_t kOffPhiK = kOffOnes + 2048;
   static constexpr uint32_t kOffSnap = kOffPhiK + kPhiBytes;
-  static constexpr uint32_t kOffX = kOffSnap + (kStateOnly ? 0 : kSnapBytes);
-  static constexpr uint32_t kOffPart = kOffX + kXRows * kT * 2;     // fp32 [128][65]
-  static constexpr uint32_t kOffDesc = kOffPart + (kStateOnly ? 0 : kT * kSV * 4);
+  static constexpr uint32_t kOffRecv = kOffSnap + (kStateOnly ? 0 : kSnapBytes);
+  static constexpr uint32_t kOffDesc = kOffRecv + (kStateOnly ? 0 : 2 * kRecvBytes);
   static constexpr uint32_t kOffBar = kOffDesc + kSlots * 8;
-  static constexpr uint32_t kSmemAlloc = kOffBar + 256 + 1024;  // + alignment slack
-  static_assert(kOffV % 1024 == 0 && kOffOnes % 1024 == 0 && kOffPhiK % 1024 == 0 &&
+  static constexpr uint32_t kSmemAlloc = kOffBar + 64 + 1024;  // + alignment slack
+  static_assert(kStageBytes % 1024 == 0 && kOffOnes % 1024 == 0 && kOffPhiK % 1024 == 0 &&
                     kOffSnap % 1024 == 0,
                 "swizzled regions need 1024-byte alignment");
-  static_assert(kOffDesc % 8 == 0 && kOffBar % 8 == 0, "alignment");
+  static_assert(kOffRecv % 16 == 0 && kOffDesc % 8 == 0 && kOffBar % 8 == 0, "alignment");
   static_assert(kSmemAlloc <= 227 * 1024, "shared memory budget");
+  static_assert(kSmemAlloc > 114 * 1024, "one CTA per SM");
 };
 
-enum Bar64 { kFull = 0, kMma = kFull + kStages, kPv, kNumBars };
+constexpr int kMaxStages64 = 3;
+enum Bar64 { kFull0 = 0, kMma = kFull0 + kMaxStages64, kPv, kNumBars };
 
-// Slot s of CTA `rank`: feature index (or -1), the two factors' rows of the
-// extended token row (64 = the constant 1, 65 = zero) and the query-side
-// weight.
+// Optional phase timeline (clock64 per tile) of thread 0 of every CTA of
+// cluster (0, 0), compiled in with -DLA_TRACE only.
+#ifdef LA_TRACE
+constexpr int kTrTiles = 32, kTrEvents = 10;
+__device__ long long la_trace64[kCl][kTrTiles][kTrEvents];
+#define LA_TRACE64(tile, ev)                                                            \
+  do {                                                                                 \
+    if (blockIdx.y == 0 && blockIdx.x < kCl && threadIdx.x == 0 && (tile) < kTrTiles) \
+      la_trace64[blockIdx.x][tile][ev] = clock64();                                    \
+  } while (0)
+#else
+#define LA_TRACE64(tile, ev) \
+  do {                       \
+  } while (0)
+#endif
+
+// Slot s of CTA `rank`: its feature (or -1), the rows a, b of the token table
+// whose product it is, and the bf16x2 weight (query-side scale, 1).
 struct SlotDesc {
   unsigned char a, b;
   short f;
-  float wq;
+  uint32_t w;
 };
 __device__ __forceinline__ SlotDesc slot_desc(int rank, int s) {
   SlotDesc d;
   const int f = rank * kFr + s;
+  uint32_t wq;  // bf16 bits of the query-side scale: exact powers of two
   if (s >= kFr || f >= kF) {
     d.a = d.b = kDqk + 1;
     d.f = -1;
-    d.wq = 0.f;
+    wq = 0u;
   } else if (f == 0) {
     d.a = d.b = kDqk;
     d.f = 0;
-    d.wq = 1.f;
+    wq = 0x3F80u;  // 1
   } else if (f <= kDqk) {
     d.a = (unsigned char)(f - 1);
     d.b = kDqk;
     d.f = (short)f;
-    d.wq = 0.125f;  // 1 / sqrt(64)
+    wq = 0x3E00u;  // 1/8 = 1/sqrt(64)
   } else {
     int r = f - 1 - kDqk, a = 0;
     while (r >= kDqk - a) {
@@ -135,8 +165,9 @@ __device__ __forceinline__ SlotDesc slot_desc(int rank, int s) {
     d.a = (unsigned char)a;
     d.b = (unsigned char)(a + r);
     d.f = (short)f;
-    d.wq = a == a + r ? 1.f / 128.f : 1.f / 64.f;  // 1/(2d) on the diagonal, 1/d off it
+    wq = r == 0 ? 0x3C00u : 0x3C80u;  // 1/128 = 1/(2d) on the diagonal, 1/64 = 1/d off it
   }
+  d.w = wq | (0x3F80u << 16);
   return d;
 }
 
@@ -161,39 +192,115 @@ __device__ __forceinline__ bool wait_teardown(uint64_t *bar, uint32_t parity) {
   return true;
 }
 
-// Tile rows (128 tokens x 64 bf16, 128B-swizzled) -> the column-major table
-// X[a][token] (bf16).  Thread t copies half a row.
-__device__ __forceinline__ void stage_rows(uint32_t tile, __nv_bfloat16 *X) {
-  const int token = threadIdx.x & (kT - 1), half = threadIdx.x >> 7;
-#pragma unroll
-  for (int ch = 0; ch < 4; ++ch) {
-    uint32_t w[4];
-    ld_shared_v4(tile + sw128_offset(token, 4 * half + ch), w[0], w[1], w[2], w[3]);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int a = 32 * half + 8 * ch + 2 * i;
-      X[a * kT + token] = __ushort_as_bfloat16((unsigned short)(w[i] & 0xFFFFu));
-      X[(a + 1) * kT + token] = __ushort_as_bfloat16((unsigned short)(w[i] >> 16));
+// Shared-memory address of `saddr` in the CTA of the cluster with rank `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                              uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b),
+               "r"(c), "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ void st_cluster_b32(uint32_t addr, uint32_t a) {
+  asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(addr), "r"(a) : "memory");
+}
+// Arrive at / wait for the cluster barrier: release / acquire at cluster
+// scope (the partials stored into other CTAs become visible to them).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Slot s of CTA `rank` at compile time: the rows a, b of the token's (q, k)
+// pairs whose product it is (64 = u, a < 0: padding) and the bf16 bits of
+// the query-side scale.
+struct SlotAB {
+  int a, b;
+  uint32_t wq;
+};
+__host__ __device__ constexpr SlotAB slot_ab(int rank, int s) {
+  const int f = rank * kFr + s;
+  if (s >= kFr || f >= kF) return {-1, -1, 0u};
+  if (f == 0) return {kDqk, kDqk, 0x3F80u};        // 1
+  if (f <= kDqk) return {f - 1, kDqk, 0x3E00u};    // x_a / 8
+  int r = f - 1 - kDqk, a = 0;
+  while (r >= kDqk - a) {
+    r -= kDqk - a;
+    ++a;
+  }
+  return {a, a + r, r == 0 ? 0x3C00u : 0x3C80u};  // x_a^2 / 128, x_a x_b / 64
+}
+__host__ __device__ constexpr bool slot_ab_matches_desc() {
+  // the compile-time list and the run-time table name the same features
+  for (int r = 0; r < kCl; ++r)
+    for (int s = 0; s < kSlots; ++s) {
+      const SlotAB d = slot_ab(r, s);
+      const int f = r * kFr + s;
+      if ((d.a < 0) != (s >= kFr || f >= kF)) return false;
     }
+  return true;
+}
+static_assert(slot_ab_matches_desc(), "slot lists");
+
+// The quarter P of a CTA's slots one thread computes: [0, 32), [32, 80),
+// [80, 128), [128, 160) (phi(Q) TMEM stores of 8 columns stay 8-aligned).
+__host__ __device__ constexpr int part_lo(int P) { return P == 0 ? 0 : P == 1 ? 32 : P == 2 ? 80 : 128; }
+__host__ __device__ constexpr int part_chunks(int P) { return P == 0 || P == 3 ? 2 : 3; }
+
+template <int R, int S>
+__device__ __forceinline__ uint32_t qk_feature(const uint32_t *x, uint32_t u) {
+  constexpr SlotAB d = slot_ab(R, S);
+  if constexpr (d.a < 0) {
+    return 0u;
+  } else {
+    uint32_t xa, xb;
+    if constexpr (d.a == kDqk) xa = u; else xa = x[d.a];
+    if constexpr (d.b == kDqk) xb = u; else xb = x[d.b];
+    const uint32_t p = hmul2_bf16(xa, xb);
+    if constexpr (d.wq == 0x3F80u) return p;
+    else return hmul2_bf16(p, d.wq | (0x3F80u << 16));
   }
 }
 
-// Eight features (slots s0 .. s0+7) of `token`, each the fp32 product
-// X[a] * X[b] * w rounded once to bf16, packed in four bf16x2 words.
-__device__ __forceinline__ void features8(const SlotDesc *desc, const __nv_bfloat16 *X, int token,
-                                          int s0, bool query, float scale, uint32_t *w) {
+// Slots S0 .. S0+15 of the thread's token: phi(K) -> smem (two 16-byte
+// chunks of the 64B-swizzled MN-major layout), phi(Q) -> 8 TMEM columns.
+template <bool kStateOnly, int R, int S0, int... I>
+__device__ __forceinline__ void feature_chunk(const uint32_t *x, uint32_t u, uint32_t phik,
+                                              uint32_t qaddr, int token,
+                                              std::integer_sequence<int, I...>) {
+  const uint32_t pq[16] = {qk_feature<R, S0 + I>(x, u)...};
+  uint32_t qf[8], kf[8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float p[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const SlotDesc d = desc[s0 + 2 * i + h];
-      const float xa = __bfloat162float(X[d.a * kT + token]);
-      const float xb = __bfloat162float(X[d.b * kT + token]);
-      p[h] = xa * xb * (query ? d.wq : 1.f) * scale;
-    }
-    w[i] = pack_bf16(p[0], p[1]);
+  for (int j = 0; j < 8; ++j) {
+    qf[j] = bf16_pair<0, 0>(pq[2 * j], pq[2 * j + 1]);
+    kf[j] = bf16_pair<1, 1>(pq[2 * j], pq[2 * j + 1]);
   }
+  st_shared_v4(phik + (S0 >> 5) * kPhiBlock + sw64_offset(token, (S0 & 31) >> 3), kf[0], kf[1],
+               kf[2], kf[3]);
+  st_shared_v4(phik + ((S0 + 8) >> 5) * kPhiBlock + sw64_offset(token, ((S0 + 8) & 31) >> 3),
+               kf[4], kf[5], kf[6], kf[7]);
+  if (!kStateOnly) tmem_st8(qaddr + S0 / 2, qf);
+}
+template <bool kStateOnly, int R, int P, int... C>
+__device__ __forceinline__ void part_features(const uint32_t *x, uint32_t u, uint32_t phik,
+                                              uint32_t qaddr, int token,
+                                              std::integer_sequence<int, C...>) {
+  (feature_chunk<kStateOnly, R, part_lo(P) + 16 * C>(x, u, phik, qaddr, token,
+                                                     std::make_integer_sequence<int, 16>{}),
+   ...);
+}
+// The code for (rank, quarter) = (idx / 4, idx % 4).
+template <bool kStateOnly, int... I>
+__device__ __forceinline__ void features_for(int idx, const uint32_t *x, uint32_t u,
+                                             uint32_t phik, uint32_t qaddr, int token,
+                                             std::integer_sequence<int, I...>) {
+  ((idx == I ? part_features<kStateOnly, I / 4, I % 4>(
+                   x, u, phik, qaddr, token, std::make_integer_sequence<int, part_chunks(I % 4)>{})
+             : void()),
+   ...);
 }
 
 template <bool kStateOnly>
@@ -208,8 +315,7 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   uint32_t *tmem_slot = (uint32_t *)(smem + L::kOffBar + 8 * kNumBars);
   volatile int *abort_flag = (volatile int *)(smem + L::kOffBar + 8 * kNumBars + 4);
   SlotDesc *desc = (SlotDesc *)(smem + L::kOffDesc);
-  __nv_bfloat16 *X = (__nv_bfloat16 *)(smem + L::kOffX);
-  float *part = (float *)(smem + L::kOffPart);
+  const float *recv = (const float *)(smem + L::kOffRecv);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // grid (kCl * segments, bh); clusters of kCl CTAs along x (output pass)
@@ -227,9 +333,6 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     grid_dependents_launch();
   }
   if (threadIdx.x < kSlots) desc[threadIdx.x] = slot_desc(rank, threadIdx.x);
-  // the constant rows of the token table: x_64 = 1, x_65 = 0
-  for (int i = threadIdx.x; i < 2 * kT; i += kThreads)
-    X[kDqk * kT + i] = __float2bfloat16(i < kT ? 1.f : 0.f);
   // constant "ones" block: A-operand rows 64..127 of [V 1 0]^T for 16 tokens
   for (int i = threadIdx.x; i < 2048 / 4; i += kThreads) {
     const int row = (i * 4) / 128, byte = (i * 4) % 128;
@@ -241,7 +344,6 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  cg::cluster_group cluster = cg::this_cluster();
 
   // inputs may be the previous kernel's output, and out may still be read by it
   grid_dependency_wait();
@@ -249,32 +351,36 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   int issued = 0;  // tiles whose loads the producer has issued
   auto issue_loads = [&](int c) {
     ++issued;
-    const int st = c % kStages;
+    const int st = c % L::kStages;
+    uint8_t *base = smem + st * L::kStageBytes;
     const int row = (int)(t_begin + (int64_t)c * kT);
-    mbar_arrive_expect_tx(&bars[kFull + st], (kStateOnly ? 2 : 3) * kTileBytes);
-    if (!kStateOnly)
-      tma_load_3d(smem + L::kOffQ + st * kTileBytes, &tm_q, &bars[kFull + st], 0, row, (int)bh);
-    tma_load_3d(smem + L::kOffK + st * kTileBytes, &tm_k, &bars[kFull + st], 0, row, (int)bh);
-    tma_load_3d(smem + L::kOffV + st * kTileBytes, &tm_v, &bars[kFull + st], 0, row, (int)bh);
+    mbar_arrive_expect_tx(&bars[kFull0 + st], L::kStageBytes);
+    if (!kStateOnly) tma_load_3d(base + L::kOffQ, &tm_q, &bars[kFull0 + st], 0, row, (int)bh);
+    tma_load_3d(base + L::kOffK, &tm_k, &bars[kFull0 + st], 0, row, (int)bh);
+    tma_load_3d(base + L::kOffV, &tm_v, &bars[kFull0 + st], 0, row, (int)bh);
   };
   if (producer && n_tiles > 0) {
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
     if (!kStateOnly) prefetch_tmap(&tm_q);
-    issue_loads(0);
+    for (int c = 0; c < L::kStages && c < n_tiles; ++c) issue_loads(c);
   }
+
+  // State warps: lane quarters 0..2 (S^T rows 0..95), two column halves:
+  // warps 4..6 columns 0..79, warps 8..10 columns 80..159.
+  const bool state_warp = (warp >= 4 && warp < 7) || (warp >= 8 && warp < 11);
+  const int e = (warp & 3) * 32 + lane;  // S^T row of a state-warp thread
+  const int col0 = warp >= 8 ? 80 : 0;
 
   // ---- seed: S_0 = init_state + the prefix slot g - 1 (this CTA's slots),
   // into TMEM and (output pass) the bf16 snapshot; snapshot rows 65..79 zero
-  const bool state_warp = warp >= 4 && warp < 7;  // lane quarters 0..2: S^T rows 0..95
-  const int e = (warp & 3) * 32 + lane;          // S^T row of a state-warp thread
   if (state_warp) {
     const float *head_a =
         !kStateOnly && p.init_state ? p.init_state + (uint64_t)bh * kF * kSV : nullptr;
     const float *head_b =
         !kStateOnly && g > 0 ? p.seg_states + ((uint64_t)bh * p.segments + (g - 1)) * kF * kSV
                              : nullptr;
-    for (int f0 = 0; f0 < kSlots; f0 += 16) {
+    for (int f0 = col0; f0 < col0 + 80; f0 += 16) {
       uint32_t w[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -309,58 +415,55 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   constexpr uint32_t id_qs = make_idesc_bf16(128, kNO, false, false);
   constexpr uint32_t id_pv = make_idesc_bf16(128, kNO, false, true);
   constexpr uint32_t id_up = make_idesc_bf16(128, kSlots, true, true);
-  constexpr uint32_t id_sc = make_idesc_bf16(128, 128, false, false);
+  constexpr uint32_t id_sc = make_idesc_bf16(128, 16, false, false);
   // a K-step of 16 tokens of [V 1 0]^T / [V 1]: start +2048 B, LBO (distance to
   // the ones block) -2048 B
   constexpr uint64_t kStep = (uint64_t)(2048 >> 4) - ((uint64_t)(2048 >> 4) << 16);
   const uint32_t a_ones = sb + L::kOffOnes;
-  const int token = threadIdx.x & (kT - 1), half = threadIdx.x >> 7;
+  const int token = threadIdx.x & (kT - 1), part = threadIdx.x >> 7;  // quarter of the slots
+  const bool intra = !kStateOnly && rank < kIntraRanks;
 
   for (int c = 0; c < n_tiles; ++c) {
-    const int st = c % kStages;
+    const int st = c % L::kStages;
+    const uint32_t stage = sb + st * L::kStageBytes;
     const int64_t t0 = t_begin + (int64_t)c * kT;
     const int valid = (int)min64(kT, t_end - t0);
-    // the next tile loads into the other stage (its last reader, tile c - 1,
-    // is done: every phase of a tile ends at a barrier)
-    if (producer && c + 1 < n_tiles) issue_loads(c + 1);
-    mbar_wait(&bars[kFull + st], (c / kStages) & 1, abort_flag);
+    LA_TRACE64(c, 0);
+    mbar_wait(&bars[kFull0 + st], (c / L::kStages) & 1, abort_flag);
+    LA_TRACE64(c, 1);
 
-    // ---- phi(K) -> smem (64B-swizzled, MN-major B of the update)
-    stage_rows(sb + L::kOffK + st * kTileBytes, X);
-    __syncthreads();
+    // ---- features: phi_r(K) -> smem (MN-major B of the update), phi_r(Q) -> TMEM
     {
-      const float kscale = token < valid ? 1.f : 0.f;  // padding tokens add nothing
-      const uint32_t base = sb + L::kOffPhiK;
-      for (int J = 10 * half; J < 10 * half + 10; ++J) {
-        uint32_t w[4];
-        features8(desc, X, token, 8 * J, false, kscale, w);
-        st_shared_v4(base + (J >> 2) * kPhiBlock + sw64_offset(token, J & 3), w[0], w[1], w[2],
-                     w[3]);
+      uint32_t x[kDqk];
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint32_t qw[4] = {0u, 0u, 0u, 0u}, kw[4];
+        if (!kStateOnly)
+          ld_shared_v4(stage + L::kOffQ + sw128_offset(token, ch), qw[0], qw[1], qw[2], qw[3]);
+        ld_shared_v4(stage + L::kOffK + sw128_offset(token, ch), kw[0], kw[1], kw[2], kw[3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          x[8 * ch + 2 * i] = bf16_pair<0, 0>(qw[i], kw[i]);
+          x[8 * ch + 2 * i + 1] = bf16_pair<1, 1>(qw[i], kw[i]);
+        }
       }
-    }
-    __syncthreads();
-    if (!kStateOnly) {
-      // ---- phi(Q) -> TMEM (lane = token; warps w and w + 4 share a quarter)
-      stage_rows(sb + L::kOffQ + st * kTileBytes, X);
-      __syncthreads();
-      const uint32_t qaddr = taddr(tmem, (warp & 3) * 32, kColPhiQ + 40 * half);
-#pragma unroll 1
-      for (int G = 0; G < 5; ++G) {  // 8 columns (16 slots) per store
-        uint32_t w[8];
-        features8(desc, X, token, 80 * half + 16 * G, true, 1.f, w);
-        features8(desc, X, token, 80 * half + 16 * G + 8, true, 1.f, w + 4);
-        tmem_st8(qaddr + 8 * G, w);
-      }
-      tmem_wait_st();
+      const uint32_t u = token < valid ? 0x3F803F80u : 0x00003F80u;
+      LA_TRACE64(c, 2);
+      features_for<kStateOnly>(rank * 4 + part, x, u, sb + L::kOffPhiK,
+                               taddr(tmem, (warp & 3) * 32, kColPhiQ), token,
+                               std::make_integer_sequence<int, 4 * kCl>{});
+      if (!kStateOnly) tmem_wait_st();
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    LA_TRACE64(c, 3);
 
-    // ---- MMAs (warp 0): O_r = phi(Q) S_c; S^T += [V 1 0]^T phi(K); CTA 0: scores
+    // ---- MMAs (warp 0): O_r = phi(Q) S_c; S^T += [V 1 0]^T phi(K); CTAs r < 8:
+    // scores of keys 16r .. 16r+15
+    const uint32_t v_base = stage + L::kOffV;
     if (warp == 0) {
-      const uint32_t v_base = sb + L::kOffV + st * kTileBytes;
       if (elect_one()) {
         if (!kStateOnly) {
           const uint64_t qs_b = make_sdesc(sb + L::kOffSnap, 16, 1024, kSwizzle128B);
@@ -376,9 +479,10 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 #pragma unroll
         for (int j = 0; j < kT / 16; ++j)
           umma_ss(tmem + kColS, da0 + kStep * j, db0 + (uint64_t)((j * 1024) >> 4), id_up, 1u);
-        if (!kStateOnly && rank == 0) {
-          const uint64_t qd = make_sdesc(sb + L::kOffQ + st * kTileBytes, 16, 1024, kSwizzle128B);
-          const uint64_t kd = make_sdesc(sb + L::kOffK + st * kTileBytes, 16, 1024, kSwizzle128B);
+        if (intra) {
+          // keys 16r .. 16r+15 are rows 16r.. of the K tile: 8-row groups 2r, 2r+1
+          const uint64_t qd = make_sdesc(stage + L::kOffQ, 16, 1024, kSwizzle128B);
+          const uint64_t kd = make_sdesc(stage + L::kOffK + rank * 2048, 16, 1024, kSwizzle128B);
 #pragma unroll
           for (int kk = 0; kk < kDqk / 16; ++kk)
             umma_ss(tmem + kColSc, qd + 2 * kk, kd + 2 * kk, id_sc, kk > 0 ? 1u : 0u);
@@ -389,49 +493,37 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
     mbar_wait(&bars[kMma], c & 1, abort_flag);
     tc_fence_after();
+    LA_TRACE64(c, 4);
 
-    if (!kStateOnly && rank == 0) {
-      // ---- intra-tile term (CTA 0): P = tril(1 + s/8 + s^2/128) over the
-      // tile's keys, then O_0 += P [V 1]
+    if (intra) {
+      // ---- P = tril(1 + s/8 + s^2/128) for keys 16r .. 16r+15, then
+      // O_r += P [V_r 1] (one K-step: V rows 16r ..)
       if (warp < 4) {
         const int row = warp * 32 + lane;
         const uint32_t srow = taddr(tmem, warp * 32, kColSc);
-        const int m = min(row, valid - 1);  // keys 0 .. m are visible to this row
+        const int m = min(row, valid - 1) - 16 * rank;  // keys 16r .. 16r+m are visible
         const uint64_t c128 = f2pack(1.f / 128.f, 1.f / 128.f), c8 = f2pack(0.125f, 0.125f);
         const uint64_t one2 = f2pack(1.f, 1.f);
-#pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {  // keys 64 hh .. 64 hh + 63
-          uint32_t r[64], w[32];
-          tmem_ld16(srow + 64 * hh, r);
-          tmem_ld16(srow + 64 * hh + 16, r + 16);
-          tmem_ld16(srow + 64 * hh + 32, r + 32);
-          tmem_ld16(srow + 64 * hh + 48, r + 48);
-          tmem_wait_ld();
+        uint32_t r[16], w[8];
+        tmem_ld16(srow, r);
+        tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int j0 = 64 * hh + 2 * i;
-            float p0, p1;
-            const uint64_t s2 = f2pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-            f2unpack(ffma2(s2, ffma2(s2, c128, c8), one2), p0, p1);
-            w[i] = pack_bf16(j0 <= m ? p0 : 0.f, j0 + 1 <= m ? p1 : 0.f);
-          }
-          // P columns 32 hh .. 32 hh + 31 (keys 64 hh ..): score columns this
-          // thread has already read
-          tmem_st16(srow + 32 * hh, w);
-          tmem_st16(srow + 32 * hh + 16, w + 16);
+        for (int i = 0; i < 8; ++i) {
+          float p0, p1;
+          const uint64_t s2 = f2pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+          f2unpack(ffma2(s2, ffma2(s2, c128, c8), one2), p0, p1);
+          w[i] = pack_bf16(2 * i <= m ? p0 : 0.f, 2 * i + 1 <= m ? p1 : 0.f);
         }
+        tmem_st8(srow, w);
         tmem_wait_st();
       }
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
       if (warp == 0) {
-        const uint32_t v_base = sb + L::kOffV + st * kTileBytes;
         const uint64_t db0 = make_sdesc(v_base, a_ones - v_base, 1024, kSwizzle128B);
         if (elect_one()) {
-#pragma unroll
-          for (int j = 0; j < kT / 16; ++j)
-            umma_ts(tmem + kColO, tmem + kColSc + 8 * j, db0 + kStep * j, id_pv, 1u);
+          umma_ts(tmem + kColO, tmem + kColSc, db0 + kStep * rank, id_pv, 1u);
           umma_commit(&bars[kPv]);
         }
         __syncwarp();
@@ -439,27 +531,35 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       mbar_wait(&bars[kPv], c & 1, abort_flag);
       tc_fence_after();
     }
+    LA_TRACE64(c, 5);
+    // this tile's stage is free (the loads of the tile after the next, in the
+    // state pass; of the next, in the output pass)
+    if (producer && issued < n_tiles) issue_loads(issued);
 
     if (!kStateOnly) {
-      // ---- O_r -> shared memory (warps 0..3, lane = row); S_{c+1} -> bf16
-      // snapshot (warps 4..6, lane = S^T row)
-      if (warp < 4) {
-        const int row = warp * 32 + lane;
-        const uint32_t obase = taddr(tmem, warp * 32, kColO);
-        float *dst = part + row * kSV;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint32_t o[16];
-          tmem_ld16(obase + 16 * q4, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) dst[16 * q4 + i] = __uint_as_float(o[i]);
-        }
-        dst[kDv] = __uint_as_float(tmem_ld1(obase + kDv));
+      // ---- row i of O_r -> CTA i / 8, buffer c & 1, slot [rank][i % 8]
+      // (warps 0..3, lane = row); S_{c+1} -> bf16 snapshot (state warps)
+      if (warp < 4 || warp >= 12) {
+        // values 0..31 (warps 0..3) or 32..64 (warps 12..15) of row
+        // 32 (warp % 4) + lane
+        const int row = (warp & 3) * 32 + lane, h = warp >= 12 ? 1 : 0;
+        const uint32_t obase = taddr(tmem, (warp & 3) * 32, kColO + 32 * h);
+        const uint32_t dst = cluster_addr(
+            sb + L::kOffRecv + (c & 1) * kRecvBytes +
+                ((rank * kRowsPerRank + (row & (kRowsPerRank - 1))) * kRecvLd + 32 * h) * 4,
+            (uint32_t)(row / kRowsPerRank));
+        uint32_t o[32];
+        tmem_ld16(obase, o);
+        tmem_ld16(obase + 16, o + 16);
+        const uint32_t den = h ? tmem_ld1(obase + 32) : 0u;
         tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          st_cluster_v4(dst + 16 * i, o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        if (h) st_cluster_b32(dst + 32 * 4, den);
       } else if (state_warp && c + 1 < n_tiles) {
         const uint32_t base = taddr(tmem, (warp & 3) * 32, kColS);
-        for (int f0 = 0; f0 < kSlots; f0 += 16) {
+        for (int f0 = col0; f0 < col0 + 80; f0 += 16) {
           uint32_t r[16];
           tmem_ld16(base + f0, r);
           tmem_wait_ld();
@@ -478,32 +578,29 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      // every CTA's partials of this tile are in its shared memory
-      cluster.sync();
+      LA_TRACE64(c, 6);
+      // every CTA's partials of this tile are in their owners' shared memory
+      cluster_sync();
       tc_fence_after();
-      // ---- rows 8 rank .. 8 rank + 7: warp w sums row 8 rank + w over the
-      // cluster (rank order), lane l owns values l and l + 32
+      LA_TRACE64(c, 7);
+      // ---- rows 8 rank .. 8 rank + 7: warp w sums values 32 (w & 1) + lane
+      // of row 8 rank + w / 2 over the 16 partials, in rank order
       {
-        const int row = rank * kRowsPerRank + warp;
-        float a0 = 0.f, a1 = 0.f, den = 0.f;
-#pragma unroll 4
+        const int r8 = warp >> 1, row = rank * kRowsPerRank + r8;
+        const int ev = 32 * (warp & 1) + lane;
+        const float *rb = recv + (c & 1) * (kRecvBytes / 4) + r8 * kRecvLd;
+        float acc = 0.f, den = 0.f;
+#pragma unroll
         for (int src = 0; src < kCl; ++src) {
-          const float *rp = cluster.map_shared_rank(part, src) + row * kSV;
-          a0 += rp[lane];
-          a1 += rp[lane + 32];
-          if (lane == 0) den += rp[kDv];
+          acc += rb[src * kRowsPerRank * kRecvLd + ev];
+          den += rb[src * kRowsPerRank * kRecvLd + kDv];
         }
-        den = __shfl_sync(0xffffffffu, den, 0);
         const float inv = p.normalize ? 1.f / (den + p.eps) : 1.f;
-        if (row < valid) {
-          __nv_bfloat16 *o = p.out + ((uint64_t)bh * p.n + t0 + row) * kDv;
-          o[lane] = __float2bfloat16_rn(a0 * inv);
-          o[lane + 32] = __float2bfloat16_rn(a1 * inv);
-        }
+        if (row < valid)
+          p.out[((uint64_t)bh * p.n + t0 + row) * kDv + ev] = __float2bfloat16_rn(acc * inv);
       }
-      // no CTA overwrites its partials while another may still read them
-      cluster.sync();
     }
+    LA_TRACE64(c, 8);
   }
 
   // ---- the state after the segment: final state (output pass, last
@@ -513,7 +610,7 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   else if (p.final_state != nullptr && g == p.segments - 1)
     dst = p.final_state + (uint64_t)bh * kF * kSV;
   if (dst && state_warp) {
-    for (int f0 = 0; f0 < kSlots; f0 += 16) {
+    for (int f0 = col0; f0 < col0 + 80; f0 += 16) {
       uint32_t r[16];
       tmem_ld16(taddr(tmem, (warp & 3) * 32, kColS + f0), r);
       tmem_wait_ld();
@@ -526,10 +623,11 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   }
 
   // ---- teardown: every issued copy has landed (each tile's loads were
-  // waited for in its iteration, unless a wait gave up)
+  // waited for in its iteration, unless a wait gave up); no CTA leaves while
+  // another may still store partials into it (the last tile's barrier)
   if (producer) {
-    for (int c = issued - kStages < 0 ? 0 : issued - kStages; c < issued; ++c)
-      wait_teardown(&bars[kFull + c % kStages], (c / kStages) & 1);
+    for (int c = issued - L::kStages < 0 ? 0 : issued - L::kStages; c < issued; ++c)
+      wait_teardown(&bars[kFull0 + c % L::kStages], (c / L::kStages) & 1);
   }
   tc_fence_before();
   __syncthreads();
@@ -580,9 +678,18 @@ int launch64(const void *q, const void *k, const void *v, const Params64 &p, int
 
 }  // namespace
 
+#ifdef LA_TRACE
+extern "C" int la_debug_read_trace64(long long *dst, int count) {
+  const int n = kCl * kTrTiles * kTrEvents;
+  if (count < n) return -1;
+  return cudaMemcpyFromSymbol(dst, la_trace64, sizeof(long long) * n) == cudaSuccess ? n : -1;
+}
+#endif
+
 bool chunked64_tc_available() {
   // 16-CTA clusters are a non-portable size: the attribute is set once per
-  // context and the device must be able to hold at least one such cluster
+  // device (per host thread) and the device must be able to hold at least
+  // one such cluster
   static thread_local int cached_device = -1;
   static thread_local bool cached = false;
   int dev = -1;
