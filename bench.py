@@ -185,33 +185,82 @@ def make_head_inputs(heads_range, seq_len, d_qk, d_v, scale, seed=1234):
 
 # --------------------------------------------------------------------------- reference arm
 
-def cpu_port_sample(seq_len, d_qk, d_v, heads_in_metric, sample_heads, sample_tokens):
-    """Time the oracle's numpy port of the reference chunked algorithm once.
-
-    Returns (metric tokens/s, seconds).  The metric counts B*N tokens for all
-    ``heads_in_metric`` heads, so ``sample_heads`` heads of ``sample_tokens``
-    tokens stand for sample_tokens * sample_heads / heads_in_metric tokens."""
+# The CPU arm: the oracle's numpy port of the reference chunked recurrence,
+# the sampled heads split over single-threaded worker processes (one per
+# usable core, at most one per head).  Its small per-chunk matmuls do not
+# speed up with BLAS threads, so the heads are what runs in parallel.  The
+# workers are started with "spawn" (safe after CUDA use in this process) and
+# each generates its heads' inputs once, outside the timed passes.
+def _cpu_worker_main(conn, heads, n, d_qk, d_v):
     import numpy as np
+    from threadpoolctl import threadpool_limits
     import oracle as O
-    rng = np.random.default_rng(7)
-    q = (rng.standard_normal((1, sample_heads, sample_tokens, d_qk)) * 0.5).astype(np.float32)
-    k = (rng.standard_normal((1, sample_heads, sample_tokens, d_qk)) * 0.5).astype(np.float32)
-    v = (rng.standard_normal((1, sample_heads, sample_tokens, d_v)) * 0.5).astype(np.float32)
-    t0 = time.perf_counter()
-    O.based_chunked(q, k, v, chunk=64, dtype=np.float32)
-    dt = time.perf_counter() - t0
-    return sample_tokens * sample_heads / heads_in_metric / dt, dt
+    limits = threadpool_limits(limits=1)  # noqa: F841  (held for the worker's life)
+    inputs = []
+    for head in heads:
+        rng = np.random.default_rng(7 + head)
+        inputs.append(tuple((rng.standard_normal((1, 1, n, d)) * 0.5).astype(np.float32)
+                            for d in (d_qk, d_qk, d_v)))
+    conn.send("ready")
+    while conn.recv() == "go":
+        for q, k, v in inputs:
+            O.based_chunked(q, k, v, chunk=64, dtype=np.float32)
+        conn.send("done")
 
 
-def host_threads():
+def usable_cores():
     try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
-        if n:
-            return int(max(n))
-    except Exception:
-        pass
-    return os.cpu_count() or 1
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+class CpuPort:
+    """Times `sample_heads` heads of `sample_tokens` tokens of the CPU port."""
+
+    def __init__(self, d_qk, d_v, sample_heads, sample_tokens):
+        import multiprocessing as mp
+        ctx = mp.get_context("spawn")
+        self.workers = max(1, min(usable_cores(), sample_heads))
+        self.sample_heads, self.sample_tokens = sample_heads, sample_tokens
+        self.conns, self.procs = [], []
+        for w in range(self.workers):
+            parent, child = ctx.Pipe()
+            proc = ctx.Process(target=_cpu_worker_main, daemon=True,
+                               args=(child, list(range(w, sample_heads, self.workers)),
+                                     sample_tokens, d_qk, d_v))
+            proc.start()
+            self.conns.append(parent)
+            self.procs.append(proc)
+        for c in self.conns:
+            if c.recv() != "ready":
+                raise RuntimeError("CPU port worker failed to start")
+
+    def sample(self, heads_in_metric):
+        """(metric tokens/s, seconds) of one pass over the sampled heads: the
+        metric counts B*N tokens for all `heads_in_metric` heads, so the sample
+        stands for sample_tokens * sample_heads / heads_in_metric tokens."""
+        t0 = time.perf_counter()
+        for c in self.conns:
+            c.send("go")
+        for c in self.conns:
+            c.recv()
+        dt = time.perf_counter() - t0
+        return self.sample_tokens * self.sample_heads / heads_in_metric / dt, dt
+
+    def describe(self):
+        return (f"{self.sample_heads} heads x {self.sample_tokens} tokens per step, fp32 numpy "
+                "port of the reference chunked recurrence (oracle/based_oracle.py based_chunked), "
+                f"heads split over {self.workers} single-threaded worker processes")
+
+    def close(self):
+        for c in self.conns:
+            try:
+                c.send("stop")
+            except (BrokenPipeError, OSError):
+                pass
+        for proc in self.procs:
+            proc.join(timeout=30)
 
 
 def run_reference(args):
@@ -221,25 +270,24 @@ def run_reference(args):
     b, h, n, dqk, dv, kind = WORKLOADS["c4"]
     n = args.seq_len or n
     sample_heads = 16 if args.mode == "heads" else 4
-    sample_tokens = min(n, 32768)
-    for _ in range(args.warmup):
-        cpu_port_sample(n, dqk, dv, h, sample_heads, sample_tokens)
-    rates, secs = [], 0.0
-    for _ in range(args.steps):
-        r, dt = cpu_port_sample(n, dqk, dv, h, sample_heads, sample_tokens)
-        rates.append(r)
-        secs += dt
-    value = args.steps * sample_tokens * sample_heads / h / secs
-    sample = (f"{sample_heads} heads x {sample_tokens} tokens per step, fp32 numpy port of the "
-              "reference chunked recurrence (oracle/based_oracle.py based_chunked)")
+    port = CpuPort(dqk, dv, sample_heads, min(n, 32768))
+    try:
+        for _ in range(args.warmup):
+            port.sample(h)
+        secs = 0.0
+        for _ in range(args.steps):
+            secs += port.sample(h)[1]
+    finally:
+        port.close()
+    value = args.steps * port.sample_tokens * port.sample_heads / h / secs
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_dict(args, b, h, n, dqk, dv),
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": host_threads(),
-                         "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": port.workers,
+                         "kind": "port", "sample": port.describe()},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -414,15 +462,18 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rates, secs = [], 0.0
-        while secs < 12.0 and len(rates) < 12:
-            r, dt = cpu_port_sample(n, dqk, dv, h, 16, min(n, 32768))
-            rates.append(r)
-            secs += dt
-        cpu = {"value": statistics.median(rates), "unit": "tokens/s", "cores": host_threads(),
-               "kind": "port",
-               "sample": f"16 heads x {min(n, 32768)} tokens, fp32 numpy port of the reference "
-                         f"chunked recurrence, {len(rates)} runs (median)"}
+        port = CpuPort(dqk, dv, 16, min(n, 32768))
+        try:
+            port.sample(h)  # warm-up
+            rates, secs = [], 0.0
+            while secs < 12.0 and len(rates) < 12:
+                r, dt = port.sample(h)
+                rates.append(r)
+                secs += dt
+        finally:
+            port.close()
+        cpu = {"value": statistics.median(rates), "unit": "tokens/s", "cores": port.workers,
+               "kind": "port", "sample": f"{port.describe()}, {len(rates)} runs (median)"}
 
     if rank == 0:
         line = {
