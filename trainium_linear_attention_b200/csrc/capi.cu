@@ -265,10 +265,10 @@ int plan_chunked_fwd(const void *q, const void *k, const void *v, const void *ou
   }
   // one wave of CTAs: a cluster run places its cluster size of CTAs on every
   // (head, segment)
-  const int wave = p.tc64      ? info.sm_count / chunked64_tc_ctas_per_segment()
-                   : p.cluster ? info.sm_count / cluster_chunked_ctas_per_segment()
-                               : info.sm_count;
-  p.g = segments == 0 ? auto_segments(bh, n, wave) : effective_segments(n, segments);
+  const int wave = p.cluster ? info.sm_count / cluster_chunked_ctas_per_segment() : info.sm_count;
+  p.g = segments != 0 ? effective_segments(n, segments)
+        : p.tc64      ? effective_segments(n, chunked64_auto_segments(bh, n, info.sm_count))
+                      : auto_segments(bh, n, wave);
   p.seg_len = p.g > 1 ? segment_len(n, p.g) : n;
   // With two segments the state pass covers only the first: a long one runs
   // as two half-length pieces so that it fills as many SMs as the output
@@ -361,7 +361,7 @@ int la_based_chunked_plan(int64_t batch_heads, int64_t seq_len, int64_t d_qk, in
       // on explicitly (the split itself needs one state per head).
       g = 2;
     } else if (use_tc64(dtype, d_qk, d_v)) {
-      g = auto_segments(batch_heads, seq_len, info.sm_count / chunked64_tc_ctas_per_segment());
+      g = chunked64_auto_segments(batch_heads, seq_len, info.sm_count);
     } else if (!use_tensor_cores(dtype, d_qk, d_v) &&
                !chunked_simt_supported(feature_dim(d_qk), d_qk, d_v) &&
                cluster_chunked_supported(d_qk, d_v)) {
@@ -560,10 +560,11 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
   if (cluster && !cluster_chunked_supported(d_qk, d_v)) return LA_ERR_UNSUPPORTED;
   // the same segmentation as la_based_chunked_fwd, so that a forward with
   // LA_CHUNKED_REUSE_SEGMENTS finds the seeds it expects
-  const int wave = tc64      ? info.sm_count / chunked64_tc_ctas_per_segment()
-                   : cluster ? info.sm_count / cluster_chunked_ctas_per_segment()
-                             : info.sm_count;
-  int g = segments == 0 ? auto_segments(bh, seq_len, wave) : effective_segments(seq_len, segments);
+  const int wave = cluster ? info.sm_count / cluster_chunked_ctas_per_segment() : info.sm_count;
+  int g = segments != 0 ? effective_segments(seq_len, segments)
+          : tc64        ? effective_segments(seq_len,
+                                             chunked64_auto_segments(bh, seq_len, info.sm_count))
+                        : auto_segments(bh, seq_len, wave);
   if (g > 1) {
     const size_t need = la_based_chunked_workspace_size(bh, seq_len, d_qk, d_v, g);
     if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u))

@@ -16,8 +16,8 @@
 //               scores = Q K_r^T                  M=128 N=16  K=64
 //               P      = tril(1 + s/8 + s^2/128)   (CUDA cores, over the scores)
 //               O_r   += P [V_r 1]                M=128 N=80  K=16
-//   every CTA   row i of O_r -> shared memory of CTA i / 8 (remote stores);
-//               cluster barrier
+//   every CTA   O_r -> own shared memory; rows 8o .. 8o+7 -> CTA o (one bulk
+//               copy per CTA, completing on CTA o's mbarrier)
 //   CTA r       rows 8r .. 8r+7: sum of the 16 partial rows in rank order,
 //               / (O[:, 64] + eps); stored
 //
@@ -25,10 +25,12 @@
 // with the normaliser, as in the d_qk = 16 kernel (tc_chunked.cu), whose
 // operand layouts this kernel reuses: summed over the cluster, phi_r(q) .
 // phi_r(k) is the full Taylor kernel 1 + s + s^2/2 of s = q.k / 8, and the
-// intra-tile partials sum to tril(P) [V 1].  The partials land in one of two
-// buffers by tile parity, so one cluster barrier per tile orders their
-// writes before their reads, and a buffer is rewritten only two tiles later,
-// after every owner has passed the next barrier.
+// intra-tile partials sum to tril(P) [V 1].  An owner waits for its 16
+// incoming blocks on its own mbarrier (bytes counted by the copies); a
+// cluster barrier split into its two halves -- arrive after the owner sums,
+// wait before the next tile's partials are staged -- keeps the staging and
+// receiving buffers from being rewritten while a copy or an owner may still
+// read them.
 //
 // Features.  Slot s of CTA r is feature f = 135 r + s in the documented order
 // [1, x_0 .. x_63, x_a x_b (a <= b) row-major].  Four threads share a token;
@@ -41,8 +43,10 @@
 // scaled by 1/8 (linear), 1/64 (a < b) or 1/128 (a = b), exact powers of
 // two, as in the d_qk = 16 kernel.
 //
-// The phases of a tile run one after another (barriers between them); the
-// next tile's Q, K, V load by TMA from the end of this tile's MMAs.  The
+// The phases of a tile run one after another (barriers between them), with
+// the owners' sums of tile c done during tile c + 1, while its MMAs run, so
+// the partials' copies fly under the next tile's features; the next tile's
+// Q, K, V load by TMA from the end of this tile's MMAs.  The
 // state-only variant (kStateOnly) runs the phi(K) / update path without a
 // cluster (every CTA is independent) and writes its slots of the segment's
 // state.
@@ -86,6 +90,8 @@ constexpr uint32_t kPhiBytes = (kSlots / 32) * kPhiBlock;
 constexpr uint32_t kSnapKBlock = kNO * 128;          // 64 slots of the 80 snapshot rows
 constexpr uint32_t kSnapBytes = 3 * kSnapKBlock;
 constexpr uint32_t kRecvBytes = kCl * kRowsPerRank * kRecvLd * 4;  // one tile's partials
+constexpr uint32_t kBlockBytes = kRowsPerRank * kRecvLd * 4;       // rows of one owner (2176 B)
+static_assert(kBlockBytes % 16 == 0, "bulk copies move multiples of 16 bytes");
 
 // The output pass holds one tile of Q, K and V (the next tile loads during
 // the partial-sum exchange); the state pass keeps three tiles of K and V in
@@ -101,8 +107,9 @@ struct Layout64 {
   static constexpr uint32_t kOffOnes = kStages * kStageBytes;         // 16 rows x 128 B
   static constexpr uint32_t kOffPhiK = kOffOnes + 2048;
   static constexpr uint32_t kOffSnap = kOffPhiK + kPhiBytes;
-  static constexpr uint32_t kOffRecv = kOffSnap + (kStateOnly ? 0 : kSnapBytes);
-  static constexpr uint32_t kOffDesc = kOffRecv + (kStateOnly ? 0 : 2 * kRecvBytes);
+  static constexpr uint32_t kOffRecv = kOffSnap + (kStateOnly ? 0 : kSnapBytes);  // [src][8][68]
+  static constexpr uint32_t kOffStage = kOffRecv + (kStateOnly ? 0 : kRecvBytes);  // [128][68]
+  static constexpr uint32_t kOffDesc = kOffStage + (kStateOnly ? 0 : kRecvBytes);
   static constexpr uint32_t kOffBar = kOffDesc + kSlots * 8;
   static constexpr uint32_t kSmemAlloc = kOffBar + 64 + 1024;  // + alignment slack
   static_assert(kStageBytes % 1024 == 0 && kOffOnes % 1024 == 0 && kOffPhiK % 1024 == 0 &&
@@ -114,7 +121,7 @@ struct Layout64 {
 };
 
 constexpr int kMaxStages64 = 3;
-enum Bar64 { kFull0 = 0, kMma = kFull0 + kMaxStages64, kPv, kNumBars };
+enum Bar64 { kFull0 = 0, kMma = kFull0 + kMaxStages64, kPv, kRecv, kNumBars };
 
 // Optional phase timeline (clock64 per tile) of thread 0 of every CTA of
 // cluster (0, 0), compiled in with -DLA_TRACE only.
@@ -198,20 +205,22 @@ __device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, uint32_t rank) 
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
-                                              uint32_t d) {
-  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b),
-               "r"(c), "r"(d)
-               : "memory");
+// The two halves of the cluster barrier (release / acquire at cluster scope).
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void st_cluster_b32(uint32_t addr, uint32_t a) {
-  asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(addr), "r"(a) : "memory");
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// Arrive at / wait for the cluster barrier: release / acquire at cluster
-// scope (the partials stored into other CTAs become visible to them).
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
-               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+// Bulk copy of `bytes` from this CTA's shared memory to another CTA's (both
+// addresses 16-byte aligned, `dst` and `mbar` shared::cluster addresses in
+// the destination CTA); the destination's mbarrier counts the bytes.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, uint32_t bytes,
+                                                  uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(dst), "r"(src), "r"(bytes), "r"(mbar)
+      : "memory");
 }
 
 // Slot s of CTA `rank` at compile time: the rows a, b of the token's (q, k)
@@ -423,6 +432,28 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   const int token = threadIdx.x & (kT - 1), part = threadIdx.x >> 7;  // quarter of the slots
   const bool intra = !kStateOnly && rank < kIntraRanks;
 
+  // Rows 8 rank .. 8 rank + 7 of tile cr, once its 16 blocks have landed:
+  // warp w sums values 32 (w & 1) + lane of row 8 rank + w / 2 over the
+  // partials in rank order, normalises and stores; then this CTA arrives on
+  // the cluster barrier (its receiving buffer may be refilled).
+  auto reduce_tile = [&](int cr) {
+    mbar_wait(&bars[kRecv], cr & 1, abort_flag);
+    const int64_t t0r = t_begin + (int64_t)cr * kT;
+    const int r8 = warp >> 1, row = rank * kRowsPerRank + r8;
+    const int ev = 32 * (warp & 1) + lane;
+    const float *rb = recv + r8 * kRecvLd;
+    float acc = 0.f, den = 0.f;
+#pragma unroll
+    for (int src = 0; src < kCl; ++src) {
+      acc += rb[src * kRowsPerRank * kRecvLd + ev];
+      den += rb[src * kRowsPerRank * kRecvLd + kDv];
+    }
+    const float inv = p.normalize ? 1.f / (den + p.eps) : 1.f;
+    if (row < min64(kT, t_end - t0r))
+      p.out[((uint64_t)bh * p.n + t0r + row) * kDv + ev] = __float2bfloat16_rn(acc * inv);
+    cluster_arrive();
+  };
+
   for (int c = 0; c < n_tiles; ++c) {
     const int st = c % L::kStages;
     const uint32_t stage = sb + st * L::kStageBytes;
@@ -491,9 +522,13 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       __syncwarp();
     }
+    // the previous tile's rows, while this tile's MMAs run (its partials
+    // have been in flight since the end of the previous tile)
+    if (!kStateOnly && c > 0) reduce_tile(c - 1);
+    LA_TRACE64(c, 4);
     mbar_wait(&bars[kMma], c & 1, abort_flag);
     tc_fence_after();
-    LA_TRACE64(c, 4);
+    LA_TRACE64(c, 5);
 
     if (intra) {
       // ---- P = tril(1 + s/8 + s^2/128) for keys 16r .. 16r+15, then
@@ -531,23 +566,21 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       mbar_wait(&bars[kPv], c & 1, abort_flag);
       tc_fence_after();
     }
-    LA_TRACE64(c, 5);
+    LA_TRACE64(c, 6);
     // this tile's stage is free (the loads of the tile after the next, in the
     // state pass; of the next, in the output pass)
     if (producer && issued < n_tiles) issue_loads(issued);
 
     if (!kStateOnly) {
-      // ---- row i of O_r -> CTA i / 8, buffer c & 1, slot [rank][i % 8]
-      // (warps 0..3, lane = row); S_{c+1} -> bf16 snapshot (state warps)
+      // every owner has summed the previous tile: the staging and receiving
+      // buffers are free
+      if (c > 0) cluster_wait();
+      // ---- O_r -> staging [row][68] (warps 0..3 values 0..31, warps 12..15
+      // values 32..64; lane = row); S_{c+1} -> bf16 snapshot (state warps)
       if (warp < 4 || warp >= 12) {
-        // values 0..31 (warps 0..3) or 32..64 (warps 12..15) of row
-        // 32 (warp % 4) + lane
         const int row = (warp & 3) * 32 + lane, h = warp >= 12 ? 1 : 0;
         const uint32_t obase = taddr(tmem, (warp & 3) * 32, kColO + 32 * h);
-        const uint32_t dst = cluster_addr(
-            sb + L::kOffRecv + (c & 1) * kRecvBytes +
-                ((rank * kRowsPerRank + (row & (kRowsPerRank - 1))) * kRecvLd + 32 * h) * 4,
-            (uint32_t)(row / kRowsPerRank));
+        const uint32_t dst = sb + L::kOffStage + (row * kRecvLd + 32 * h) * 4;
         uint32_t o[32];
         tmem_ld16(obase, o);
         tmem_ld16(obase + 16, o + 16);
@@ -555,49 +588,47 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          st_cluster_v4(dst + 16 * i, o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-        if (h) st_cluster_b32(dst + 32 * 4, den);
+          st_shared_v4(dst + 16 * i, o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        if (h) asm volatile("st.shared.b32 [%0], %1;" ::"r"(dst + 32 * 4), "r"(den) : "memory");
       } else if (state_warp && c + 1 < n_tiles) {
-        const uint32_t base = taddr(tmem, (warp & 3) * 32, kColS);
-        for (int f0 = col0; f0 < col0 + 80; f0 += 16) {
-          uint32_t r[16];
-          tmem_ld16(base + f0, r);
+        // 80 columns: the next group's TMEM load is in flight while this
+        // group is packed and stored
+        const uint32_t base = taddr(tmem, (warp & 3) * 32, kColS + col0);
+        uint32_t r0[16], r1[16];
+        tmem_ld16(base, r0);
+#pragma unroll
+        for (int grp = 0; grp < 5; ++grp) {
+          uint32_t *cur = (grp & 1) ? r1 : r0;
+          uint32_t *nxt = (grp & 1) ? r0 : r1;
           tmem_wait_ld();
+          if (grp + 1 < 5) tmem_ld16(base + 16 * (grp + 1), nxt);
+          const int f0 = col0 + 16 * grp;
           if (e <= kDv) {
             const uint32_t blk = sb + L::kOffSnap + (f0 >> 6) * kSnapKBlock;
             const int ch = (f0 & 63) >> 3;
 #pragma unroll
             for (int h = 0; h < 2; ++h)
               st_shared_v4(blk + sw128_offset(e, ch + h),
-                           pack_bf16(__uint_as_float(r[8 * h + 0]), __uint_as_float(r[8 * h + 1])),
-                           pack_bf16(__uint_as_float(r[8 * h + 2]), __uint_as_float(r[8 * h + 3])),
-                           pack_bf16(__uint_as_float(r[8 * h + 4]), __uint_as_float(r[8 * h + 5])),
-                           pack_bf16(__uint_as_float(r[8 * h + 6]), __uint_as_float(r[8 * h + 7])));
+                           pack_bf16(__uint_as_float(cur[8 * h + 0]), __uint_as_float(cur[8 * h + 1])),
+                           pack_bf16(__uint_as_float(cur[8 * h + 2]), __uint_as_float(cur[8 * h + 3])),
+                           pack_bf16(__uint_as_float(cur[8 * h + 4]), __uint_as_float(cur[8 * h + 5])),
+                           pack_bf16(__uint_as_float(cur[8 * h + 6]), __uint_as_float(cur[8 * h + 7])));
           }
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      LA_TRACE64(c, 6);
-      // every CTA's partials of this tile are in their owners' shared memory
-      cluster_sync();
+      __syncthreads();
       tc_fence_after();
       LA_TRACE64(c, 7);
-      // ---- rows 8 rank .. 8 rank + 7: warp w sums values 32 (w & 1) + lane
-      // of row 8 rank + w / 2 over the 16 partials, in rank order
-      {
-        const int r8 = warp >> 1, row = rank * kRowsPerRank + r8;
-        const int ev = 32 * (warp & 1) + lane;
-        const float *rb = recv + (c & 1) * (kRecvBytes / 4) + r8 * kRecvLd;
-        float acc = 0.f, den = 0.f;
-#pragma unroll
-        for (int src = 0; src < kCl; ++src) {
-          acc += rb[src * kRowsPerRank * kRecvLd + ev];
-          den += rb[src * kRowsPerRank * kRecvLd + kDv];
-        }
-        const float inv = p.normalize ? 1.f / (den + p.eps) : 1.f;
-        if (row < valid)
-          p.out[((uint64_t)bh * p.n + t0 + row) * kDv + ev] = __float2bfloat16_rn(acc * inv);
+      if (warp == 0 && lane < kCl) {
+        // lane o: rows 8o .. 8o+7 -> block [rank] of CTA o, counted on its
+        // mbarrier; this CTA's own mbarrier expects the 16 blocks of its rows
+        const uint32_t o = (uint32_t)lane;
+        bulk_copy_to_peer(cluster_addr(sb + L::kOffRecv + rank * kBlockBytes, o),
+                          sb + L::kOffStage + o * kBlockBytes, kBlockBytes,
+                          cluster_addr(smem_u32(&bars[kRecv]), o));
+        if (lane == 0) mbar_arrive_expect_tx(&bars[kRecv], kCl * kBlockBytes);
       }
     }
     LA_TRACE64(c, 8);
@@ -622,9 +653,16 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
   }
 
+  // the last tile's rows; then every owner has summed (so every bulk copy
+  // of this CTA's partials, read from its staging buffer, has landed)
+  // before any CTA of the cluster leaves
+  if (!kStateOnly && n_tiles > 0) {
+    reduce_tile(n_tiles - 1);
+    cluster_wait();
+  }
+
   // ---- teardown: every issued copy has landed (each tile's loads were
-  // waited for in its iteration, unless a wait gave up); no CTA leaves while
-  // another may still store partials into it (the last tile's barrier)
+  // waited for in its iteration, unless a wait gave up)
   if (producer) {
     for (int c = issued - L::kStages < 0 ? 0 : issued - L::kStages; c < issued; ++c)
       wait_teardown(&bars[kFull0 + c % L::kStages], (c / L::kStages) & 1);
@@ -686,18 +724,21 @@ extern "C" int la_debug_read_trace64(long long *dst, int count) {
 }
 #endif
 
+namespace {
+thread_local int g_cached_device = -1;
+thread_local int g_max_clusters = 0;  // 16-CTA clusters the device holds at once
+}  // namespace
+
 bool chunked64_tc_available() {
   // 16-CTA clusters are a non-portable size: the attribute is set once per
   // device (per host thread) and the device must be able to hold at least
   // one such cluster
-  static thread_local int cached_device = -1;
-  static thread_local bool cached = false;
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     cudaGetLastError();
     return false;
   }
-  if (dev == cached_device) return cached;
+  if (dev == g_cached_device) return g_max_clusters > 0;
   bool ok = false;
   const void *fn = (const void *)chunked64_tc_kernel<false>;
   constexpr uint32_t kSmem = Layout64<false>::kSmemAlloc;
@@ -716,14 +757,41 @@ bool chunked64_tc_available() {
     cfg.numAttrs = 1;
     int clusters = 0;
     ok = cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) == cudaSuccess && clusters > 0;
+    g_max_clusters = ok ? clusters : 0;
   }
   cudaGetLastError();
-  cached_device = dev;
-  cached = ok;
+  g_cached_device = dev;
+  if (!ok) g_max_clusters = 0;
   return ok;
 }
 
 int chunked64_tc_ctas_per_segment() { return kCl; }
+
+// Segments per head: the g that minimises the estimated time of the output
+// pass, in waves of the clusters the device holds at once (7 on a B200),
+// plus the state pass over the first g - 1 segments (16 independent CTAs
+// per segment) and the running-sum launch, at least 1024 tokens per segment.
+// The state pass's cost per tile (0.7 of an output tile) and the launches'
+// (3 tiles) are fitted to B=1, H=16, N=4096 on a B200: one segment (three
+// waves of 7, 7 and 2 clusters) 0.546 ms, two segments 0.581 ms.
+int chunked64_auto_segments(int64_t bh, int64_t n, int sm_count) {
+  if (bh <= 0 || n <= 0 || !chunked64_tc_available()) return 1;
+  const int64_t w = g_max_clusters, tiles = (n + kT - 1) / kT;
+  const int64_t max_g = (n + 1023) / 1024 < 16 ? (n + 1023) / 1024 : 16;
+  int best = 1;
+  double best_t = 0.0;
+  for (int64_t g = 1; g <= max_g; ++g) {
+    const double seg_tiles = (double)((tiles + g - 1) / g);
+    const double out_waves = (double)((bh * g + w - 1) / w);
+    const double st_waves = g > 1 ? (double)((kCl * bh * (g - 1) + sm_count - 1) / sm_count) : 0.0;
+    const double t = out_waves * seg_tiles + 0.7 * st_waves * seg_tiles + (g > 1 ? 3.0 : 0.0);
+    if (g == 1 || t < best_t) {
+      best_t = t;
+      best = (int)g;
+    }
+  }
+  return best;
+}
 
 int launch_chunked64_state_tc(const void *k, const void *v, float *seg_states, int64_t bh,
                               int64_t n, int segments, int n_launch, int64_t seg_len,

@@ -45,6 +45,9 @@ int launch_chunked_output_tc(const void *q, const void *k, const void *v, void *
 // out needs 16-byte alignment.
 bool chunked64_tc_available();
 int chunked64_tc_ctas_per_segment();
+// Segments per head for a default (segments = 0) run: the estimated fastest
+// split given how many 16-CTA clusters the device holds at once.
+int chunked64_auto_segments(int64_t bh, int64_t n, int sm_count);
 int launch_chunked64_state_tc(const void *k, const void *v, float *seg_states, int64_t bh,
                               int64_t n, int segments, int n_launch, int64_t seg_len,
                               cudaStream_t s);
