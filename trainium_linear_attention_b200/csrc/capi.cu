@@ -29,6 +29,8 @@ void *driver_entry(const char *name) {
   return ptr;
 }
 
+}  // namespace
+
 // Unique id (cuCtxGetId) of the context current on this thread; false if no
 // context is current or the driver cannot tell.
 bool current_context_id(unsigned long long *id) {
@@ -44,7 +46,6 @@ bool current_context_id(unsigned long long *id) {
   return get_id(ctx, id) == CUDA_SUCCESS;
 }
 
-}  // namespace
 
 void *context_symbol_address(const void *symbol) {
   struct Entry {

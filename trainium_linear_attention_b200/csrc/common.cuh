@@ -54,6 +54,10 @@ int current_device_info(DeviceInfo *info);
 // by the context's unique id.
 void *context_symbol_address(const void *symbol);
 
+// Unique id (cuCtxGetId) of the context current on this thread; false if no
+// context is current or the driver cannot tell.
+bool current_context_id(unsigned long long *id);
+
 // Raises `func`'s dynamic shared-memory limit to `bytes` in the current
 // context, once: later calls make no CUDA API call, so a launch that follows
 // can be captured into a CUDA graph.

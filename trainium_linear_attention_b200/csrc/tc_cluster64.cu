@@ -50,6 +50,7 @@
 // state-only variant (kStateOnly) runs the phi(K) / update path without a
 // cluster (every CTA is independent) and writes its slots of the segment's
 // state.
+#include <mutex>
 #include <utility>
 
 #include "tc_common.cuh"
@@ -616,10 +617,12 @@ chunked64_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           }
         }
       }
+      // the copies start once the staging warps are done; the snapshot warps
+      // finish meanwhile (the next tile's barrier orders their stores before
+      // the MMAs that read them)
       fence_proxy_async_smem();
       tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
+      if (warp < 4 || warp >= 12) named_barrier_sync(1, 256);
       LA_TRACE64(c, 7);
       if (warp == 0 && lane < kCl) {
         // lane o: rows 8o .. 8o+7 -> block [rank] of CTA o, counted on its
@@ -725,23 +728,13 @@ extern "C" int la_debug_read_trace64(long long *dst, int count) {
 #endif
 
 namespace {
-thread_local int g_cached_device = -1;
-thread_local int g_max_clusters = 0;  // 16-CTA clusters the device holds at once
-}  // namespace
-
-bool chunked64_tc_available() {
-  // 16-CTA clusters are a non-portable size: the attribute is set once per
-  // device (per host thread) and the device must be able to hold at least
-  // one such cluster
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  if (dev == g_cached_device) return g_max_clusters > 0;
-  bool ok = false;
+// 16-CTA clusters the device of each context holds at once (0: none), found
+// once per context: the non-portable cluster size is enabled for the kernel
+// and the occupancy of one such cluster is queried.
+int query_max_clusters() {
   const void *fn = (const void *)chunked64_tc_kernel<false>;
   constexpr uint32_t kSmem = Layout64<false>::kSmemAlloc;
+  int clusters = 0;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
       allow_dynamic_smem(fn, (int)kSmem) == LA_OK) {
     cudaLaunchConfig_t cfg = {};
@@ -755,15 +748,37 @@ bool chunked64_tc_available() {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    int clusters = 0;
-    ok = cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) == cudaSuccess && clusters > 0;
-    g_max_clusters = ok ? clusters : 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) != cudaSuccess) clusters = 0;
   }
   cudaGetLastError();
-  g_cached_device = dev;
-  if (!ok) g_max_clusters = 0;
-  return ok;
+  return clusters > 0 ? clusters : 0;
 }
+
+int max_clusters() {
+  struct Entry {
+    unsigned long long ctx;
+    int clusters;
+  };
+  static std::mutex mu;
+  static Entry cache[64];
+  static int used = 0;
+  unsigned long long ctx = 0;
+  const bool known = current_context_id(&ctx);
+  if (known) {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i)
+      if (cache[i].ctx == ctx) return cache[i].clusters;
+  }
+  const int clusters = query_max_clusters();
+  if (known) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (used < 64) cache[used++] = Entry{ctx, clusters};
+  }
+  return clusters;
+}
+}  // namespace
+
+bool chunked64_tc_available() { return max_clusters() > 0; }
 
 int chunked64_tc_ctas_per_segment() { return kCl; }
 
@@ -775,8 +790,9 @@ int chunked64_tc_ctas_per_segment() { return kCl; }
 // (3 tiles) are fitted to B=1, H=16, N=4096 on a B200: one segment (three
 // waves of 7, 7 and 2 clusters) 0.546 ms, two segments 0.581 ms.
 int chunked64_auto_segments(int64_t bh, int64_t n, int sm_count) {
-  if (bh <= 0 || n <= 0 || !chunked64_tc_available()) return 1;
-  const int64_t w = g_max_clusters, tiles = (n + kT - 1) / kT;
+  const int64_t w = max_clusters();
+  if (bh <= 0 || n <= 0 || w <= 0) return 1;
+  const int64_t tiles = (n + kT - 1) / kT;
   const int64_t max_g = (n + 1023) / 1024 < 16 ? (n + 1023) / 1024 : 16;
   int best = 1;
   double best_t = 0.0;
