@@ -14,7 +14,12 @@ NCCL all-gather of per-rank states per step).
 
 Timing: W untimed warm-up steps, then exactly K steps, each bracketed by CUDA
 events on the launching stream; the per-rank sum is max-reduced over ranks
-after a barrier.  L2: a step streams 1.34 GB (config 4) through the 126 MB
+after a barrier.  After the barrier and synchronize that open the timed
+region, a ~0.1 ms spin kernel (outside the events) keeps the GPU busy while
+the host enqueues the first step, so that the first step, like the others,
+is timed from a queue the host has already filled (otherwise it alone would
+include the host's ~30 us per-call launch cost and the idle GPU's wake-up;
+``e2e`` keeps every host cost).  L2: a step streams 1.34 GB (config 4) through the 126 MB
 L2, so no data of a step survives to the next; ``--l2 flush`` additionally
 writes a 256 MB buffer before every timed step (outside the events; its dirty
 lines are then written back during the step).  ``value`` = B*N tokens (heads not counted, the reference's
@@ -26,7 +31,8 @@ sequence-parallel mode: serial copies around the sequence-parallel forward).
 ``sp_phases_ms`` (sequence-parallel mode) splits a step into the state pass,
 the NCCL all-gather with the prefix sum, and the seeded forward.
 ``--impl reference`` times the CPU port of the reference's chunked algorithm
-(oracle/, numpy, all host threads) on a bounded sample of the same workload.
+(oracle/, numpy, one single-threaded worker process per usable core) on a
+bounded sample of the same workload.
 The other configurations (C2, C3 sliding window, the C5 parallel/chunked
 crossover sweep) are measured by ``python -m trainium_linear_attention_b200.sweep``.
 """
@@ -53,6 +59,7 @@ WORKLOADS = {
 }
 METRIC = "BASED chunked attn tokens/s @N=32K,H=16 on 1/2/4/8 B200; % of roofline"
 L2_FLUSH_BYTES = 256 << 20
+QUEUE_SPIN_CYCLES = 200_000  # ~0.1 ms at 1.9 GHz: longer than the host's enqueue of one step
 
 
 def parse_args():
@@ -107,7 +114,10 @@ def profile_traffic_per_token(kernel: str):
 # --------------------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML while running."""
+    """Samples SM clock and throttle reasons through NVML from start() to
+    stop(), keeping only the samples taken while the window is open (the
+    timed region): NVML is initialised and the thread started before the
+    warm-up, so the GPU does not idle for them between warm-up and timing."""
 
     REASONS = {
         0x0000000000000004: "sw_power_cap",
@@ -124,6 +134,7 @@ class ClockSampler:
         self.reasons = set()
         self.max_mhz = None
         self._stop = threading.Event()
+        self._window = threading.Event()
         self._thread = None
         try:
             import pynvml
@@ -137,23 +148,30 @@ class ClockSampler:
     def _run(self):
         nv = self.nv
         while not self._stop.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
-                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                for bit, name in self.REASONS.items():
-                    if mask & bit:
-                        self.reasons.add(name)
-            except Exception:
-                pass
+            if self._window.is_set():
+                try:
+                    self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                    mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                    for bit, name in self.REASONS.items():
+                        if mask & bit:
+                            self.reasons.add(name)
+                except Exception:
+                    pass
             time.sleep(self.period)
 
-    def __enter__(self):
+    def start(self):
         if self.nv is not None:
             self._thread = threading.Thread(target=self._run, daemon=True)
             self._thread.start()
         return self
 
-    def __exit__(self, *exc):
+    def open_window(self):
+        self._window.set()
+
+    def close_window(self):
+        self._window.clear()
+
+    def stop(self):
         self._stop.set()
         if self._thread:
             self._thread.join()
@@ -372,26 +390,31 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- device-resident value
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
+    # ---- device-resident value: the launch count and the clock sampler
+    # first, then the warm-up directly before the timed steps (no idle GPU
+    # between them but the barrier)
     launches_per_step = count_library_launches(step)
-    barrier()
-    torch.cuda.synchronize()
+    clk = ClockSampler(local).start()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for _ in range(args.warmup):
+        step()
     if args.mode == "sp":
         for key in sp_sums:
             sp_sums[key] = 0.0 if key != "steps" else 0
-    with ClockSampler(local) as clk:
-        for i in range(args.steps):
-            if args.l2 == "flush":
-                flush.zero_()
-            starts[i].record(stream)
-            step()
-            ends[i].record(stream)
-        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clk.open_window()
+    torch.cuda._sleep(QUEUE_SPIN_CYCLES)  # busy GPU while the first step is enqueued
+    for i in range(args.steps):
+        if args.l2 == "flush":
+            flush.zero_()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    clk.close_window()
+    clk.stop()
     barrier()
     torch.cuda.synchronize()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]

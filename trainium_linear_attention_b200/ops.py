@@ -8,7 +8,9 @@ to another implementation.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import functools
 
 import torch
 
@@ -47,12 +49,33 @@ def _check_qkv(q, k, v, same_dv: bool = False):
     return _dtype_code(q)
 
 
-def _stream_ptr(device) -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+# Host cost matters: a call's launch latency is exposed whenever the GPU is
+# idle, so the per-call Python work below avoids object churn (raw stream
+# handle, plain ints for pointers, no device switch when already current,
+# plan results cached per shape).
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 
-def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
-    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+def _stream_ptr(device) -> int:
+    """The raw cudaStream_t of the current stream of `device`."""
+    index = torch.device(device).index
+    if index is None:
+        index = torch.cuda.current_device()
+    if _raw_stream is not None:
+        return _raw_stream(index)
+    return torch.cuda.current_stream(index).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _on_device(device):
+    """Make `device` current for the call (a no-op when it already is)."""
+    index = torch.device(device).index
+    if index is None or index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(index)
 
 
 def based_parallel(q, k, v, eps: float = 1e-6) -> torch.Tensor:
@@ -62,7 +85,7 @@ def based_parallel(q, k, v, eps: float = 1e-6) -> torch.Tensor:
     b, h, t, d = q.shape
     dv = v.shape[-1]
     out = torch.empty((b, h, t, dv), dtype=q.dtype, device=q.device)
-    with torch.cuda.device(q.device):
+    with _on_device(q.device):
         st = N.lib().la_based_parallel_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(out), b, h, t, d, dv,
                                            code, float(eps), _stream_ptr(q.device))
     N.check(st, "la_based_parallel_fwd")
@@ -75,11 +98,18 @@ def feature_dim(d_qk: int) -> int:
 
 def chunked_plan(batch_heads: int, seq_len: int, d_qk: int, d_v: int, dtype: torch.dtype,
                  segments: int = 0):
-    """(segments, workspace_bytes) the library will use for this shape."""
+    """(segments, workspace_bytes) the library will use for this shape on the
+    current device."""
+    return _chunked_plan(int(batch_heads), int(seq_len), int(d_qk), int(d_v), _DTYPES[dtype],
+                         int(segments), torch.cuda.current_device())
+
+
+@functools.lru_cache(maxsize=1024)
+def _chunked_plan(batch_heads, seq_len, d_qk, d_v, code, segments, device_index):
     g = ctypes.c_int(0)
     ws = ctypes.c_size_t(0)
-    st = N.lib().la_based_chunked_plan(batch_heads, seq_len, d_qk, d_v, _DTYPES[dtype],
-                                       int(segments), ctypes.byref(g), ctypes.byref(ws))
+    st = N.lib().la_based_chunked_plan(batch_heads, seq_len, d_qk, d_v, code, segments,
+                                       ctypes.byref(g), ctypes.byref(ws))
     N.check(st, "la_based_chunked_plan")
     return g.value, ws.value
 
@@ -119,7 +149,7 @@ def based_chunked(q, k, v, chunk_size: int = 64, eps: float = 1e-6, normalize: b
         init_state = init_state.contiguous()
     out = torch.empty((b, h, t, dv), dtype=q.dtype, device=q.device)
     final = torch.empty((b * h, F, dv + 1), dtype=torch.float32, device=q.device) if return_state else None
-    with torch.cuda.device(q.device):
+    with _on_device(q.device):
         _, ws_bytes = chunked_plan(b * h, t, d, dv, q.dtype, segments)
         if workspace is None:
             workspace = _workspace(ws_bytes, q.device)
@@ -146,7 +176,7 @@ def based_chunked_state(k, v, segments: int = 0, workspace: torch.Tensor | None 
     b, h, t, d = k.shape
     dv = v.shape[-1]
     state = torch.empty((b * h, feature_dim(d), dv + 1), dtype=torch.float32, device=k.device)
-    with torch.cuda.device(k.device):
+    with _on_device(k.device):
         _, ws_bytes = chunked_plan(b * h, t, d, dv, k.dtype, segments)
         if workspace is None:
             workspace = _workspace(ws_bytes, k.device)
@@ -166,7 +196,7 @@ def sliding_window(q, k, v, window_size: int = 64) -> torch.Tensor:
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     b, h, t, d = q.shape
     out = torch.empty_like(q)
-    with torch.cuda.device(q.device):
+    with _on_device(q.device):
         st = N.lib().la_sliding_window_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(out), b, h, t, d, code,
                                            int(window_size), _stream_ptr(q.device))
     N.check(st, "la_sliding_window_fwd")
@@ -186,7 +216,7 @@ def based_layer(q, k, v, window_size: int = 64, eps: float = 1e-6, segments: int
     b, h, t, d = q.shape
     dv = v.shape[-1]
     out = torch.empty((b, h, t, dv), dtype=q.dtype, device=q.device)
-    with torch.cuda.device(q.device):
+    with _on_device(q.device):
         g, ws_bytes = chunked_plan(b * h, t, d, dv, q.dtype, segments)
         if workspace is None:
             workspace = _workspace(ws_bytes, q.device)
@@ -241,7 +271,7 @@ def based_chunked_host(q, k, v, chunk_size: int = 64, eps: float = 1e-6, normali
     of = out.view(bh, t, dv)
     groups = max(1, min(int(head_groups), bh))
     step = -(-bh // groups)
-    with torch.cuda.device(device):
+    with _on_device(device):
         compute = torch.cuda.current_stream(device)
         h2d, d2h = _side_streams(device)
         qd = torch.empty((bh, t, d), dtype=q.dtype, device=device)
