@@ -300,6 +300,39 @@ def test_chunked_reuse_segments():
     assert O.rel_l2(np64(y), want) <= TOL_BF16
 
 
+@pytest.mark.parametrize("dqk,t,segments", [(16, 2500, 4), (64, 2100, 3)])
+def test_chunked_reuse_segments_both_widths(dqk, t, segments):
+    """The state entry point leaves the running sums a forward with
+    reuse_segments seeds from, on the d_qk = 16 kernel and on the d_qk = 64
+    cluster kernel (state pass without a cluster, then the 16-CTA forward)."""
+    q, k, v = cuda(*inputs((1, 2, t, dqk), 64, seed=13 + dqk))
+    g, ws_bytes = ops.chunked_plan(2, t, dqk, 64, torch.bfloat16, segments=segments)
+    assert g == segments
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=DEV)
+    ops.based_chunked_state(k, v, segments=g, workspace=ws)
+    y = ops.based_chunked(q, k, v, segments=g, workspace=ws, reuse_segments=True)
+    assert torch.equal(y, ops.based_chunked(q, k, v, segments=g))
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+
+
+def test_chunked_d64_unaligned_inputs():
+    """bf16 d_qk = 64 tensors whose data is not 16-byte aligned (TMA cannot
+    address them) run on the CUDA-core cluster kernel with the same result."""
+    q, k, v = cuda(*inputs((1, 2, 300, 64), 64, seed=22))
+
+    def shifted(x):
+        buf = torch.empty(x.numel() + 1, dtype=x.dtype, device=DEV)
+        y = buf[1:].view(x.shape)
+        y.copy_(x)
+        return y
+
+    y = ops.based_chunked(shifted(q), shifted(k), shifted(v))
+    want = O.based_attn_reduced(np64(q), np64(k), np64(v))
+    assert O.rel_l2(np64(y), want) <= TOL_BF16
+    assert O.rel_l2(np64(y), np64(ops.based_chunked(q, k, v))) <= 1e-2
+
+
 def test_chunked_sequence_parallel_emulated():
     """The sequence-parallel recipe (per-rank states, exclusive prefix, seeded
     forward) run for 4 emulated ranks on one GPU."""
