@@ -61,11 +61,12 @@ def shard_tokens(x: torch.Tensor, rank: int, world: int) -> torch.Tensor:
 
 
 def exclusive_prefix(states: torch.Tensor, rank: int) -> torch.Tensor:
-    """Sum of ``states[0:rank]`` accumulated in rank order (``states``: (P, ...))."""
-    acc = torch.zeros_like(states[0])
-    for r in range(rank):
-        acc += states[r]
-    return acc
+    """Sum of ``states[0:rank]`` (``states``: (P, ...)) in one reduction over
+    the rank dimension (deterministic: same shapes, same order on every call;
+    one kernel instead of one addition per earlier rank)."""
+    if rank == 0:
+        return torch.zeros_like(states[0])
+    return states[:rank].sum(0)
 
 
 @dataclass
