@@ -369,15 +369,12 @@ def run_ours(args):
         def step():
             return ops.based_chunked(q, k, v, chunk_size=64, segments=seg, workspace=workspace)
     else:
+        # phase events stay pending until after the timed steps (no host
+        # wait inside a step)
         sp_timings = D.SPTimings()
-        sp_sums = {"state_ms": 0.0, "exchange_ms": 0.0, "forward_ms": 0.0, "steps": 0}
 
         def step():
-            y = D.sequence_parallel_forward(q, k, v, chunk_size=64, timings=sp_timings)
-            for key in ("state_ms", "exchange_ms", "forward_ms"):
-                sp_sums[key] += getattr(sp_timings, key)
-            sp_sums["steps"] += 1
-            return y
+            return D.sequence_parallel_forward(q, k, v, chunk_size=64, timings=sp_timings)
 
     def barrier():
         if world > 1:
@@ -400,8 +397,7 @@ def run_ours(args):
     for _ in range(args.warmup):
         step()
     if args.mode == "sp":
-        for key in sp_sums:
-            sp_sums[key] = 0.0 if key != "steps" else 0
+        sp_timings.reset()
     barrier()
     torch.cuda.synchronize()
     clk.open_window()
@@ -426,8 +422,9 @@ def run_ours(args):
     if args.mode == "sp":
         # per-step device time of each phase, max over ranks (state pass,
         # NCCL all-gather + prefix sum, seeded forward)
-        n_sp = max(1, sp_sums["steps"])
-        sp_split = {key: max_over_ranks(sp_sums[key] / n_sp)
+        sp_timings.resolve()
+        n_sp = max(1, sp_timings.steps)
+        sp_split = {key: max_over_ranks(getattr(sp_timings, key) / n_sp)
                     for key in ("state_ms", "exchange_ms", "forward_ms")}
 
     # ---- end to end through the public API (pinned host in, host out)

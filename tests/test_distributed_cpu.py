@@ -40,6 +40,36 @@ def test_exclusive_prefix_order():
     assert torch.equal(D.exclusive_prefix(states, 3), states[:3].sum(0))
 
 
+class _FakeEvent:
+    """Stands in for a CUDA event: a timestamp in ms, and a count of waits."""
+
+    def __init__(self, t):
+        self.t, self.waits = t, 0
+
+    def elapsed_time(self, other):
+        return other.t - self.t
+
+    def synchronize(self):
+        self.waits += 1
+
+
+def test_sp_timings_resolve_after_the_steps():
+    """Phase events stay pending until resolve(), which adds each forward's
+    three phases; reset() drops what the warm-up recorded."""
+    t = D.SPTimings()
+    t.pending.append([_FakeEvent(x) for x in (0.0, 1.0, 1.5, 4.0)])
+    t.reset()
+    assert (t.steps, t.state_ms, t.exchange_ms, t.forward_ms) == (0, 0.0, 0.0, 0.0)
+    steps = [[_FakeEvent(x) for x in (0.0, 2.0, 2.5, 6.0)],
+             [_FakeEvent(x) for x in (10.0, 11.0, 12.5, 13.0)]]
+    t.pending.extend(steps)
+    assert t.steps == 0 and t.state_ms == 0.0  # nothing read before resolve
+    t.resolve()
+    assert t.steps == 2 and not t.pending
+    assert (t.state_ms, t.exchange_ms, t.forward_ms) == (3.0, 2.0, 4.0)
+    assert all(ev[3].waits == 1 for ev in steps)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

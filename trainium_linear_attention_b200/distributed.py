@@ -71,11 +71,35 @@ def exclusive_prefix(states: torch.Tensor, rank: int) -> torch.Tensor:
 
 @dataclass
 class SPTimings:
-    """Device-side milliseconds of one sequence-parallel forward (CUDA only)."""
+    """Device-side milliseconds of sequence-parallel forwards (CUDA only).
+
+    Each forward records four events on the stream (before the state pass,
+    after it, after the exchange and prefix, after the seeded forward) and
+    leaves them pending: nothing in the step waits for the device, so steps
+    run back to back.  ``resolve()`` waits for the recorded events and adds
+    each forward's phases to the totals; ``steps`` counts the forwards added.
+    """
     state_ms: float = 0.0
     exchange_ms: float = 0.0
     forward_ms: float = 0.0
+    steps: int = 0
+    pending: list = field(default_factory=list)
     extra: dict = field(default_factory=dict)
+
+    def resolve(self) -> "SPTimings":
+        for ev in self.pending:
+            ev[3].synchronize()
+            self.state_ms += ev[0].elapsed_time(ev[1])
+            self.exchange_ms += ev[1].elapsed_time(ev[2])
+            self.forward_ms += ev[2].elapsed_time(ev[3])
+            self.steps += 1
+        self.pending.clear()
+        return self
+
+    def reset(self) -> None:
+        self.resolve()
+        self.state_ms = self.exchange_ms = self.forward_ms = 0.0
+        self.steps = 0
 
 
 def _default_state_fn(workspace_holder):
@@ -131,10 +155,7 @@ def sequence_parallel_forward(q, k, v, group=None, *, chunk_size: int = 64, eps:
     out = forward_fn(q, k, v, prefix)
     if ev:
         ev[3].record()
-        ev[3].synchronize()
-        timings.state_ms = ev[0].elapsed_time(ev[1])
-        timings.exchange_ms = ev[1].elapsed_time(ev[2])
-        timings.forward_ms = ev[2].elapsed_time(ev[3])
+        timings.pending.append(ev)
     return out
 
 
