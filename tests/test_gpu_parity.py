@@ -680,3 +680,34 @@ def test_traced_solution_matches_eager(t):
         assert torch.equal(y, T.solution(q2, k2, v2))
     with pytest.raises(ValueError):
         traced(q[:, :, :10], k[:, :, :10], v[:, :, :10])
+
+
+@pytest.mark.parametrize("dim,heads,t,dtype,attention,window", [
+    (64, 4, 300, torch.float32, "parallel", None),   # head_dim 16, fp32: CUDA-core kernels
+    (256, 4, 1100, torch.bfloat16, "auto", None),    # head_dim 64, bf16: chunked d_qk = 64 cluster kernel
+    (64, 4, 500, torch.bfloat16, "parallel", 32),    # full BASED layer through the module
+])
+def test_based_module_matches_reference_module(dim, heads, t, dtype, attention, window):
+    """The kernel module (benchmarks/based_attention_benchmark.py:47-69 names)
+    with the reference module's weights gives the reference module's output
+    (projections in fp64 around the oracle's attention, or the oracle's
+    BASED + sliding-window sum)."""
+    torch.manual_seed(11)
+    ref = T.TrainiumBasedLinearAttention(dim, heads=heads).double()
+    mod = T.TrainiumBasedLinearAttentionNKI(dim, heads=heads, window_size=window,
+                                           attention=attention).to(DEV, dtype)
+    mod.load_state_dict({k: w.to(dtype) for k, w in ref.state_dict().items()})
+    x = (torch.randn(2, t, dim, dtype=torch.float64) * 0.5)
+    with torch.no_grad():
+        y = mod(x.to(DEV, dtype))
+        # the oracle on the projections the kernel module computed
+        hd = dim // heads
+        qkv = [np64(p(x.to(DEV, dtype)).view(2, t, heads, hd).transpose(1, 2))
+               for p in (mod.q_proj, mod.k_proj, mod.v_proj)]
+        att = O.based_attn_reduced(*qkv)
+        if window:
+            att = att + O.sliding_window_attn(*qkv, window)
+        att = torch.from_numpy(att).to(DEV, dtype).transpose(1, 2).reshape(2, t, dim)
+        want = mod.o_proj(att)
+    tol = TOL_FP32 if dtype == torch.float32 else TOL_BF16
+    assert O.rel_l2(np64(y), np64(want)) <= tol

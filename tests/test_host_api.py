@@ -71,3 +71,34 @@ def test_native_check_is_false_without_gpu():
     if torch.cuda.is_available():
         pytest.skip("a GPU is present")
     assert PA._check_nki() is False
+
+
+def test_based_modules_match_reference_wrappers():
+    """benchmarks/based_attention_benchmark.py:24-69: same constructor
+    arguments and parameter names; the reference-path module equals the
+    projections around the oracle's BASED attention; the kernel module
+    refuses CPU tensors (no CPU fallback)."""
+    from trainium_linear_attention_b200.benchmarks import based_attention_benchmark as BM
+
+    for cls in (BM.TrainiumBasedLinearAttention, BM.TrainiumBasedLinearAttentionNKI):
+        sig = inspect.signature(cls.__init__)
+        assert list(sig.parameters)[:4] == ["self", "dim", "heads", "eps"]
+        assert sig.parameters["heads"].default == 8 and sig.parameters["eps"].default == 1e-6
+    torch.manual_seed(3)
+    ref = BM.TrainiumBasedLinearAttention(32, heads=2).double()
+    assert sorted(ref.state_dict()) == ["k_proj.weight", "o_proj.weight", "q_proj.weight",
+                                        "v_proj.weight"]
+    x = torch.randn(2, 40, 32, dtype=torch.float64)
+    with torch.no_grad():
+        y = ref(x)
+        heads = [p(x).view(2, 40, 2, 16).transpose(1, 2).numpy()
+                 for p in (ref.q_proj, ref.k_proj, ref.v_proj)]
+        att = torch.from_numpy(O.based_attn_reduced(*heads))
+        want = ref.o_proj(att.transpose(1, 2).reshape(2, 40, 32))
+    assert O.rel_l2(y.numpy(), want.numpy()) <= 1e-10
+    mod = BM.TrainiumBasedLinearAttentionNKI(32, heads=2, window_size=8)
+    mod.load_state_dict(ref.float().state_dict())
+    with pytest.raises(ValueError, match="CUDA"):
+        mod(x.float())
+    with pytest.raises(ValueError):
+        BM.TrainiumBasedLinearAttentionNKI(32, heads=2, attention="dense")

@@ -13,6 +13,8 @@ from .kernels.chunked_attention import (  # noqa: F401
     chunked_identity_numerator, ref_identity_numerator, based_chunked_host)
 from .kernels.sliding_attention import nki_sliding_window_attn, ref_sliding_window_attn  # noqa: F401
 from .kernels.based_layer import based_layer, ref_based_layer  # noqa: F401
+from .kernels.based_module import (  # noqa: F401
+    TrainiumBasedLinearAttention, TrainiumBasedLinearAttentionNKI)
 from ._native import LaError  # noqa: F401
 
 __all__ = [
@@ -20,5 +22,6 @@ __all__ = [
     "chunked_nki_numerator", "based_chunked",
     "based_chunked_state", "taylor_feature_map", "chunked_identity_numerator",
     "ref_identity_numerator", "based_chunked_host", "nki_sliding_window_attn",
-    "ref_sliding_window_attn", "based_layer", "ref_based_layer", "LaError",
+    "ref_sliding_window_attn", "based_layer", "ref_based_layer",
+    "TrainiumBasedLinearAttention", "TrainiumBasedLinearAttentionNKI", "LaError",
 ]
