@@ -588,12 +588,13 @@ def test_solution_dispatch_and_errors():
         T.based_chunked(qq, qq, qq)
 
 
-def test_solution_short_sequence_takes_parallel_kernel():
-    """N = 256 is below the measured crossover: solution() runs the parallel
-    kernel (one launch, bit-identical to solution_nki, different from the
-    chunked kernel's rounding) and matches the oracle."""
+@pytest.mark.parametrize("t", [256, 512])
+def test_solution_short_sequence_takes_parallel_kernel(t):
+    """N = 256 and 512 are at or below the measured crossover: solution() runs
+    the parallel kernel (one launch, bit-identical to solution_nki, different
+    from the chunked kernel's rounding) and matches the oracle."""
     from trainium_linear_attention_b200 import _native as N
-    q, k, v = inputs((4, 16, 256, 16), 64, seed=256)
+    q, k, v = inputs((4, 16, t, 16), 64, seed=t)
     qd, kd, vd = cuda(q, k, v)
     torch.cuda.synchronize()
     before = N.lib().la_launch_count()
@@ -670,10 +671,12 @@ def test_traced_solution_matches_eager(t):
     """trace_solution captures solution() for one shape in a CUDA graph (the
     parallel kernel at N = 256, the chunked kernel with its segment-state pass
     at N = 3000); replays on new inputs equal the eager call bit for bit."""
-    from trainium_linear_attention_b200.kernels.pytorch_attention import solution_kind
+    from trainium_linear_attention_b200.kernels.pytorch_attention import (
+        CROSSOVER_SEQ_LEN_BF16_TC, solution_kind)
     q, k, v = cuda(*inputs((1, 4, t, 16), 64, seed=t + 1))
     traced = T.trace_solution(q, k, v)
-    assert traced.kind == solution_kind(q, k, v) == ("parallel" if t <= 384 else "chunked")
+    want_kind = "parallel" if t <= CROSSOVER_SEQ_LEN_BF16_TC else "chunked"
+    assert traced.kind == solution_kind(q, k, v) == want_kind
     for seed in (1, 2):
         q2, k2, v2 = cuda(*inputs((1, 4, t, 16), 64, seed=t + 10 * seed))
         y = traced(q2, k2, v2).clone()

@@ -127,17 +127,21 @@ parallel_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
   const uint64_t one2 = f2pack(1.f, 1.f);
   for (int kt = 0; kt < nkt; ++kt) {
     const int st = kt % kStages;
-    if (threadIdx.x == 0) {
+    if (warp == 0) {
+      // warp 0 waits converged and issues through one elected lane
       // S(kt) overwrites P(kt-1): P V of the previous tile has finished, which
       // also frees its K/V stage for tile kt+2
-      if (kt > 0) mbar_wait(&bars[kPVDone], (kt - 1) & 1, abort_flag);
-      if (kt > 0 && kt + kStages - 1 < nkt) load_kv(kt + kStages - 1);
-      mbar_wait(&bars[kFull0 + st], (kt / kStages) & 1, abort_flag);
+      if (kt > 0) mbar_wait_warp(&bars[kPVDone], (kt - 1) & 1, abort_flag);
+      if (lane == 0 && kt > 0 && kt + kStages - 1 < nkt) load_kv(kt + kStages - 1);
+      mbar_wait_warp(&bars[kFull0 + st], (kt / kStages) & 1, abort_flag);
       tc_fence_after();
       const uint64_t da = make_sdesc(sb + kOffQ, 16, 256, kSwizzle32B);
       const uint64_t db = make_sdesc(sb + kOffK + st * kQBytes, 16, 256, kSwizzle32B);
-      umma_ss(tmem + kColS, da, db, id_s, 0);
-      umma_commit(&bars[kSReady]);
+      if (elect_one()) {
+        umma_ss(tmem + kColS, da, db, id_s, 0);
+        umma_commit(&bars[kSReady]);
+      }
+      __syncwarp();
     }
     mbar_wait(&bars[kSReady], kt & 1, abort_flag);
     __syncwarp();
@@ -169,15 +173,18 @@ parallel_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     tmem_wait_st();
     tc_fence_before();
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (warp == 0) {
       tc_fence_after();
       const uint32_t v_base = sb + kOffV + st * kVBytes;
       const uint64_t db0 = make_sdesc(v_base, (sb + kOffOnes) - v_base, 1024, kSwizzle128B);
+      if (elect_one()) {
 #pragma unroll
-      for (int j = 0; j < kT / 16; ++j)
-        umma_ts(tmem + kColO, tmem + kColS + 8 * j, db0 + kStep * j, id_pv,
-                (kt > 0 || j > 0) ? 1u : 0u);
-      umma_commit(&bars[kPVDone]);
+        for (int j = 0; j < kT / 16; ++j)
+          umma_ts(tmem + kColO, tmem + kColS + 8 * j, db0 + kStep * j, id_pv,
+                  (kt > 0 || j > 0) ? 1u : 0u);
+        umma_commit(&bars[kPVDone]);
+      }
+      __syncwarp();
     }
   }
   mbar_wait(&bars[kPVDone], (nkt - 1) & 1, abort_flag);
@@ -397,7 +404,8 @@ parallel_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // the warp waits converged and issues through one elected lane
+    {
       constexpr uint32_t id_s = make_idesc_bf16(128, 128, false, false);
       constexpr uint32_t id_pv = make_idesc_bf16(128, kNO, false, true);
       // a K-step of 16 keys: start address +2048 B, LBO (distance to the ones block) -2048 B
@@ -405,33 +413,41 @@ parallel_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       // scores of step s (key tile kt of the item of turn j)
       auto issue_s = [&](int s, int j, int kt, int qt) -> bool {
         const int st = s % kStages, b = s & 1, qs = j & 1;
-        if (!mbar_wait(&bars[kKVFull + st], (s / kStages) & 1, abort_flag)) return false;
-        if (kt == 0 && !mbar_wait(&bars[kQFull + qs], (j >> 1) & 1, abort_flag)) return false;
-        if (s >= 2 && !mbar_wait(&bars[kSPFree + b], ((s >> 1) - 1) & 1, abort_flag)) return false;
+        if (!mbar_wait_warp(&bars[kKVFull + st], (s / kStages) & 1, abort_flag)) return false;
+        if (kt == 0 && !mbar_wait_warp(&bars[kQFull + qs], (j >> 1) & 1, abort_flag)) return false;
+        if (s >= 2 && !mbar_wait_warp(&bars[kSPFree + b], ((s >> 1) - 1) & 1, abort_flag))
+          return false;
         tc_fence_after();
         const uint64_t da = make_sdesc(sb + kOffQ + qs * kQBytes, 16, 256, kSwizzle32B);
         const uint64_t db = make_sdesc(sb + kOffK + st * kQBytes, 16, 256, kSwizzle32B);
-        umma_ss(tmem + kColS + 128 * b, da, db, id_s, 0);
-        umma_commit(&bars[kSReady + b]);
-        if (kt == qt) umma_commit(&bars[kQEmpty + qs]);  // the item's last read of Q
+        if (elect_one()) {
+          umma_ss(tmem + kColS + 128 * b, da, db, id_s, 0);
+          umma_commit(&bars[kSReady + b]);
+          if (kt == qt) umma_commit(&bars[kQEmpty + qs]);  // the item's last read of Q
+        }
+        __syncwarp();
         return true;
       };
       // P V of step s into the O accumulator of turn j
       auto issue_pv = [&](int s, int j, int kt, int qt) -> bool {
         const int st = s % kStages, b = s & 1, o = j & 1;
-        if (!mbar_wait(&bars[kPReady + b], (s >> 1) & 1, abort_flag)) return false;
-        if (kt == 0 && j >= 2 && !mbar_wait(&bars[kOFree + o], ((j >> 1) - 1) & 1, abort_flag))
+        if (!mbar_wait_warp(&bars[kPReady + b], (s >> 1) & 1, abort_flag)) return false;
+        if (kt == 0 && j >= 2 &&
+            !mbar_wait_warp(&bars[kOFree + o], ((j >> 1) - 1) & 1, abort_flag))
           return false;
         tc_fence_after();
         const uint32_t v_base = sb + kOffV + st * kVBytes;
         const uint64_t db0 = make_sdesc(v_base, (sb + kOffOnes) - v_base, 1024, kSwizzle128B);
+        if (elect_one()) {
 #pragma unroll
-        for (int jj = 0; jj < kT / 16; ++jj)
-          umma_ts(tmem + kColO + 128 * o, tmem + kColS + 128 * b + 8 * jj, db0 + kStep * jj, id_pv,
-                  (kt > 0 || jj > 0) ? 1u : 0u);
-        umma_commit(&bars[kSPFree + b]);
-        umma_commit(&bars[kKVEmpty + st]);
-        if (kt == qt) umma_commit(&bars[kOReady + o]);
+          for (int jj = 0; jj < kT / 16; ++jj)
+            umma_ts(tmem + kColO + 128 * o, tmem + kColS + 128 * b + 8 * jj, db0 + kStep * jj,
+                    id_pv, (kt > 0 || jj > 0) ? 1u : 0u);
+          umma_commit(&bars[kSPFree + b]);
+          umma_commit(&bars[kKVEmpty + st]);
+          if (kt == qt) umma_commit(&bars[kOReady + o]);
+        }
+        __syncwarp();
         return true;
       };
       // in order: the scores of step s, then P V of step s - 1
@@ -447,8 +463,10 @@ parallel_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         }
       }
       if (ok && pj >= 0) issue_pv(s - 1, pj, pkt, pqt);
-      umma_commit(&bars[kDone]);
-      wait_teardown(&bars[kDone], 0);
+      if (elect_one()) umma_commit(&bars[kDone]);
+      __syncwarp();
+      if (lane == 0) wait_teardown(&bars[kDone], 0);
+      __syncwarp();
     }
   } else if (warp < 10) {
     // ------------------------------------------------------------ polynomial

@@ -179,13 +179,14 @@ sliding_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     // ------------------------------------------------------------ MMA issuer
     // With two TMEM buffers the scores of tile j are issued before P V of
     // tile j-1, so they are ready when the softmax warps finish tile j-1.
-    if (lane == 0) {
+    // The warp waits converged and issues through one elected lane.
+    {
       constexpr uint32_t id_s = make_idesc_bf16(128, kSpan, false, false);
       constexpr uint32_t id_o = make_idesc_bf16(128, kD, false, true);
       auto issue_s = [&](int j) -> bool {
         const int s = j % kStages, b = j % kBufs;
-        if (!mbar_wait(&bars[kFull + s], (j / kStages) & 1, abort_flag)) return false;
-        if (j >= kBufs && !mbar_wait(&bars[kTFree + b], ((j / kBufs) - 1) & 1, abort_flag))
+        if (!mbar_wait_warp(&bars[kFull + s], (j / kStages) & 1, abort_flag)) return false;
+        if (j >= kBufs && !mbar_wait_warp(&bars[kTFree + b], ((j / kBufs) - 1) & 1, abort_flag))
           return false;
         tc_fence_after();
         const uint32_t st = sb + s * L::kStageBytes;
@@ -195,24 +196,30 @@ sliding_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         constexpr auto kSw = kDqk == 64 ? kSwizzle128B : kSwizzle32B;
         const uint64_t qd = make_sdesc(st, 16, kSbo, kSw);
         const uint64_t kd = make_sdesc(st + L::kOffK, 16, kSbo, kSw);
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < kDqk / 16; ++kk)  // K steps of 16 (32 bytes) along the rows
-          umma_ss(tmem + b * L::kBufCols, qd + 2 * kk, kd + 2 * kk, id_s, kk > 0 ? 1u : 0u);
-        umma_commit(&bars[kSReady + b]);
+          for (int kk = 0; kk < kDqk / 16; ++kk)  // K steps of 16 (32 bytes) along the rows
+            umma_ss(tmem + b * L::kBufCols, qd + 2 * kk, kd + 2 * kk, id_s, kk > 0 ? 1u : 0u);
+          umma_commit(&bars[kSReady + b]);
+        }
+        __syncwarp();
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
         const int s = j % kStages, b = j % kBufs;
-        if (!mbar_wait(&bars[kPReady + b], (j / kBufs) & 1, abort_flag)) return false;
+        if (!mbar_wait_warp(&bars[kPReady + b], (j / kBufs) & 1, abort_flag)) return false;
         tc_fence_after();
         const uint64_t vd = make_sdesc(sb + s * L::kStageBytes + L::kOffV, 16, 1024, kSwizzle128B);
         const uint32_t sp = tmem + b * L::kBufCols;
+        if (elect_one()) {
 #pragma unroll
-        for (int jj = 0; jj < kSpan / 16; ++jj)  // 16 keys (2048 bytes of V) per step
-          umma_ts(sp + kSpan, sp + 8 * jj, vd + (uint64_t)((jj * 2048) >> 4), id_o,
-                  jj > 0 ? 1u : 0u);
-        umma_commit(&bars[kOReady + b]);
-        umma_commit(&bars[kEmpty + s]);  // Q, K (read by S) and V are done with
+          for (int jj = 0; jj < kSpan / 16; ++jj)  // 16 keys (2048 bytes of V) per step
+            umma_ts(sp + kSpan, sp + 8 * jj, vd + (uint64_t)((jj * 2048) >> 4), id_o,
+                    jj > 0 ? 1u : 0u);
+          umma_commit(&bars[kOReady + b]);
+          umma_commit(&bars[kEmpty + s]);  // Q, K (read by S) and V are done with
+        }
+        __syncwarp();
         return true;
       };
       if (kBufs == 2) {
@@ -226,8 +233,10 @@ sliding_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         for (int j = 0; j < count; ++j)
           if (!issue_s(j) || !issue_pv(j)) break;
       }
-      umma_commit(&bars[kDone]);
-      wait_teardown(&bars[kDone], 0);
+      if (elect_one()) umma_commit(&bars[kDone]);
+      __syncwarp();
+      if (lane == 0) wait_teardown(&bars[kDone], 0);
+      __syncwarp();
     }
   } else if (warp < 10) {
     // ------------------------------------------------------------ softmax -> P

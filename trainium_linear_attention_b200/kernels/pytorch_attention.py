@@ -37,10 +37,11 @@ CROSSOVER_SEQ_LEN_BF16 = 1024
 #: the same for fp32 inputs (both kernels on CUDA cores)
 CROSSOVER_SEQ_LEN_FP32 = 2048
 #: bf16 with d_qk = 16, d_v = 64 (both forms on tcgen05 kernels): measured at
-#: B*N = 262144, H = 16 on B200, parallel 0.41 ms vs chunked 0.74 ms at
-#: N = 256, but 0.62 vs 0.57 ms at N = 512 and 3.05 vs 0.44 at N = 4096; the
-#: limit sits between the two measured points
-CROSSOVER_SEQ_LEN_BF16_TC = 384
+#: B*N = 262144, H = 16 on B200, parallel 0.35 ms vs chunked 0.74 ms at
+#: N = 256 and 0.53 vs 0.55 ms at N = 512 (the persistent parallel kernel,
+#: up to 4 query tiles), but 0.96 vs 0.45 ms at N = 1024 (one CTA per query
+#: tile) and 2.86 vs 0.40 at N = 4096
+CROSSOVER_SEQ_LEN_BF16_TC = 512
 
 
 def _check_nki() -> bool:

@@ -4,9 +4,10 @@
 
 c2   chunked BASED, B=4, H=16, N=2048, d_qk=16, d_v=64 (configuration 2)
 c3   sliding-window softmax attention, B=4, H=16, N=4096, d=64, W=64 (config 3)
-c5   parallel and chunked BASED at B*N = 262144, H=16, N = 512 .. 65536 (by
+c5   parallel and chunked BASED at B*N = 262144, H=16, N = 256 .. 65536 (by
      default; --c5-min-n / --c5-max-n): the crossover that ``solution()``
-     dispatches on (config 5)
+     dispatches on (config 5 is N = 512 .. 65536; N = 256 is the short side
+     of the crossover)
 ident   chunked identity-feature-map numerator, B=4, H=16, N=2048, d_qk=16, d_v=64
 d64     chunked BASED at d_qk = d_v = 64 (F = 2145, the state split over a 16-CTA
         cluster), B=1, H=16, N=4096
@@ -96,7 +97,7 @@ def main():
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--what", default="c2,c3,c5,share,ident,d64,layer")
     ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--c5-min-n", type=int, default=512)
+    ap.add_argument("--c5-min-n", type=int, default=256)
     ap.add_argument("--c5-max-n", type=int, default=65536)
     args = ap.parse_args()
     what = set(args.what.split(","))
