@@ -189,6 +189,35 @@ int auto_segments(int64_t bh, int64_t n, int sm_count) {
   return effective_segments(n, (int)g);
 }
 
+// The same for the tensor-core chunked kernel (bf16, d_qk = 16, d_v = 64),
+// which pays for segments: the state pass, the running sums and their
+// launches.  Among 1 .. auto_segments(...) segments it takes the count with
+// the lowest estimated time, fixed(g) + tiles per segment * per_tile(g), in
+// microseconds fitted to B200 measurements (L2 flushed, one call) of 20
+// shapes with 1 to 8 segments (B*H = 16..128, N = 1024..8192): unsplit 11.6 +
+// 1.45 per tile; two segments 25.2 + 1.56 per tile (state pass + output);
+// more 31.5 + 1.56 (plus the running-sum launch).  E.g. B=4, H=16, N=2048:
+// unsplit 0.035 ms vs 0.038 with two segments; N=4096 at 32 heads: four
+// segments 0.044 ms vs 0.058 unsplit.
+int tc_auto_segments(int64_t bh, int64_t n, int sm_count) {
+  const int g_max = auto_segments(bh, n, sm_count);
+  int best = 1;
+  double best_t = 0.0;
+  for (int g = 1; g <= g_max; ++g) {
+    const int eff = effective_segments(n, g);
+    if (eff != g) continue;  // the same split as a smaller count
+    const int64_t tiles = ((g > 1 ? segment_len(n, g) : n) + kSegmentTile - 1) / kSegmentTile;
+    const double fixed = g == 1 ? 11.6 : g == 2 ? 25.2 : 31.5;
+    const double per_tile = g == 1 ? 1.45 : 1.56;
+    const double t = fixed + (double)tiles * per_tile;
+    if (g == 1 || t < best_t) {
+      best = g;
+      best_t = t;
+    }
+  }
+  return best;
+}
+
 // Lead/main split of the tensor-core chunked forward, for SMs / 2 < bh < SMs
 // (where equal segments leave SMs - bh SMs idle): each head's main CTA covers
 // [lead, n) and is seeded by a state pass over [0, lead); the bh short lead
@@ -269,7 +298,10 @@ int plan_chunked_fwd(const void *q, const void *k, const void *v, const void *ou
   const int wave = p.cluster ? info.sm_count / cluster_chunked_ctas_per_segment() : info.sm_count;
   p.g = segments != 0 ? effective_segments(n, segments)
         : p.tc64      ? effective_segments(n, chunked64_auto_segments(bh, n, info.sm_count))
-                      : auto_segments(bh, n, wave);
+        // (by shape, not alignment: la_based_chunked_plan sizes workspaces
+        // without the pointers)
+        : use_tensor_cores(dtype, d_qk, d_v) ? tc_auto_segments(bh, n, info.sm_count)
+                                             : auto_segments(bh, n, wave);
   p.seg_len = p.g > 1 ? segment_len(n, p.g) : n;
   // With two segments the state pass covers only the first: a long one runs
   // as two half-length pieces so that it fills as many SMs as the output
@@ -367,6 +399,8 @@ int la_based_chunked_plan(int64_t batch_heads, int64_t seq_len, int64_t d_qk, in
                !chunked_simt_supported(feature_dim(d_qk), d_qk, d_v) &&
                cluster_chunked_supported(d_qk, d_v)) {
       g = auto_segments(batch_heads, seq_len, info.sm_count / cluster_chunked_ctas_per_segment());
+    } else if (use_tensor_cores(dtype, d_qk, d_v)) {
+      g = tc_auto_segments(batch_heads, seq_len, info.sm_count);
     } else {
       g = auto_segments(batch_heads, seq_len, info.sm_count);
     }
@@ -565,7 +599,8 @@ int la_based_chunked_state(const void *k, const void *v, float *state_out, int64
   int g = segments != 0 ? effective_segments(seq_len, segments)
           : tc64        ? effective_segments(seq_len,
                                              chunked64_auto_segments(bh, seq_len, info.sm_count))
-                        : auto_segments(bh, seq_len, wave);
+          : use_tensor_cores(dtype, d_qk, d_v) ? tc_auto_segments(bh, seq_len, info.sm_count)
+                                               : auto_segments(bh, seq_len, wave);
   if (g > 1) {
     const size_t need = la_based_chunked_workspace_size(bh, seq_len, d_qk, d_v, g);
     if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255u))
