@@ -19,8 +19,8 @@
 // polynomial form 1 + s + s^2/2 and the normaliser carried both as state row
 // 64 (z = sum phi(k)) and as the ones column of [V 1] (the row sum of P).
 // The 153 features never touch HBM: each token's phi(Q) is expanded in
-// registers and stored to TMEM, its phi(K) to shared memory, by the thread
-// that owns the token.
+// registers and stored to TMEM, its phi(K) to shared memory, by a thread that
+// owns the token.
 //
 // A thread pays ~100 cycles to issue one M=128, K=16 tcgen05.mma (measured:
 // one thread issues no faster than one per ~100-150 cycles, longer than an
@@ -28,19 +28,21 @@
 // the state updates UP(c), the other QS(c), PV(c) and the scores of tile
 // c+1.  (Giving QS, PV and the scores a thread each, with P in its own TMEM
 // columns, was measured 9% slower.)  The state snapshot and phi(K) of tile
-// c+1 are produced while QS(c) and PV(c) run, phi(Q) of tile c+1 while PV(c)
-// and UP(c+1) run, and P of tile c+1 while UP(c+1) and QS(c+1) run.
+// c+1 are produced while QS(c) and PV(c) run, phi(Q) of tile c+1 (by the
+// epilogue warps, before they store the output of tile c) while PV(c) runs,
+// and P of tile c+1 while UP(c+1) and QS(c+1) run.
 //
 // Warp roles (800 threads, one CTA per SM):
 //   warp 19     TMA producer: Q/K tiles (2-stage ring) and V tiles (3-stage ring)
 //   warp 23     TMEM allocator + update MMA issuer (S^T += ...)
 //   warp 24     output MMA issuer (phi(Q) S, P [V 1], scores)
-//   warps 0-3   features: phi(K) -> smem (2 buffers), phi(Q) -> TMEM
+//   warps 0-3   features: phi(K) -> smem (2 buffers)
 //   warps 4-11  polynomial: scores -> P (TMEM); two warps per TMEM lane quarter
 //   warps 16-18, 20-22  state: S^T (TMEM, fp32) -> bf16 snapshot in smem (2
 //               buffers); lane quarters 0-2 (S^T rows >= 96 are always zero),
 //               two warps per quarter, 80 feature columns each
-//   warps 12-15 epilogue: O (TMEM) -> normalised bf16 output rows
+//   warps 12-15 epilogue: phi(Q) of tile c+1 -> TMEM, then O of tile c
+//               (TMEM) -> normalised bf16 output rows
 //
 // The state-only variant (kStateOnly) runs just the phi(K) / update path and
 // writes the segment's state; it seeds the later segments of a head.
@@ -405,7 +407,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     // quarters' polynomial warp pairs
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t count = 1;
-      if (i >= kQKEmpty && i < kQKEmpty + kMaxStages) count = kStateOnly ? 1 : 2;
+      if (i >= kQKEmpty && i < kQKEmpty + kMaxStages) count = kStateOnly ? 1 : 3;
       if (i >= kVEmpty && i < kVEmpty + kMaxStages) count = 2;
       if ((i == kUpDone0 || i == kUpDone1) && kStateOnly) count = 2;
       if (i == kDone) count = 2;
@@ -630,10 +632,9 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     }
   } else if (warp < kWarpPoly) {
     // ------------------------------------------------------------ features
-    // phi(K) of tile c + 1 is produced before phi(Q) of tile c: the update
-    // of tile c + 1 (the state chain) waits on the former, while phi(Q) S of
-    // tile c has slack; both tiles' Q/K stages are resident (the ring is
-    // deeper than two tiles, and a stage is released only after its phi(Q)).
+    // phi(K) of every tile, into two shared-memory buffers (the state
+    // chain: the update of tile c waits on it).  phi(Q) is the epilogue
+    // warps' (it sits on the output chain, and they are idle between tiles).
     const int wq = warp & 3;
     const int row = wq * 32 + lane;  // token within the tile == TMEM lane
     const bool leader = (warp == kWarpFeat && lane == 0);
@@ -666,47 +667,13 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       named_barrier_sync(1, 128);
       if (leader) {
         mbar_arrive(&bars[kPhiKReady0 + s]);
-        // kw has been consumed; in the state pass the stage is done with
-        if (kStateOnly) mbar_arrive(&bars[kQKEmpty + sq]);
+        // K of tile c has been read (the full kernel's stage also waits for
+        // the scores MMA and phi(Q))
+        mbar_arrive(&bars[kQKEmpty + sq]);
       }
       LA_TRACE_AT(1, c, 1);
     };
-    auto do_phiq = [&](int c) {
-      const int sq = c % kQKStages;  // Q/K stage (still holds Q of tile c)
-      uint32_t qw[8];
-      const uint32_t qt = sb + kOffQ + sq * kQBytes;
-      ld_shared_v4(qt + sw32_offset(row, 0), qw[0], qw[1], qw[2], qw[3]);
-      ld_shared_v4(qt + sw32_offset(row, 1), qw[4], qw[5], qw[6], qw[7]);
-      // phi(Q) -> TMEM once phi(Q) S of the previous tile has read it
-      if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
-      named_barrier_sync(1, 128);
-      tc_fence_after();
-      LA_TRACE_AT(1, c, 5);
-      FeatIn fs;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        fs.w[i] = qw[i];
-        fs.s16[i] = hmul2_bf16(qw[i], 0x3D803D80u);  // x / 16  (exact)
-        fs.s32[i] = hmul2_bf16(qw[i], 0x3D003D00u);  // x / 32  (exact)
-      }
-      fs.one = 0x3F80u;
-      store_phiq<kIdentity>(fs, taddr(tmem, wq * 32, kColPhiQ),
-                            std::make_integer_sequence<int, kSlots / 32>{});
-      tmem_wait_st();
-      LA_TRACE_AT(1, c, 6);
-      tc_fence_before();
-      named_barrier_sync(1, 128);
-      if (leader) {
-        mbar_arrive(&bars[kPhiQReady]);
-        mbar_arrive(&bars[kQKEmpty + sq]);  // Q and K of tile c consumed: release the stage
-      }
-      LA_TRACE_AT(1, c, 2);
-    };
-    if (n_chunks > 0) do_phik(0);
-    for (int c = 0; c < n_chunks; ++c) {
-      if (c + 1 < n_chunks) do_phik(c + 1);
-      if (!kStateOnly) do_phiq(c);
-    }
+    for (int c = 0; c < n_chunks; ++c) do_phik(c);
   } else if (warp < kWarpEpi) {
     // ------------------------------------------------------------ polynomial
     if (!kStateOnly) {
@@ -966,14 +933,49 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     if (!kStateOnly) {
       const int wq = warp & 3;  // rows 32wq .. 32wq+31 of the tile, one per lane
       const bool leader = (warp == kWarpEpi && lane == 0);
+      const int row = wq * 32 + lane;  // token within the tile == TMEM lane
+      // phi(Q) of tile c -> TMEM (a single buffer, free once phi(Q) S of tile
+      // c - 1 has read it).  Produced here, ahead of the output of tile
+      // c - 1: phi(Q) S of tile c waits for it, while the output of tile
+      // c - 1 only has to leave TMEM before phi(Q) S of tile c writes O.
+      auto do_phiq = [&](int c) {
+        const int sq = c % kQKStages;  // Q/K stage of tile c
+        mbar_wait(&bars[kQKFull + sq], (c / kQKStages) & 1, abort_flag);
+        uint32_t qw[8];
+        const uint32_t qt = sb + kOffQ + sq * kQBytes;
+        ld_shared_v4(qt + sw32_offset(row, 0), qw[0], qw[1], qw[2], qw[3]);
+        ld_shared_v4(qt + sw32_offset(row, 1), qw[4], qw[5], qw[6], qw[7]);
+        if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
+        named_barrier_sync(4, 128);
+        tc_fence_after();
+        FeatIn fs;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          fs.w[i] = qw[i];
+          fs.s16[i] = hmul2_bf16(qw[i], 0x3D803D80u);  // x / 16  (exact)
+          fs.s32[i] = hmul2_bf16(qw[i], 0x3D003D00u);  // x / 32  (exact)
+        }
+        fs.one = 0x3F80u;
+        store_phiq<kIdentity>(fs, taddr(tmem, wq * 32, kColPhiQ),
+                              std::make_integer_sequence<int, kSlots / 32>{});
+        tmem_wait_st();
+        tc_fence_before();
+        named_barrier_sync(4, 128);
+        if (leader) {
+          mbar_arrive(&bars[kPhiQReady]);
+          mbar_arrive(&bars[kQKEmpty + sq]);  // Q of tile c has been read
+        }
+      };
       // this lane's store target after the transpose: piece (lane & 3) of row
-      // (lane & ~3) of its quarter, advanced one tile per iteration; rows_left
+      // (lane & ~3) of its quarter, advanced one tile per output; rows_left
       // counts the rows of the segment from that row on
       const int gi = lane & 3;
       uint4 *dst_row = (uint4 *)(p.out + ((uint64_t)bh * p.n + t_begin + wq * 32 + (lane & ~3)) * kDv) +
                        2 * gi;
       int64_t rows_left = t_end - (t_begin + wq * 32 + (lane & ~3));
+      if (n_chunks > 0) do_phiq(0);
       for (int c = 0; c < n_chunks; ++c, dst_row += kT * kDv / 8, rows_left -= kT) {
+        if (c + 1 < n_chunks) do_phiq(c + 1);
         mbar_wait(&bars[kOReady], c & 1, abort_flag);
         named_barrier_sync(4, 128);
         tc_fence_after();
