@@ -401,10 +401,11 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
 #endif
   if (threadIdx.x == 0) {
     // every barrier: one arrival (a leader thread, a TMA expect-tx or a
-    // tcgen05.commit), except: a Q/K stage is released by the features and
-    // (full kernel) the scores MMA, a V stage by the update and (full kernel)
-    // P V, `done` by both MMA issuers, each half of P by the four lane
-    // quarters' polynomial warp pairs
+    // tcgen05.commit), except: a Q/K stage is released by the phi(K) warps
+    // and (full kernel) the phi(Q) warps and a polynomial warp once the
+    // scores are done, a V stage by the update and (full kernel) P V,
+    // `done` by both MMA issuers, each half of P by the four lane quarters'
+    // polynomial warp pairs
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t count = 1;
       if (i >= kQKEmpty && i < kQKEmpty + kMaxStages) count = kStateOnly ? 1 : 3;
@@ -551,10 +552,11 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         const int s = c % kQKStages;
         const uint64_t da = make_sdesc(sb + kOffQ + s * kQBytes, 16, 256, kSwizzle32B);
         const uint64_t db = make_sdesc(sb + kOffK + s * kQBytes, 16, 256, kSwizzle32B);
+        // (the polynomial warps release the Q/K stage once they have seen
+        // the scores complete: one commit fewer on this issuer's chain)
         if (elect_one()) {
           umma_ss(tmem + kColSc, da, db, id_sc, 0);
           umma_commit(&bars[kScReady]);
-          umma_commit(&bars[kQKEmpty + s]);
         }
         __syncwarp();
       };
@@ -623,8 +625,10 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           const int c1 = c + 1;
           if (!mbar_wait_warp(&bars[kQKFull + c1 % kQKStages], (c1 / kQKStages) & 1, abort_flag))
             break;
+          LA_TRACE_AT(1, c, 5);
           tc_fence_after();
           issue_scores(c + 1);
+          LA_TRACE_AT(1, c, 6);
         }
       }
       if (elect_one()) umma_commit(&bars[kDone]);
@@ -689,6 +693,8 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         const int valid = (int)min64(kT, t_end - t0);
         mbar_wait(&bars[kScReady], c & 1, abort_flag);
         named_barrier_sync(2, 256);
+        // the scores MMA has read Q and K of tile c: its part of the stage is free
+        if (warp == kWarpPoly && lane == 0) mbar_arrive(&bars[kQKEmpty + c % kQKStages]);
         tc_fence_after();
         LA_TRACE_AT(2, c, 0);
         // P = tril(1 + s/4 + s^2/32) for raw scores s = q.k (d = 16).  Key group
@@ -947,6 +953,7 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         ld_shared_v4(qt + sw32_offset(row, 1), qw[4], qw[5], qw[6], qw[7]);
         if (c > 0) mbar_wait(&bars[kQSDone0 + ((c - 1) & 1)], ((c - 1) >> 1) & 1, abort_flag);
         named_barrier_sync(4, 128);
+        LA_TRACE_AT(4, c, 3);
         tc_fence_after();
         FeatIn fs;
 #pragma unroll
@@ -959,8 +966,10 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         store_phiq<kIdentity>(fs, taddr(tmem, wq * 32, kColPhiQ),
                               std::make_integer_sequence<int, kSlots / 32>{});
         tmem_wait_st();
+        LA_TRACE_AT(4, c, 4);
         tc_fence_before();
         named_barrier_sync(4, 128);
+        LA_TRACE_AT(4, c, 5);
         if (leader) {
           mbar_arrive(&bars[kPhiQReady]);
           mbar_arrive(&bars[kQKEmpty + sq]);  // Q of tile c has been read
