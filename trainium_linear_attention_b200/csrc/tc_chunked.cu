@@ -567,16 +567,25 @@ chunked_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       }
       for (int c = 0; ok && c < n_chunks; ++c) {
         const int b = c & 1;
-        // O = phi(Q) S_c   (K = 160 features in 10 steps; S_c is snapshot b)
-        if (!mbar_wait_warp(&bars[kPhiQReady], c & 1, abort_flag)) break;
-        LA_TRACE_AT(0, c, 4);
-        if (!mbar_wait_warp(&bars[kSnapReady0 + b], (c >> 1) & 1, abort_flag)) break;
-        LA_TRACE_AT(0, c, 5);
-        if (c > 0 && !mbar_wait_warp(&bars[kOFree], (c - 1) & 1, abort_flag)) break;
-        LA_TRACE_AT(0, c, 6);
-        // let the update of tile c enter the pipe first: the next snapshot,
-        // and so the next tile, waits on it
-        if (!__all_sync(0xffffffffu, spin_until_at_least(up_issued, c + 1, abort_flag))) break;
+        // O = phi(Q) S_c   (K = 160 features in 10 steps; S_c is snapshot b).
+        // Its four conditions have usually all been met by the time this
+        // warp gets here: test them together first, and wait on them one by
+        // one only if one is still open.
+        const bool ready = mbar_test_wait(&bars[kPhiQReady], c & 1) &&
+                           mbar_test_wait(&bars[kSnapReady0 + b], (c >> 1) & 1) &&
+                           (c == 0 || mbar_test_wait(&bars[kOFree], (c - 1) & 1)) &&
+                           *up_issued >= c + 1;
+        if (!__all_sync(0xffffffffu, ready)) {
+          if (!mbar_wait_warp(&bars[kPhiQReady], c & 1, abort_flag)) break;
+          LA_TRACE_AT(0, c, 4);
+          if (!mbar_wait_warp(&bars[kSnapReady0 + b], (c >> 1) & 1, abort_flag)) break;
+          LA_TRACE_AT(0, c, 5);
+          if (c > 0 && !mbar_wait_warp(&bars[kOFree], (c - 1) & 1, abort_flag)) break;
+          LA_TRACE_AT(0, c, 6);
+          // let the update of tile c enter the pipe first: the next snapshot,
+          // and so the next tile, waits on it
+          if (!__all_sync(0xffffffffu, spin_until_at_least(up_issued, c + 1, abort_flag))) break;
+        }
         tc_fence_after();
         LA_TRACE_AT(0, c, 1);
         const uint64_t qs_b_desc = b ? qs_b_desc1 : qs_b_desc0;

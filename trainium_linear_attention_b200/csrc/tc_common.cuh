@@ -62,6 +62,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of whether the phase with the given parity has completed
+// (acquire semantics, like a completed wait).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // As mbar_try_wait, but the thread may sleep in hardware until the phase
 // completes or about `suspend_ns` nanoseconds pass, instead of returning at
 // once: waiting warps then take no issue slots or shared-memory bandwidth.
